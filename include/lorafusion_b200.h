@@ -1,0 +1,183 @@
+/*
+ * lorafusion_b200 — C ABI of the B200 (sm_100a) fused multi-adapter LoRA operator.
+ *
+ * The operator computes, for a fused batch whose rows are routed to adapters by
+ * contiguous row ranges ("routes"):
+ *
+ *   forward   y        = x W^T + s_i (x A_i^T) B_i^T                 (rows of route -> adapter i)
+ *   backward  grad_x   = g W   + s_i (g B_i) A_i
+ *             grad_B_i = s_i sum_rows g^T (x A_i^T)
+ *             grad_A_i = s_i sum_rows (g B_i)^T x
+ *
+ * with x [T,K], W [N,K], A_i [r_i,K], B_i [N,r_i], g = grad_out [T,N], s_i = alpha_i / r_i.
+ * This is lorafusion's op contract (lorafusion/ops/mock_ops.py:15-95); the Python module
+ * lorafusion_b200.b200_ops exposes it with the reference's exact call signature
+ * (fused_lora_forward / fused_lora_backward) on top of these entry points.
+ *
+ * Conventions
+ *  - Every pointer argument named *_dev is device memory; everything else is host memory.
+ *  - Matrices are dense row-major.  The caller owns every buffer; the library allocates
+ *    nothing per call (scratch space is the caller's `workspace`).
+ *  - Every entry point returns an lf_status; nothing aborts or traps.
+ *  - Work is enqueued on the given stream; calls do not synchronize.
+ */
+#ifndef LORAFUSION_B200_H
+#define LORAFUSION_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LF_API __attribute__((visibility("default")))
+#else
+#define LF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* lf_stream_t; /* a cudaStream_t */
+
+typedef enum lf_status {
+  LF_OK = 0,
+  LF_ERR_INVALID_ARG = 1,   /* null pointer, bad shape/stride, bad enum             -> ValueError   */
+  LF_ERR_ROUTING = 2,       /* routes do not tile [0,T) in order, slot out of range -> ValueError   */
+  LF_ERR_UNSUPPORTED = 3,   /* dtype/rank/alignment this build does not handle      -> ValueError   */
+  LF_ERR_CUDA = 4,          /* a CUDA runtime/driver call failed                    -> RuntimeError */
+  LF_ERR_CAPACITY = 5,      /* a caller buffer (table, workspace) is too small      -> ValueError   */
+  LF_ERR_DEVICE = 6         /* a kernel reported a bounded-wait timeout             -> RuntimeError */
+} lf_status;
+
+typedef enum lf_dtype { LF_F32 = 0, LF_BF16 = 1, LF_F16 = 2 } lf_dtype;
+
+/* Rows per fused-row tile used by every kernel's routing tables. */
+#define LF_TILE_ROWS 128
+
+/* Sizes and section offsets (in int32 words) of a routing table built by lf_plan_tables. */
+typedef struct lf_plan_info {
+  int32_t total_rows;      /* T */
+  int32_t n_routes;
+  int32_t n_slots;         /* adapters that own at least one route, in order of first appearance */
+  int32_t n_tiles;         /* ceil(T / LF_TILE_ROWS) */
+  int32_t n_segtiles;      /* route x tile intersections ("segment tiles") */
+  int32_t r_pad;           /* padded rank shared by every slot: 16, 32 or 64 */
+  int32_t max_rank;
+  int32_t rank_total;      /* sum of slot ranks: rows of the concatenated grad_a blocks */
+  int32_t n_shrink_units;  /* (tile, run of segment tiles) work units of the shrink */
+  int32_t table_words;     /* int32 words of the table in use */
+  /* section offsets */
+  int32_t off_tile_st;     /* [n_tiles+1]  CSR: segment tiles of each row tile */
+  int32_t off_st_tile;     /* [n_segtiles] row tile of each segment tile */
+  int32_t off_st_lo;       /* [n_segtiles] first row inside the tile */
+  int32_t off_st_hi;       /* [n_segtiles] one past the last row inside the tile */
+  int32_t off_st_slot;     /* [n_segtiles] adapter slot */
+  int32_t off_st_route;    /* [n_segtiles] index of the route it came from */
+  int32_t off_st_scale;    /* [n_segtiles] float bits of the slot's scaling */
+  int32_t off_slot_st;     /* [n_slots+1]  CSR: segment tiles of each slot, in route order */
+  int32_t off_slot_list;   /* [n_segtiles] */
+  int32_t off_slot_rank;   /* [n_slots]    rank of each slot */
+  int32_t off_rank_prefix; /* [n_slots+1]  exclusive prefix sum of ranks */
+  int32_t off_slot_order;  /* [n_slots]    slots by descending segment-tile count */
+  int32_t off_unit_tile;   /* [n_shrink_units] */
+  int32_t off_unit_st0;    /* [n_shrink_units] */
+  int32_t off_unit_nst;    /* [n_shrink_units] */
+} lf_plan_info;
+
+/* Upper bound on the int32 words lf_plan_tables needs. */
+LF_API int32_t lf_plan_table_words(int32_t n_routes, int32_t total_rows, int32_t n_slots);
+
+/*
+ * Build the device routing table on the host.
+ * Replaces the per-route Python loops of lorafusion/ops/triton_ops.py:398-407 and :435-466
+ * (and the row-range walk of mock_ops.py:40-46, :71-93): routes are
+ * TileRoutingConfig.routes (lorafusion/ops/config.py:29-47) mapped to adapter slots.
+ * Checks what TileRoutingConfig.validate checks (config.py:55-69) -> LF_ERR_ROUTING.
+ *   route_start/route_end/route_slot : [n_routes]
+ *   slot_rank/slot_scale             : [n_slots] rank r_i and scaling alpha_i/r_i
+ *   table                            : host buffer of table_capacity int32 words
+ * The caller copies `table` (info->table_words words) to device memory.
+ */
+LF_API int lf_plan_tables(const int32_t* route_start, const int32_t* route_end, const int32_t* route_slot,
+                   int32_t n_routes, int32_t total_rows, const int32_t* slot_rank, const float* slot_scale,
+                   int32_t n_slots, int32_t* table, int32_t table_capacity, lf_plan_info* info);
+
+/* Operands of one projection. */
+typedef struct lf_problem {
+  int32_t dtype;        /* lf_dtype of x, W, grad_out, outputs and packed adapters */
+  int32_t T, K, N;      /* rows, in_features, out_features */
+  const void* x_dev;    /* [T,K] */
+  const void* w_dev;    /* [N,K] */
+  const void* a_pack_dev;  /* [n_slots, r_pad, K]  A_i rows, zero padded   (forward shrink)  */
+  const void* b_pack_dev;  /* [n_slots, N, r_pad]  B_i, zero padded columns (forward expand) */
+  const void* bt_pack_dev; /* [n_slots, r_pad, N]  B_i^T                     (backward shrink) */
+  const void* at_pack_dev; /* [n_slots, K, r_pad]  A_i^T                     (backward expand) */
+} lf_problem;
+
+/* Workspace bytes the forward / backward need for this table and dtype. */
+LF_API size_t lf_forward_workspace_bytes(const lf_plan_info* info, int32_t dtype);
+LF_API size_t lf_backward_workspace_bytes(const lf_plan_info* info, int32_t dtype);
+
+/*
+ * Pack per-adapter matrices into one zero-padded slab (one launch for all slots).
+ * Replaces the memoized fp16 transposed copies of lorafusion/ops/triton_ops.py:114-152.
+ * For slot s, src_ptrs_dev[s] points at a row-major matrix whose rank dimension is
+ * dim `rank_dim` (0: [r_s, other], 1: [other, r_s]).  The slab is [n_slots, d0, d1]:
+ *   transpose = 0: dst[s][i][j] = src_s[i][j]
+ *   transpose = 1: dst[s][i][j] = src_s[j][i]
+ * and zero wherever the source index is outside the matrix.
+ */
+LF_API int lf_pack_adapters(int32_t src_dtype, int32_t dst_dtype, const uint64_t* src_ptrs_dev,
+                     const int32_t* slot_rank_dev, int32_t n_slots, int32_t rank_dim, int32_t other_dim,
+                     int32_t transpose, int32_t d0, int32_t d1, void* dst_dev, lf_stream_t stream);
+
+/*
+ * Forward: y [T,N] (dtype of the problem).
+ * Replaces triton_ops.fused_lora_forward (lorafusion/ops/triton_ops.py:373-409) and
+ * mock_ops.fused_lora_forward (lorafusion/ops/mock_ops.py:15-48).
+ */
+LF_API int lf_forward(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, void* y_dev,
+               void* workspace_dev, size_t workspace_bytes, lf_stream_t stream);
+
+/*
+ * The forward in separately launchable stages (same arguments as lf_forward), so a caller
+ * can time or overlap them.  `stages` is a bit mask:
+ *   LF_STAGE_SHRINK   routed shrink: workspace <- s_i x A_i^T, masked per segment tile
+ *   LF_STAGE_EXPAND   fused base GEMM + LoRA expand into y (reads the shrink's workspace)
+ *   LF_STAGE_BASE     base GEMM only, y = x W^T (the "LoRA disabled" yardstick)
+ * lf_forward == lf_forward_stages(..., LF_STAGE_SHRINK | LF_STAGE_EXPAND).
+ * Has no counterpart in the reference (its forward is one call per route).
+ */
+#define LF_STAGE_SHRINK 1
+#define LF_STAGE_EXPAND 2
+#define LF_STAGE_BASE 4
+LF_API int lf_forward_stages(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, void* y_dev,
+                             void* workspace_dev, size_t workspace_bytes, int32_t stages, lf_stream_t stream);
+
+/*
+ * Backward: grad_x [T,K]; grad_a = concatenated [r_s, K] blocks and grad_b = concatenated
+ * [N, r_s] blocks, slot after slot (slot s starts at rank_prefix[s]*K and rank_prefix[s]*N).
+ * Replaces triton_ops.fused_lora_backward (triton_ops.py:412-468) and
+ * mock_ops.fused_lora_backward (mock_ops.py:51-95).
+ */
+LF_API int lf_backward(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
+                const void* grad_out_dev, void* grad_x_dev, void* grad_a_dev, void* grad_b_dev,
+                void* workspace_dev, size_t workspace_bytes, lf_stream_t stream);
+
+/*
+ * Read and clear the device-side error word (bounded-wait timeouts inside kernels).
+ * Synchronizes the current device.  *code = 0 when no kernel reported a problem.
+ */
+LF_API int lf_device_error(int32_t* code);
+
+/* Static description of a status code. */
+LF_API const char* lf_status_string(int status);
+
+/* Build identification: "lorafusion_b200 <version> sm_100a". */
+LF_API const char* lf_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LORAFUSION_B200_H */

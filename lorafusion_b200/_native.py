@@ -1,0 +1,125 @@
+"""ctypes binding of the C ABI declared in ``include/lorafusion_b200.h``.
+
+The shared library is built in-tree (``python -m lorafusion_b200.csrc.build``)
+into ``lorafusion_b200/_lib/liblorafusion_b200.so``.  :func:`lib` loads it once
+and raises ``RuntimeError`` when it is missing: the operator has no fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "liblorafusion_b200.so")
+HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "lorafusion_b200.h")
+
+LF_OK = 0
+LF_ERR_INVALID_ARG = 1
+LF_ERR_ROUTING = 2
+LF_ERR_UNSUPPORTED = 3
+LF_ERR_CUDA = 4
+LF_ERR_CAPACITY = 5
+LF_ERR_DEVICE = 6
+
+LF_F32, LF_BF16, LF_F16 = 0, 1, 2
+LF_STAGE_SHRINK, LF_STAGE_EXPAND, LF_STAGE_BASE = 1, 2, 4
+TILE_ROWS = 128
+
+_c_i32 = ctypes.c_int32
+_c_p = ctypes.c_void_p
+
+
+class PlanInfo(ctypes.Structure):
+    _fields_ = [(name, _c_i32) for name in (
+        "total_rows", "n_routes", "n_slots", "n_tiles", "n_segtiles", "r_pad", "max_rank", "rank_total",
+        "n_shrink_units", "table_words",
+        "off_tile_st", "off_st_tile", "off_st_lo", "off_st_hi", "off_st_slot", "off_st_route", "off_st_scale",
+        "off_slot_st", "off_slot_list", "off_slot_rank", "off_rank_prefix", "off_slot_order",
+        "off_unit_tile", "off_unit_st0", "off_unit_nst")]
+
+
+class Problem(ctypes.Structure):
+    _fields_ = [
+        ("dtype", _c_i32), ("T", _c_i32), ("K", _c_i32), ("N", _c_i32),
+        ("x_dev", _c_p), ("w_dev", _c_p), ("a_pack_dev", _c_p), ("b_pack_dev", _c_p),
+        ("bt_pack_dev", _c_p), ("at_pack_dev", _c_p),
+    ]
+
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def _declare(L: ctypes.CDLL) -> None:
+    P = ctypes.POINTER
+    L.lf_plan_table_words.argtypes = [_c_i32, _c_i32, _c_i32]
+    L.lf_plan_table_words.restype = _c_i32
+    L.lf_plan_tables.argtypes = [P(_c_i32), P(_c_i32), P(_c_i32), _c_i32, _c_i32, P(_c_i32),
+                                 P(ctypes.c_float), _c_i32, P(_c_i32), _c_i32, P(PlanInfo)]
+    L.lf_plan_tables.restype = ctypes.c_int
+    L.lf_forward_workspace_bytes.argtypes = [P(PlanInfo), _c_i32]
+    L.lf_forward_workspace_bytes.restype = ctypes.c_size_t
+    L.lf_backward_workspace_bytes.argtypes = [P(PlanInfo), _c_i32]
+    L.lf_backward_workspace_bytes.restype = ctypes.c_size_t
+    L.lf_pack_adapters.argtypes = [_c_i32, _c_i32, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+                                   _c_p, _c_p]
+    L.lf_pack_adapters.restype = ctypes.c_int
+    L.lf_forward.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, ctypes.c_size_t, _c_p]
+    L.lf_forward.restype = ctypes.c_int
+    L.lf_forward_stages.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, ctypes.c_size_t, _c_i32, _c_p]
+    L.lf_forward_stages.restype = ctypes.c_int
+    L.lf_backward.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_size_t, _c_p]
+    L.lf_backward.restype = ctypes.c_int
+    L.lf_device_error.argtypes = [P(_c_i32)]
+    L.lf_device_error.restype = ctypes.c_int
+    L.lf_status_string.argtypes = [ctypes.c_int]
+    L.lf_status_string.restype = ctypes.c_char_p
+    L.lf_version.argtypes = []
+    L.lf_version.restype = ctypes.c_char_p
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; ``RuntimeError`` if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"lorafusion_b200 native library not found at {LIB_PATH}; "
+                    "build it with `python -m lorafusion_b200.csrc.build` (needs nvcc for sm_100a)")
+            L = ctypes.CDLL(LIB_PATH)
+            _declare(L)
+            _lib = L
+    return _lib
+
+
+def header_symbols() -> list[str]:
+    """Names of every entry point the public header declares."""
+    text = open(HEADER_PATH).read()
+    return re.findall(r"^LF_API\s+[\w\s\*]+?\b(lf_\w+)\s*\(", text, flags=re.M)
+
+
+def status_text(code: int) -> str:
+    return lib().lf_status_string(code).decode()
+
+
+def check(code: int, what: str) -> None:
+    """Map a C status to the reference's exception types."""
+    if code == LF_OK:
+        return
+    msg = f"{what}: {status_text(code)} (status {code})"
+    if code in (LF_ERR_CUDA, LF_ERR_DEVICE):
+        raise RuntimeError(msg)
+    raise ValueError(msg)
+
+
+def device_error() -> int:
+    """Read and clear the kernels' device status word (synchronizes the device)."""
+    v = _c_i32(0)
+    check(lib().lf_device_error(ctypes.byref(v)), "lf_device_error")
+    return int(v.value)

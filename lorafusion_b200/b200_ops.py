@@ -1,0 +1,327 @@
+"""B200 backend of lorafusion's fused multi-adapter LoRA op.
+
+Drop-in for ``lorafusion.ops.mock_ops`` / ``lorafusion.ops.triton_ops``: the same
+two functions with the same signatures, return conventions and exceptions
+(``lorafusion/ops/mock_ops.py:15-95``, ``lorafusion/ops/triton_ops.py:373-468``),
+so ``Coordinator(backend=b200_ops)`` (``lorafusion/runtime/coordinator.py:32,58-65``)
+runs it unchanged.  All arithmetic happens in the sm_100a library behind
+``include/lorafusion_b200.h``; there is no CPU path and no fallback: CPU inputs
+raise ``ValueError`` and a missing library raises ``RuntimeError``.
+
+Per call, on the current CUDA stream:
+  forward   1 routed shrink + 1 fused base-GEMM/LoRA-expand launch
+  backward  2 routed shrinks + 1 fused dX launch + 2 segmented gram launches
+
+Host work is cached the way ``triton_ops._prepare`` caches its weight copies
+(``triton_ops.py:114-145``): routing tables per routing object, packed adapter
+slabs per (tensor identity, storage pointer, version counter) of every adapter
+tensor, converted base weights likewise.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import weakref
+
+import numpy as np
+import torch
+
+from lorafusion_b200 import _native as nat
+
+_DTYPE_CODE = {torch.float32: nat.LF_F32, torch.bfloat16: nat.LF_BF16, torch.float16: nat.LF_F16}
+
+__all__ = ["fused_lora_forward", "fused_lora_backward", "clear_weight_cache", "last_launch_count"]
+
+
+# --------------------------------------------------------------------------- caches
+_ROUTE_CACHE: dict[int, tuple] = {}
+_PLAN_CACHE: dict[tuple, "_Plan"] = {}
+_PACK_CACHE: dict[tuple, dict] = {}
+_WEIGHT_CACHE: dict[tuple, tuple] = {}
+_CACHE_MAX = 256
+_LAUNCHES = {"forward": 2, "backward": 5}
+_last_launches = 0
+
+
+def clear_weight_cache() -> None:
+    """Drop every cached table, packed adapter slab and converted weight."""
+    _ROUTE_CACHE.clear()
+    _PLAN_CACHE.clear()
+    _PACK_CACHE.clear()
+    _WEIGHT_CACHE.clear()
+
+
+def last_launch_count() -> int:
+    """Kernel launches issued by the most recent op call (0 for empty problems)."""
+    return _last_launches
+
+
+def _route_arrays(routing):
+    """(starts, ends, adapter ids, slot of each route, slot adapter ids) for a routing object."""
+    routes = routing.routes
+    key = id(routing)
+    hit = _ROUTE_CACHE.get(key)
+    if hit is not None:
+        ref, rlist, n, arrays = hit
+        if ref() is routing and rlist is routes and n == len(routes):
+            return arrays
+    starts = np.fromiter((r.row_start for r in routes), dtype=np.int32, count=len(routes))
+    ends = np.fromiter((r.row_end for r in routes), dtype=np.int32, count=len(routes))
+    aids = [r.adapter_id for r in routes]
+    slot_of: dict[int, int] = {}
+    route_slot = np.empty(len(routes), dtype=np.int32)
+    for i, aid in enumerate(aids):
+        route_slot[i] = slot_of.setdefault(aid, len(slot_of))
+    arrays = (starts, ends, route_slot, list(slot_of))
+    if len(_ROUTE_CACHE) >= _CACHE_MAX:
+        _ROUTE_CACHE.clear()
+    try:
+        _ROUTE_CACHE[key] = (weakref.ref(routing), routes, len(routes), arrays)
+    except TypeError:  # pragma: no cover - routing object without weakref support
+        pass
+    return arrays
+
+
+class _Plan:
+    __slots__ = ("info", "table_dev", "slots", "ranks")
+
+    def __init__(self, info, table_dev, slots, ranks):
+        self.info = info
+        self.table_dev = table_dev
+        self.slots = slots
+        self.ranks = ranks
+
+
+def _plan(routing, total_rows: int, adapters, lora_a, device: torch.device) -> _Plan:
+    starts, ends, route_slot, slots = _route_arrays(routing)
+    ranks = tuple(int(lora_a[aid].shape[0]) for aid in slots)
+    scales = tuple(float(adapters[aid].scaling) for aid in slots)
+    key = (id(routing), total_rows, device, ranks, scales)
+    hit = _PLAN_CACHE.get(key)
+    if hit is not None and hit[0]() is routing:
+        return hit[1]
+    L = nat.lib()
+    n_routes = len(starts)
+    cap = L.lf_plan_table_words(n_routes, total_rows, len(slots))
+    if cap < 0:
+        raise ValueError("routing too large for int32 tables")
+    table = torch.empty(max(cap, 1), dtype=torch.int32, pin_memory=True)
+    info = nat.PlanInfo()
+    rk = np.asarray(ranks, dtype=np.int32)
+    sc = np.asarray(scales, dtype=np.float32)
+    i32p = ctypes.POINTER(ctypes.c_int32)
+    rc = L.lf_plan_tables(
+        starts.ctypes.data_as(i32p), ends.ctypes.data_as(i32p), route_slot.ctypes.data_as(i32p), n_routes,
+        total_rows, rk.ctypes.data_as(i32p), sc.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), len(slots),
+        ctypes.cast(table.data_ptr(), i32p), cap, ctypes.byref(info))
+    nat.check(rc, "lf_plan_tables")
+    table_dev = table[: max(info.table_words, 1)].to(device, non_blocking=True)
+    plan = _Plan(info, table_dev, slots, ranks)
+    if len(_PLAN_CACHE) >= _CACHE_MAX:
+        _PLAN_CACHE.clear()
+    try:
+        _PLAN_CACHE[key] = (weakref.ref(routing), plan)
+    except TypeError:  # pragma: no cover
+        pass
+    return plan
+
+
+def _tensor_sig(t: torch.Tensor):
+    return (id(t), t.data_ptr(), t._version)
+
+
+def _pack(plan: _Plan, lora_a, lora_b, dtype: torch.dtype, K: int, N: int, device, backward: bool) -> dict:
+    """Zero-padded adapter slabs in the layouts the kernels read (cached)."""
+    slots = plan.slots
+    a_list = [lora_a[aid] for aid in slots]
+    b_list = [lora_b[aid] for aid in slots]
+    key = (tuple(slots), tuple(_tensor_sig(t) for t in a_list), tuple(_tensor_sig(t) for t in b_list),
+           dtype, K, N, device, plan.info.r_pad)
+    entry = _PACK_CACHE.get(key)
+    if entry is None:
+        for aid, a, b, r in zip(slots, a_list, b_list, plan.ranks):
+            if a.dim() != 2 or a.shape[1] != K or b.dim() != 2 or b.shape != (N, r):
+                raise ValueError(
+                    f"adapter {aid}: lora_a {tuple(a.shape)} / lora_b {tuple(b.shape)} do not match "
+                    f"in_features={K}, out_features={N}")
+            if a.device != device or b.device != device:
+                raise ValueError(f"adapter {aid}: LoRA weights must live on {device}")
+        if len(_PACK_CACHE) >= _CACHE_MAX:
+            _PACK_CACHE.clear()
+        a_src = [t if t.is_contiguous() else t.contiguous() for t in a_list]
+        b_src = [t if t.is_contiguous() else t.contiguous() for t in b_list]
+        entry = {"src": (a_src, b_src), "keep": (a_list, b_list)}
+        _PACK_CACHE[key] = entry
+    want = ("a", "b", "bt", "at") if backward else ("a", "b")
+    missing = [w for w in want if w not in entry]
+    if missing:
+        _fill_packs(entry, plan, dtype, K, N, device, missing)
+    return entry
+
+
+def _fill_packs(entry, plan: _Plan, dtype, K, N, device, which) -> None:
+    L = nat.lib()
+    a_src, b_src = entry["src"]
+    n = len(plan.slots)
+    rp = plan.info.r_pad
+    ranks_dev = torch.tensor(plan.ranks if n else [0], dtype=torch.int32).to(device, non_blocking=True)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    dst_code = _DTYPE_CODE[dtype]
+    for w in which:
+        srcs = a_src if w in ("a", "at") else b_src
+        src_code = _DTYPE_CODE.get(srcs[0].dtype) if n else dst_code
+        if n and any(t.dtype != srcs[0].dtype for t in srcs):
+            srcs = [t.to(srcs[0].dtype) for t in srcs]
+            entry.setdefault("converted", []).append(srcs)
+        if src_code is None:
+            raise ValueError(f"unsupported LoRA weight dtype {srcs[0].dtype}")
+        ptrs = torch.tensor([t.data_ptr() for t in srcs] if n else [0], dtype=torch.int64).to(
+            device, non_blocking=True)
+        # (rank_dim, other_dim, transpose, d0, d1)
+        spec = {
+            "a": (0, K, 0, rp, K),   # A_i [r, K]  -> [slot, r_pad, K]
+            "at": (0, K, 1, K, rp),  # A_i [r, K]  -> [slot, K, r_pad]
+            "b": (1, N, 0, N, rp),   # B_i [N, r]  -> [slot, N, r_pad]
+            "bt": (1, N, 1, rp, N),  # B_i [N, r]  -> [slot, r_pad, N]
+        }[w]
+        dst = torch.empty((max(n, 1), spec[3], spec[4]), dtype=dtype, device=device)
+        rc = L.lf_pack_adapters(src_code, dst_code, ptrs.data_ptr(), ranks_dev.data_ptr(), n, spec[0], spec[1],
+                                spec[2], spec[3], spec[4], dst.data_ptr(), stream)
+        nat.check(rc, "lf_pack_adapters")
+        entry[w] = dst
+        entry.setdefault("ptr_bufs", []).append((ptrs, ranks_dev))
+
+
+def _weight(base_weight: torch.Tensor, dtype, device) -> torch.Tensor:
+    """Base weight as a contiguous tensor of the activation dtype (converted copies cached)."""
+    if base_weight.device != device:
+        raise ValueError(f"base_weight must live on {device}")
+    if base_weight.dtype == dtype and base_weight.is_contiguous():
+        return base_weight
+    key = (id(base_weight), dtype)
+    hit = _WEIGHT_CACHE.get(key)
+    if hit is not None:
+        ref, ptr, ver, conv = hit
+        if ref() is base_weight and ptr == base_weight.data_ptr() and ver == base_weight._version:
+            return conv
+    conv = base_weight.to(dtype).contiguous()
+    if len(_WEIGHT_CACHE) >= _CACHE_MAX:
+        _WEIGHT_CACHE.clear()
+    try:
+        _WEIGHT_CACHE[key] = (weakref.ref(base_weight), base_weight.data_ptr(), base_weight._version, conv)
+    except TypeError:  # pragma: no cover
+        pass
+    return conv
+
+
+def _activation(t: torch.Tensor, name: str) -> torch.Tensor:
+    if t.dim() != 2:
+        raise ValueError(f"{name} must be 2-D, got shape {tuple(t.shape)}")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor: lorafusion_b200 has no CPU path")
+    if t.dtype not in _DTYPE_CODE:
+        raise ValueError(f"{name}: unsupported dtype {t.dtype} (float32, bfloat16, float16)")
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def _problem(code, T, K, N, x, w, packs) -> nat.Problem:
+    p = nat.Problem()
+    p.dtype, p.T, p.K, p.N = code, T, K, N
+    p.x_dev = x.data_ptr()
+    p.w_dev = w.data_ptr()
+    p.a_pack_dev = packs["a"].data_ptr()
+    p.b_pack_dev = packs["b"].data_ptr()
+    if "bt" in packs:
+        p.bt_pack_dev = packs["bt"].data_ptr()
+        p.at_pack_dev = packs["at"].data_ptr()
+    return p
+
+
+def fused_lora_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> torch.Tensor:
+    """``y = x W^T + s_i (x A_i^T) B_i^T`` per routed row range.
+
+    Same contract as ``mock_ops.fused_lora_forward`` (mock_ops.py:15-48):
+    ``routing.validate`` runs first (``ValueError``); the result is a new
+    ``[T, out_features]`` tensor in ``x.dtype``.
+    """
+    global _last_launches
+    routing.validate(x.shape[0])
+    _last_launches = 0
+    x = _activation(x, "x")
+    device = x.device
+    T, K = x.shape
+    N = base_weight.shape[0]
+    if base_weight.dim() != 2 or base_weight.shape[1] != K:
+        raise ValueError(f"base_weight {tuple(base_weight.shape)} does not match x {tuple(x.shape)}")
+    dtype = x.dtype
+    code = _DTYPE_CODE[dtype]
+    for r in routing.routes:  # KeyError for an unknown adapter, like the reference
+        adapters[r.adapter_id]
+    w = _weight(base_weight, dtype, device)
+    plan = _plan(routing, T, adapters, lora_a, device)
+    packs = _pack(plan, lora_a, lora_b, dtype, K, N, device, backward=False)
+    y = torch.empty((T, N), dtype=dtype, device=device)
+    if T == 0 or N == 0:
+        return y
+    L = nat.lib()
+    ws_bytes = L.lf_forward_workspace_bytes(ctypes.byref(plan.info), code)
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=device)
+    prob = _problem(code, T, K, N, x, w, packs)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    rc = L.lf_forward(ctypes.byref(prob), ctypes.byref(plan.info), plan.table_dev.data_ptr(), y.data_ptr(),
+                      ws.data_ptr(), ws.numel(), stream)
+    nat.check(rc, "lf_forward")
+    _last_launches = _LAUNCHES["forward"]
+    return y
+
+
+def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, routing):
+    """Return ``(grad_x, grad_lora_a, grad_lora_b)`` as ``mock_ops.fused_lora_backward``.
+
+    mock_ops.py:51-95: the base weight is frozen (no gradient); the dicts hold
+    one entry per adapter that owns a route, in order of first appearance,
+    each summed over that adapter's routes; tensors are in ``x.dtype``.
+    """
+    global _last_launches
+    routing.validate(x.shape[0])
+    _last_launches = 0
+    x = _activation(x, "x")
+    g = _activation(grad_out, "grad_out")
+    device = x.device
+    T, K = x.shape
+    N = base_weight.shape[0]
+    if g.shape != (T, N):
+        raise ValueError(f"grad_out {tuple(g.shape)} does not match [{T}, {N}]")
+    if base_weight.dim() != 2 or base_weight.shape[1] != K:
+        raise ValueError(f"base_weight {tuple(base_weight.shape)} does not match x {tuple(x.shape)}")
+    dtype = x.dtype
+    if g.dtype != dtype:
+        g = g.to(dtype)
+    code = _DTYPE_CODE[dtype]
+    for r in routing.routes:
+        adapters[r.adapter_id]
+    w = _weight(base_weight, dtype, device)
+    plan = _plan(routing, T, adapters, lora_a, device)
+    packs = _pack(plan, lora_a, lora_b, dtype, K, N, device, backward=True)
+    info = plan.info
+    rtot = info.rank_total
+    grad_x = torch.empty((T, K), dtype=dtype, device=device)
+    ga_flat = torch.empty(max(rtot * K, 1), dtype=dtype, device=device)
+    gb_flat = torch.empty(max(rtot * N, 1), dtype=dtype, device=device)
+    L = nat.lib()
+    ws_bytes = L.lf_backward_workspace_bytes(ctypes.byref(info), code)
+    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=device)
+    prob = _problem(code, T, K, N, x, w, packs)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    rc = L.lf_backward(ctypes.byref(prob), ctypes.byref(info), plan.table_dev.data_ptr(), g.data_ptr(),
+                       grad_x.data_ptr(), ga_flat.data_ptr(), gb_flat.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+    nat.check(rc, "lf_backward")
+    _last_launches = _LAUNCHES["backward"] if T > 0 else 0
+    grad_a: dict[int, torch.Tensor] = {}
+    grad_b: dict[int, torch.Tensor] = {}
+    off = 0
+    for aid, r in zip(plan.slots, plan.ranks):
+        grad_a[aid] = ga_flat[off * K:(off + r) * K].view(r, K)
+        grad_b[aid] = gb_flat[off * N:(off + r) * N].view(N, r)
+        off += r
+    return grad_x, grad_a, grad_b

@@ -1,0 +1,339 @@
+// C ABI of the fused multi-adapter LoRA operator: argument checks, TMA descriptors,
+// kernel dispatch.  No torch types cross this boundary; see include/lorafusion_b200.h.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "lf_internal.cuh"
+
+namespace lf {
+
+// Device status word written by bounded waits inside the kernels (one per device context).
+__device__ int g_device_status = 0;
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct DeviceState {
+  bool ready = false;
+  int num_sms = 0;
+  int* status = nullptr;  // address of g_device_status on this device
+};
+
+std::mutex g_mu;
+DeviceState g_dev[64];
+EncodeTiledFn g_encode = nullptr;
+
+int elem_bytes(int dtype) { return dtype == LF_F32 ? 4 : 2; }
+
+cudaError_t device_state(DeviceState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& d = g_dev[dev];
+  if (!d.ready) {
+    e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.status), g_device_status);
+    if (e != cudaSuccess) return e;
+    d.ready = true;
+  }
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return e != cudaSuccess ? e : cudaErrorUnknown;
+    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  *out = &d;
+  return cudaSuccess;
+}
+
+// 2-D tile map over a row-major [outer, inner] matrix with row pitch `pitch_bytes`.
+bool make_map(CUtensorMap* m, int dtype, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch_bytes,
+              uint32_t box_inner, uint32_t box_outer) {
+  const uint32_t span = box_inner * static_cast<uint32_t>(elem_bytes(dtype));
+  CUtensorMapSwizzle sw = span == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                          : span == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                       : CU_TENSOR_MAP_SWIZZLE_32B;
+  if (span != 128 && span != 64 && span != 32) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {pitch_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt = dtype == LF_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  std::memset(m, 0, sizeof(*m));
+  CUresult r = g_encode(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int to_status(cudaError_t e) { return e == cudaSuccess ? LF_OK : LF_ERR_CUDA; }
+
+size_t segtile_elems(const lf_plan_info* info) {
+  return static_cast<size_t>(info->n_segtiles) * LF_TILE_ROWS * static_cast<size_t>(info->r_pad);
+}
+
+// one S_ext buffer, sized for f32 so the CUDA-core path can use it too, 256-byte multiple
+size_t sext_bytes(const lf_plan_info* info) { return (segtile_elems(info) * 4 + 255) & ~size_t(255); }
+
+int check_problem(const lf_problem* p, const lf_plan_info* info, const int32_t* table_dev) {
+  if (!p || !info || (!table_dev && info->table_words > 0)) return LF_ERR_INVALID_ARG;
+  if (p->dtype != LF_F32 && p->dtype != LF_BF16 && p->dtype != LF_F16) return LF_ERR_INVALID_ARG;
+  if (p->T < 0 || p->K < 0 || p->N < 0) return LF_ERR_INVALID_ARG;
+  if (p->T != info->total_rows) return LF_ERR_ROUTING;
+  if (info->r_pad != 16 && info->r_pad != 32 && info->r_pad != 64) return LF_ERR_INVALID_ARG;
+  return LF_OK;
+}
+
+// Tensor-core path: bf16/f16 with every row pitch and base 16-byte aligned (TMA).
+bool tc_eligible(const lf_problem* p, std::initializer_list<const void*> ptrs) {
+  if (p->dtype == LF_F32) return false;
+  if (p->K == 0 || p->N == 0 || p->K % 8 != 0 || p->N % 8 != 0) return false;
+  for (const void* q : ptrs)
+    if (q && !aligned16(q)) return false;
+  return true;
+}
+
+}  // namespace
+
+Tables make_tables(const lf_plan_info* info, const int32_t* table_dev) {
+  Tables t{};
+  t.base = table_dev;
+  t.off_tile_st = info->off_tile_st;
+  t.off_st_tile = info->off_st_tile;
+  t.off_st_lo = info->off_st_lo;
+  t.off_st_hi = info->off_st_hi;
+  t.off_st_slot = info->off_st_slot;
+  t.off_st_scale = info->off_st_scale;
+  t.off_slot_st = info->off_slot_st;
+  t.off_slot_list = info->off_slot_list;
+  t.off_slot_rank = info->off_slot_rank;
+  t.off_rank_prefix = info->off_rank_prefix;
+  t.off_slot_order = info->off_slot_order;
+  t.off_unit_tile = info->off_unit_tile;
+  t.off_unit_st0 = info->off_unit_st0;
+  t.off_unit_nst = info->off_unit_nst;
+  t.n_tiles = info->n_tiles;
+  t.n_segtiles = info->n_segtiles;
+  t.n_slots = info->n_slots;
+  t.n_units = info->n_shrink_units;
+  t.r_pad = info->r_pad;
+  t.err = nullptr;
+  return t;
+}
+
+}  // namespace lf
+
+using namespace lf;
+
+extern "C" size_t lf_forward_workspace_bytes(const lf_plan_info* info, int32_t dtype) {
+  (void)dtype;
+  return info ? sext_bytes(info) : 0;
+}
+
+extern "C" size_t lf_backward_workspace_bytes(const lf_plan_info* info, int32_t dtype) {
+  (void)dtype;
+  return info ? 2 * sext_bytes(info) : 0;
+}
+
+extern "C" int lf_pack_adapters(int32_t src_dtype, int32_t dst_dtype, const uint64_t* src_ptrs_dev,
+                                const int32_t* slot_rank_dev, int32_t n_slots, int32_t rank_dim, int32_t other_dim,
+                                int32_t transpose, int32_t d0, int32_t d1, void* dst_dev, lf_stream_t stream) {
+  if (src_dtype < 0 || src_dtype > 2 || dst_dtype < 0 || dst_dtype > 2) return LF_ERR_INVALID_ARG;
+  if (n_slots < 0 || d0 < 0 || d1 < 0 || other_dim < 0 || (rank_dim != 0 && rank_dim != 1)) return LF_ERR_INVALID_ARG;
+  if (n_slots == 0 || d0 == 0 || d1 == 0) return LF_OK;
+  if (!src_ptrs_dev || !slot_rank_dev || !dst_dev) return LF_ERR_INVALID_ARG;
+  return to_status(pack_adapters(src_dtype, dst_dtype, src_ptrs_dev, slot_rank_dev, n_slots, rank_dim, other_dim,
+                                 transpose, d0, d1, dst_dev, static_cast<cudaStream_t>(stream)));
+}
+
+extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
+                                 void* y_dev, void* workspace_dev, size_t workspace_bytes, int32_t stages,
+                                 lf_stream_t stream) {
+  int rc = check_problem(prob, info, table_dev);
+  if (rc != LF_OK) return rc;
+  if (stages <= 0 || stages > 7 || ((stages & LF_STAGE_EXPAND) && (stages & LF_STAGE_BASE))) return LF_ERR_INVALID_ARG;
+  const int T = prob->T, K = prob->K, N = prob->N;
+  if (T == 0 || N == 0) return LF_OK;
+  if (!prob->x_dev || !prob->w_dev || !prob->a_pack_dev || !prob->b_pack_dev || !y_dev) return LF_ERR_INVALID_ARG;
+  if (workspace_bytes < sext_bytes(info) || (!workspace_dev && sext_bytes(info) > 0)) return LF_ERR_CAPACITY;
+  DeviceState* ds = nullptr;
+  cudaError_t e = device_state(&ds);
+  if (e != cudaSuccess) return LF_ERR_CUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Tables tb = make_tables(info, table_dev);
+  tb.err = ds->status;
+  const int dt = prob->dtype;
+  const int rp = info->r_pad;
+  const bool do_shrink = (stages & LF_STAGE_SHRINK) != 0;
+  const bool do_gemm = (stages & (LF_STAGE_EXPAND | LF_STAGE_BASE)) != 0;
+  const bool lora = (stages & LF_STAGE_EXPAND) != 0 && info->n_segtiles > 0;
+
+  if (tc_eligible(prob, {prob->x_dev, prob->w_dev, prob->a_pack_dev, prob->b_pack_dev, y_dev, workspace_dev})) {
+    TcMaps maps;
+    CUtensorMap a_map;
+    const size_t es = 2;
+    bool ok = make_map(&maps.p, dt, prob->x_dev, K, T, K * es, 64, 128) &&
+              make_map(&maps.q, dt, prob->w_dev, K, N, K * es, 64, 256) &&
+              make_map(&a_map, dt, prob->a_pack_dev, K, static_cast<uint64_t>(info->n_slots) * rp, K * es, 64, rp);
+    if (info->n_segtiles > 0)
+      ok = ok &&
+           make_map(&maps.s, dt, workspace_dev, rp, static_cast<uint64_t>(info->n_segtiles) * LF_TILE_ROWS, rp * es,
+                    rp, 128) &&
+           make_map(&maps.l, dt, prob->b_pack_dev, rp, static_cast<uint64_t>(info->n_slots) * N, rp * es, rp, 256);
+    else
+      maps.s = maps.l = maps.p;
+    if (!ok) return LF_ERR_UNSUPPORTED;
+    if (do_shrink) {
+      e = tc_shrink(dt, maps.p, a_map, K, tb, workspace_dev, ds->num_sms, st);
+      if (e != cudaSuccess) return LF_ERR_CUDA;
+    }
+    if (do_gemm) e = tc_gemm(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st);
+    return to_status(e);
+  }
+
+  float* s_ext = static_cast<float*>(workspace_dev);
+  if (do_shrink) {
+    e = simt_shrink(dt, prob->x_dev, K, K, prob->a_pack_dev, tb, s_ext, st);
+    if (e != cudaSuccess) return LF_ERR_CUDA;
+  }
+  if (do_gemm)
+    e = simt_gemm(dt, prob->x_dev, K, prob->w_dev, K, 1, T, N, K, s_ext, lora ? prob->b_pack_dev : nullptr, tb, y_dev,
+                  N, st);
+  return to_status(e);
+}
+
+extern "C" int lf_forward(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, void* y_dev,
+                          void* workspace_dev, size_t workspace_bytes, lf_stream_t stream) {
+  return lf_forward_stages(prob, info, table_dev, y_dev, workspace_dev, workspace_bytes,
+                           LF_STAGE_SHRINK | LF_STAGE_EXPAND, stream);
+}
+
+extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
+                           const void* grad_out_dev, void* grad_x_dev, void* grad_a_dev, void* grad_b_dev,
+                           void* workspace_dev, size_t workspace_bytes, lf_stream_t stream) {
+  int rc = check_problem(prob, info, table_dev);
+  if (rc != LF_OK) return rc;
+  const int T = prob->T, K = prob->K, N = prob->N;
+  const size_t sb = sext_bytes(info);
+  if (workspace_bytes < 2 * sb || (!workspace_dev && sb > 0)) return LF_ERR_CAPACITY;
+  DeviceState* ds = nullptr;
+  cudaError_t e = device_state(&ds);
+  if (e != cudaSuccess) return LF_ERR_CUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int dt = prob->dtype;
+  const size_t es = static_cast<size_t>(elem_bytes(dt));
+  if (info->n_slots > 0 && (!grad_a_dev || !grad_b_dev)) return LF_ERR_INVALID_ARG;
+  if (T == 0 || info->n_segtiles == 0) {  // adapters whose routes are all empty still get (zero) gradients
+    const size_t ra = static_cast<size_t>(info->rank_total);
+    if (ra > 0 && K > 0 && cudaMemsetAsync(grad_a_dev, 0, ra * K * es, st) != cudaSuccess) return LF_ERR_CUDA;
+    if (ra > 0 && N > 0 && cudaMemsetAsync(grad_b_dev, 0, ra * N * es, st) != cudaSuccess) return LF_ERR_CUDA;
+    if (T == 0) return LF_OK;
+  }
+  if (!prob->x_dev || !prob->w_dev || !grad_out_dev || !grad_x_dev) return LF_ERR_INVALID_ARG;
+  if (info->n_slots > 0 && (!prob->a_pack_dev || !prob->bt_pack_dev || !prob->at_pack_dev))
+    return LF_ERR_INVALID_ARG;
+  Tables tb = make_tables(info, table_dev);
+  tb.err = ds->status;
+  const int rp = info->r_pad;
+  char* ws = static_cast<char*>(workspace_dev);
+  void* s_f = ws;
+  void* s_b = ws + sb;
+
+  if (tc_eligible(prob, {prob->x_dev, prob->w_dev, prob->a_pack_dev, prob->bt_pack_dev, prob->at_pack_dev,
+                         grad_out_dev, grad_x_dev, workspace_dev})) {
+    CUtensorMap p_x, p_g, a_map, bt_map, sf_map, sb_map;
+    TcMaps dx;
+    bool ok = make_map(&p_x, dt, prob->x_dev, K, T, K * es, 64, 128) &&
+              make_map(&p_g, dt, grad_out_dev, N, T, N * es, 64, 128) &&
+              make_map(&dx.q, dt, prob->w_dev, K, N, K * es, 64, 64);
+    const bool lora = info->n_segtiles > 0 && info->n_slots > 0;
+    if (lora)
+      ok = ok &&
+           make_map(&a_map, dt, prob->a_pack_dev, K, static_cast<uint64_t>(info->n_slots) * rp, K * es, 64, rp) &&
+           make_map(&bt_map, dt, prob->bt_pack_dev, N, static_cast<uint64_t>(info->n_slots) * rp, N * es, 64, rp) &&
+           make_map(&sf_map, dt, s_f, rp, static_cast<uint64_t>(info->n_segtiles) * LF_TILE_ROWS, rp * es, rp, 128) &&
+           make_map(&sb_map, dt, s_b, rp, static_cast<uint64_t>(info->n_segtiles) * LF_TILE_ROWS, rp * es, rp, 128) &&
+           make_map(&dx.l, dt, prob->at_pack_dev, rp, static_cast<uint64_t>(info->n_slots) * K, rp * es, rp, 256);
+    if (!ok) return LF_ERR_UNSUPPORTED;
+    dx.p = p_g;
+    if (lora) {
+      dx.s = sb_map;
+      e = tc_shrink(dt, p_x, a_map, K, tb, s_f, ds->num_sms, st);
+      if (e != cudaSuccess) return LF_ERR_CUDA;
+      e = tc_shrink(dt, p_g, bt_map, N, tb, s_b, ds->num_sms, st);
+      if (e != cudaSuccess) return LF_ERR_CUDA;
+    } else {
+      dx.s = dx.l = p_g;
+    }
+    e = tc_gemm(dt, true, dx, T, K, N, lora, tb, grad_x_dev, K, ds->num_sms, st);
+    if (e != cudaSuccess) return LF_ERR_CUDA;
+    if (lora) {
+      e = tc_gram(dt, p_g, sf_map, N, tb, grad_b_dev, 0, ds->num_sms, st);
+      if (e != cudaSuccess) return LF_ERR_CUDA;
+      e = tc_gram(dt, p_x, sb_map, K, tb, grad_a_dev, 1, ds->num_sms, st);
+      if (e != cudaSuccess) return LF_ERR_CUDA;
+    }
+    return LF_OK;
+  }
+
+  float* sf = static_cast<float*>(s_f);
+  float* sbp = static_cast<float*>(s_b);
+  e = simt_shrink(dt, prob->x_dev, K, K, prob->a_pack_dev, tb, sf, st);
+  if (e != cudaSuccess) return LF_ERR_CUDA;
+  e = simt_shrink(dt, grad_out_dev, N, N, prob->bt_pack_dev, tb, sbp, st);
+  if (e != cudaSuccess) return LF_ERR_CUDA;
+  // grad_x = g W + S_b . A   (Q(c, m) = W[m][c])
+  e = simt_gemm(dt, grad_out_dev, N, prob->w_dev, 1, K, T, K, N, sbp, prob->at_pack_dev, tb, grad_x_dev, K, st);
+  if (e != cudaSuccess) return LF_ERR_CUDA;
+  e = simt_gram(dt, grad_out_dev, N, N, sf, tb, grad_b_dev, 0, st);
+  if (e != cudaSuccess) return LF_ERR_CUDA;
+  e = simt_gram(dt, prob->x_dev, K, K, sbp, tb, grad_a_dev, 1, st);
+  return to_status(e);
+}
+
+extern "C" int lf_device_error(int32_t* code) {
+  if (!code) return LF_ERR_INVALID_ARG;
+  DeviceState* ds = nullptr;
+  if (device_state(&ds) != cudaSuccess) return LF_ERR_CUDA;
+  if (cudaDeviceSynchronize() != cudaSuccess) return LF_ERR_CUDA;
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess) return LF_ERR_CUDA;
+  const int zero = 0;
+  if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)) != cudaSuccess) return LF_ERR_CUDA;
+  *code = v;
+  return LF_OK;
+}
+
+extern "C" const char* lf_status_string(int status) {
+  switch (status) {
+    case LF_OK:
+      return "ok";
+    case LF_ERR_INVALID_ARG:
+      return "invalid argument";
+    case LF_ERR_ROUTING:
+      return "routes do not tile the fused rows";
+    case LF_ERR_UNSUPPORTED:
+      return "unsupported dtype, rank or alignment";
+    case LF_ERR_CUDA:
+      return "CUDA call failed";
+    case LF_ERR_CAPACITY:
+      return "buffer too small";
+    case LF_ERR_DEVICE:
+      return "a kernel gave up waiting (device timeout)";
+    default:
+      return "unknown status";
+  }
+}
+
+extern "C" const char* lf_version(void) { return "lorafusion_b200 0.1.0 sm_100a"; }

@@ -1,0 +1,71 @@
+// Internal declarations shared by the kernel translation units and the C ABI layer.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/lorafusion_b200.h"
+
+namespace lf {
+
+// Device view of the routing table (see lf_plan_info for the sections).
+struct Tables {
+  const int32_t* base;
+  int32_t off_tile_st, off_st_tile, off_st_lo, off_st_hi, off_st_slot, off_st_scale;
+  int32_t off_slot_st, off_slot_list, off_slot_rank, off_rank_prefix, off_slot_order;
+  int32_t off_unit_tile, off_unit_st0, off_unit_nst;
+  int32_t n_tiles, n_segtiles, n_slots, n_units, r_pad;
+  int* err;  // device status word for bounded-wait timeouts
+
+  __device__ __forceinline__ int32_t tile_st(int t) const { return base[off_tile_st + t]; }
+  __device__ __forceinline__ int32_t st_tile(int j) const { return base[off_st_tile + j]; }
+  __device__ __forceinline__ int32_t st_lo(int j) const { return base[off_st_lo + j]; }
+  __device__ __forceinline__ int32_t st_hi(int j) const { return base[off_st_hi + j]; }
+  __device__ __forceinline__ int32_t st_slot(int j) const { return base[off_st_slot + j]; }
+  __device__ __forceinline__ float st_scale(int j) const { return __int_as_float(base[off_st_scale + j]); }
+  __device__ __forceinline__ int32_t slot_st(int s) const { return base[off_slot_st + s]; }
+  __device__ __forceinline__ int32_t slot_list(int i) const { return base[off_slot_list + i]; }
+  __device__ __forceinline__ int32_t slot_rank(int s) const { return base[off_slot_rank + s]; }
+  __device__ __forceinline__ int32_t rank_prefix(int s) const { return base[off_rank_prefix + s]; }
+  __device__ __forceinline__ int32_t slot_order(int i) const { return base[off_slot_order + i]; }
+  __device__ __forceinline__ int32_t unit_tile(int u) const { return base[off_unit_tile + u]; }
+  __device__ __forceinline__ int32_t unit_st0(int u) const { return base[off_unit_st0 + u]; }
+  __device__ __forceinline__ int32_t unit_nst(int u) const { return base[off_unit_nst + u]; }
+};
+
+Tables make_tables(const lf_plan_info* info, const int32_t* table_dev);
+
+// --------------------------------------------------------------- SIMT (any dtype, f32 math)
+// S_ext[st][row][j] = (row in segment) ? scale * sum_k P[tile*128+row][k] * Apk[slot][j][k] : 0
+cudaError_t simt_shrink(int dtype, const void* P, int64_t ldp, int Kred, const void* apk, const Tables& tb,
+                        float* s_ext, cudaStream_t st);
+// out[t][n] = sum_k P[t][k] Q(n,k) + sum_j S_ext[st(t)][row][j] * L[slot][n][j],  Q(n,k) = Q[n*qsn + k*qsk]
+cudaError_t simt_gemm(int dtype, const void* P, int64_t ldp, const void* Q, int64_t qsn, int64_t qsk, int T, int Nout,
+                      int Kred, const float* s_ext, const void* lpk, const Tables& tb, void* out, int64_t ldo,
+                      cudaStream_t st);
+// grad[slot] = sum_{rows of slot} D[row][c] * S_ext[..][row][j]; layout [C][rank] or [rank][C] (transpose_out)
+cudaError_t simt_gram(int dtype, const void* D, int64_t ldd, int C, const float* s_ext, const Tables& tb,
+                      void* out, int transpose_out, cudaStream_t st);
+
+// --------------------------------------------------------------- tcgen05 (bf16 / f16)
+struct TcMaps {
+  CUtensorMap p;   // [T, Kred] box (64, 128)
+  CUtensorMap q;   // K-major: [Nout, Kred] box (64, 256);  MN-major: [Kred, Nout] box (64, 64)
+  CUtensorMap s;   // S_ext [n_st*128, r_pad] box (r_pad, 128)
+  CUtensorMap l;   // L [n_slots*Nout, r_pad] box (r_pad, 256)
+};
+
+cudaError_t tc_shrink(int dtype, const CUtensorMap& p_map, const CUtensorMap& a_map, int Kred, const Tables& tb,
+                      void* s_ext, int num_sms, cudaStream_t st);
+cudaError_t tc_gemm(int dtype, bool q_mn_major, const TcMaps& maps, int T, int Nout, int Kred, bool lora,
+                    const Tables& tb, void* out, int64_t ldo, int num_sms, cudaStream_t st);
+cudaError_t tc_gram(int dtype, const CUtensorMap& d_map, const CUtensorMap& s_map, int C, const Tables& tb,
+                    void* out, int transpose_out, int num_sms, cudaStream_t st);
+
+// --------------------------------------------------------------- packing
+cudaError_t pack_adapters(int src_dtype, int dst_dtype, const uint64_t* src_ptrs, const int32_t* ranks,
+                          int n_slots, int rank_dim, int other_dim, int transpose, int d0, int d1, void* dst,
+                          cudaStream_t st);
+
+}  // namespace lf

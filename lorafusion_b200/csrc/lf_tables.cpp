@@ -1,0 +1,169 @@
+// Host-side routing tables: routes (contiguous row ranges -> adapter slot) are cut
+// along the fixed 128-row tile grid of the fused batch into "segment tiles"
+// (route x tile).  Every kernel walks these tables; no kernel needs per-row lookups.
+//
+// Follows the route semantics of lorafusion/ops/config.py:29-69 (TileRoute,
+// TileRoutingConfig.validate) and the per-route work of lorafusion/ops/mock_ops.py:40-46,71-93.
+#include <algorithm>
+#include <cstring>
+#include <numeric>
+#include <vector>
+
+#include "../../include/lorafusion_b200.h"
+
+namespace {
+
+int pad_rank(int r) {
+  if (r <= 16) return 16;
+  if (r <= 32) return 32;
+  if (r <= 64) return 64;
+  return -1;
+}
+
+}  // namespace
+
+extern "C" int32_t lf_plan_table_words(int32_t n_routes, int32_t total_rows, int32_t n_slots) {
+  if (n_routes < 0 || total_rows < 0 || n_slots < 0) return -1;
+  const int64_t n_tiles = (static_cast<int64_t>(total_rows) + LF_TILE_ROWS - 1) / LF_TILE_ROWS;
+  // every route adds at most (tiles it spans) segment tiles; sum <= n_routes + n_tiles
+  const int64_t n_st = static_cast<int64_t>(n_routes) + n_tiles;
+  const int64_t words = (n_tiles + 1) + 6 * n_st + (n_slots + 1) + n_st + n_slots + (n_slots + 1) + n_slots +
+                        3 * n_st + 16;
+  return words > 0x7fffffff ? -1 : static_cast<int32_t>(words);
+}
+
+extern "C" int lf_plan_tables(const int32_t* route_start, const int32_t* route_end, const int32_t* route_slot,
+                              int32_t n_routes, int32_t total_rows, const int32_t* slot_rank,
+                              const float* slot_scale, int32_t n_slots, int32_t* table, int32_t table_capacity,
+                              lf_plan_info* info) {
+  if (!info || !table || n_routes < 0 || total_rows < 0 || n_slots < 0) return LF_ERR_INVALID_ARG;
+  if (n_routes > 0 && (!route_start || !route_end || !route_slot)) return LF_ERR_INVALID_ARG;
+  if (n_slots > 0 && (!slot_rank || !slot_scale)) return LF_ERR_INVALID_ARG;
+  std::memset(info, 0, sizeof(*info));
+
+  // validation: same checks as TileRoutingConfig.validate, plus slot range
+  int64_t expect = 0;
+  for (int32_t i = 0; i < n_routes; ++i) {
+    if (route_start[i] != expect) return LF_ERR_ROUTING;
+    if (route_end[i] < route_start[i]) return LF_ERR_ROUTING;
+    if (route_slot[i] < 0 || route_slot[i] >= n_slots) return LF_ERR_ROUTING;
+    expect = route_end[i];
+  }
+  if (expect != total_rows) return LF_ERR_ROUTING;
+
+  int max_rank = 1;
+  for (int32_t s = 0; s < n_slots; ++s) {
+    if (slot_rank[s] <= 0) return LF_ERR_INVALID_ARG;
+    max_rank = std::max(max_rank, static_cast<int>(slot_rank[s]));
+  }
+  const int r_pad = pad_rank(max_rank);
+  if (r_pad < 0) return LF_ERR_UNSUPPORTED;
+
+  const int32_t n_tiles = (total_rows + LF_TILE_ROWS - 1) / LF_TILE_ROWS;
+
+  // segment tiles in route order == row order
+  std::vector<int32_t> st_tile, st_lo, st_hi, st_slot, st_route;
+  std::vector<int32_t> tile_first(n_tiles + 1, 0);
+  for (int32_t i = 0; i < n_routes; ++i) {
+    int32_t r0 = route_start[i], r1 = route_end[i];
+    while (r0 < r1) {
+      const int32_t t = r0 / LF_TILE_ROWS;
+      const int32_t tile_end = std::min<int64_t>(static_cast<int64_t>(t + 1) * LF_TILE_ROWS, r1);
+      st_tile.push_back(t);
+      st_lo.push_back(r0 - t * LF_TILE_ROWS);
+      st_hi.push_back(tile_end - t * LF_TILE_ROWS);
+      st_slot.push_back(route_slot[i]);
+      st_route.push_back(i);
+      r0 = tile_end;
+    }
+  }
+  const int32_t n_st = static_cast<int32_t>(st_tile.size());
+  for (int32_t j = 0; j < n_st; ++j) tile_first[st_tile[j] + 1]++;
+  for (int32_t t = 0; t < n_tiles; ++t) tile_first[t + 1] += tile_first[t];
+
+  // per-slot lists (route order)
+  std::vector<int32_t> slot_first(n_slots + 1, 0), slot_list(n_st);
+  for (int32_t j = 0; j < n_st; ++j) slot_first[st_slot[j] + 1]++;
+  for (int32_t s = 0; s < n_slots; ++s) slot_first[s + 1] += slot_first[s];
+  {
+    std::vector<int32_t> fill(slot_first.begin(), slot_first.end() - 1);
+    for (int32_t j = 0; j < n_st; ++j) slot_list[fill[st_slot[j]]++] = j;
+  }
+  std::vector<int32_t> rank_prefix(n_slots + 1, 0);
+  for (int32_t s = 0; s < n_slots; ++s) rank_prefix[s + 1] = rank_prefix[s] + slot_rank[s];
+  std::vector<int32_t> order(n_slots);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) {
+    return (slot_first[a + 1] - slot_first[a]) > (slot_first[b + 1] - slot_first[b]);
+  });
+
+  // shrink units: runs of consecutive segment tiles of one row tile, N = run * r_pad <= 128
+  const int32_t group = std::max(1, 128 / r_pad);
+  std::vector<int32_t> u_tile, u_st0, u_nst;
+  for (int32_t t = 0; t < n_tiles; ++t) {
+    for (int32_t j = tile_first[t]; j < tile_first[t + 1]; j += group) {
+      u_tile.push_back(t);
+      u_st0.push_back(j);
+      u_nst.push_back(std::min(group, tile_first[t + 1] - j));
+    }
+  }
+  const int32_t n_units = static_cast<int32_t>(u_tile.size());
+
+  // lay out the sections
+  int32_t w = 0;
+  auto take = [&](int32_t n) {
+    const int32_t o = w;
+    w += n;
+    return o;
+  };
+  info->off_tile_st = take(n_tiles + 1);
+  info->off_st_tile = take(n_st);
+  info->off_st_lo = take(n_st);
+  info->off_st_hi = take(n_st);
+  info->off_st_slot = take(n_st);
+  info->off_st_route = take(n_st);
+  info->off_st_scale = take(n_st);
+  info->off_slot_st = take(n_slots + 1);
+  info->off_slot_list = take(n_st);
+  info->off_slot_rank = take(n_slots);
+  info->off_rank_prefix = take(n_slots + 1);
+  info->off_slot_order = take(n_slots);
+  info->off_unit_tile = take(n_units);
+  info->off_unit_st0 = take(n_units);
+  info->off_unit_nst = take(n_units);
+  if (w > table_capacity) return LF_ERR_CAPACITY;
+
+  auto put = [&](int32_t off, const std::vector<int32_t>& v) {
+    if (!v.empty()) std::memcpy(table + off, v.data(), v.size() * sizeof(int32_t));
+  };
+  put(info->off_tile_st, tile_first);
+  put(info->off_st_tile, st_tile);
+  put(info->off_st_lo, st_lo);
+  put(info->off_st_hi, st_hi);
+  put(info->off_st_slot, st_slot);
+  put(info->off_st_route, st_route);
+  for (int32_t j = 0; j < n_st; ++j) {
+    const float s = slot_scale[st_slot[j]];
+    std::memcpy(table + info->off_st_scale + j, &s, sizeof(float));
+  }
+  put(info->off_slot_st, slot_first);
+  put(info->off_slot_list, slot_list);
+  if (n_slots) std::memcpy(table + info->off_slot_rank, slot_rank, n_slots * sizeof(int32_t));
+  put(info->off_rank_prefix, rank_prefix);
+  put(info->off_slot_order, order);
+  put(info->off_unit_tile, u_tile);
+  put(info->off_unit_st0, u_st0);
+  put(info->off_unit_nst, u_nst);
+
+  info->total_rows = total_rows;
+  info->n_routes = n_routes;
+  info->n_slots = n_slots;
+  info->n_tiles = n_tiles;
+  info->n_segtiles = n_st;
+  info->r_pad = r_pad;
+  info->max_rank = max_rank;
+  info->rank_total = rank_prefix[n_slots];
+  info->n_shrink_units = n_units;
+  info->table_words = w;
+  return LF_OK;
+}

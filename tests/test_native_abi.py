@@ -1,0 +1,149 @@
+"""The C-ABI library loads on a CPU-only host, exports every entry point the
+header declares, and its host-side table builder is bit-exact (no GPU needed)."""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from lorafusion_b200 import _native as nat
+
+
+def _tables(routes, total_rows, ranks, scales):
+    L = nat.lib()
+    starts = np.array([r[0] for r in routes], dtype=np.int32)
+    ends = np.array([r[1] for r in routes], dtype=np.int32)
+    slots = np.array([r[2] for r in routes], dtype=np.int32)
+    rk = np.array(ranks, dtype=np.int32)
+    sc = np.array(scales, dtype=np.float32)
+    cap = L.lf_plan_table_words(len(routes), total_rows, len(ranks))
+    table = np.zeros(max(cap, 1), dtype=np.int32)
+    info = nat.PlanInfo()
+    i32p = ctypes.POINTER(ctypes.c_int32)
+    rc = L.lf_plan_tables(starts.ctypes.data_as(i32p), ends.ctypes.data_as(i32p), slots.ctypes.data_as(i32p),
+                          len(routes), total_rows, rk.ctypes.data_as(i32p),
+                          sc.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), len(ranks),
+                          table.ctypes.data_as(i32p), cap, ctypes.byref(info))
+    return rc, info, table
+
+
+def _sec(info, table, name, n):
+    off = getattr(info, "off_" + name)
+    return table[off:off + n]
+
+
+def test_library_loads_and_exports_header_symbols():
+    L = nat.lib()
+    declared = nat.header_symbols()
+    assert len(declared) >= 10
+    for name in declared:
+        assert hasattr(L, name), f"{name} declared in include/lorafusion_b200.h but not exported"
+    assert L.lf_version().decode().startswith("lorafusion_b200")
+    assert nat.status_text(nat.LF_ERR_ROUTING).startswith("routes")
+
+
+def test_plan_info_struct_matches_header():
+    text = open(nat.HEADER_PATH).read()
+    body = text.split("typedef struct lf_plan_info {")[1].split("} lf_plan_info;")[0]
+    names = [ln.split(";")[0].split()[-1] for ln in body.splitlines() if ln.strip().startswith("int32_t")]
+    assert names == [f[0] for f in nat.PlanInfo._fields_]
+    body = text.split("typedef struct lf_problem {")[1].split("} lf_problem;")[0]
+    fields = []
+    for ln in body.splitlines():
+        ln = ln.split("/*")[0].strip()
+        if not ln:
+            continue
+        decl = ln.rstrip(";")
+        for part in decl.split(","):
+            fields.append(part.strip().split()[-1].lstrip("*"))
+    assert fields == [f[0] for f in nat.Problem._fields_]
+
+
+def _reconstruct(info, table):
+    n_st = info.n_segtiles
+    tile = _sec(info, table, "st_tile", n_st)
+    lo = _sec(info, table, "st_lo", n_st)
+    hi = _sec(info, table, "st_hi", n_st)
+    slot = _sec(info, table, "st_slot", n_st)
+    route = _sec(info, table, "st_route", n_st)
+    out = {}
+    for j in range(n_st):
+        r0 = int(tile[j]) * nat.TILE_ROWS + int(lo[j])
+        r1 = int(tile[j]) * nat.TILE_ROWS + int(hi[j])
+        cur = out.setdefault(int(route[j]), [r0, r1, int(slot[j])])
+        assert cur[2] == slot[j]
+        if cur[1] < r1:
+            assert cur[1] == r0
+            cur[1] = r1
+        if cur[0] > r0:
+            cur[0] = r0
+    return out
+
+
+def test_tables_round_trip_reference_routes(layout_golden):
+    """Every golden route layout survives the tile cut bit-exactly."""
+    z = layout_golden
+    for name in [str(n) for n in z["names"]]:
+        routes = [tuple(int(v) for v in r) for r in z[f"{name}/routes"]]
+        T = routes[-1][1] if routes else 0
+        slot_of = {}
+        sroutes = [(s, e, slot_of.setdefault(a, len(slot_of))) for s, e, a in routes]
+        rc, info, table = _tables(sroutes, T, [16] * len(slot_of), [2.0] * len(slot_of))
+        assert rc == 0, name
+        rec = _reconstruct(info, table)
+        nonempty = [(i, r) for i, r in enumerate(sroutes) if r[1] > r[0]]
+        assert sorted(rec) == [i for i, _ in nonempty]
+        for i, r in nonempty:
+            assert tuple(rec[i]) == r, (name, i)
+        # CSR over tiles covers every segment tile once, in row order
+        tile_st = _sec(info, table, "tile_st", info.n_tiles + 1)
+        assert tile_st[0] == 0 and tile_st[-1] == info.n_segtiles and np.all(np.diff(tile_st) >= 0)
+        # per-slot lists are in route order and partition the segment tiles
+        slot_st = _sec(info, table, "slot_st", info.n_slots + 1)
+        lst = _sec(info, table, "slot_list", info.n_segtiles)
+        assert sorted(lst.tolist()) == list(range(info.n_segtiles))
+        for s in range(info.n_slots):
+            part = lst[slot_st[s]:slot_st[s + 1]]
+            assert np.all(np.diff(part) > 0)
+        # shrink units cover each tile's segment tiles in runs of <= 128 / r_pad
+        nst = _sec(info, table, "unit_nst", info.n_shrink_units)
+        assert nst.sum() == info.n_segtiles and nst.max(initial=1) <= 128 // info.r_pad
+
+
+def test_tables_errors_and_padding():
+    assert _tables([(0, 10, 0), (12, 20, 0)], 20, [8], [2.0])[0] == nat.LF_ERR_ROUTING
+    assert _tables([(0, 10, 0)], 20, [8], [2.0])[0] == nat.LF_ERR_ROUTING
+    assert _tables([(0, 10, 1)], 10, [8], [2.0])[0] == nat.LF_ERR_ROUTING
+    assert _tables([(0, 10, 0)], 10, [65], [2.0])[0] == nat.LF_ERR_UNSUPPORTED
+    for r, pad in [(1, 16), (16, 16), (17, 32), (32, 32), (33, 64), (64, 64)]:
+        rc, info, _ = _tables([(0, 300, 0)], 300, [r], [1.0])
+        assert rc == 0 and info.r_pad == pad and info.rank_total == r
+    rc, info, _ = _tables([], 0, [], [])
+    assert rc == 0 and info.n_segtiles == 0 and info.n_tiles == 0
+    rc, info, table = _tables([(0, 0, 0), (0, 5, 1)], 5, [4, 8], [2.0, 1.0])
+    assert rc == 0 and info.n_slots == 2 and info.n_segtiles == 1
+    slot_st = _sec(info, table, "slot_st", 3)
+    assert slot_st.tolist() == [0, 0, 1]
+
+
+def test_workspace_sizes():
+    rc, info, _ = _tables([(0, 1000, 0), (1000, 1300, 1)], 1300, [16, 64], [2.0, 2.0])
+    assert rc == 0
+    L = nat.lib()
+    fw = L.lf_forward_workspace_bytes(ctypes.byref(info), nat.LF_BF16)
+    bw = L.lf_backward_workspace_bytes(ctypes.byref(info), nat.LF_BF16)
+    assert fw >= info.n_segtiles * 128 * info.r_pad * 4 and fw % 256 == 0
+    assert bw == 2 * fw
+
+
+def test_ops_raise_without_gpu_inputs():
+    import torch
+    from lorafusion_b200 import b200_ops
+    from lorafusion_b200.config import AdapterSpec, TileRoute, TileRoutingConfig
+    x = torch.zeros(4, 8)
+    rt = TileRoutingConfig(16, [TileRoute(0, 4, 0)])
+    ad = {0: AdapterSpec(0, 2, 4.0, 8, 8)}
+    with pytest.raises(ValueError, match="CUDA"):
+        b200_ops.fused_lora_forward(x, torch.zeros(8, 8), {0: torch.zeros(2, 8)}, {0: torch.zeros(8, 2)}, ad, rt)
+    with pytest.raises(ValueError, match="covers"):
+        b200_ops.fused_lora_forward(torch.zeros(5, 8), torch.zeros(8, 8), {}, {}, ad, rt)

@@ -1,0 +1,233 @@
+"""GPU parity of the B200 op against the CPU oracle and the reference's golden outputs.
+
+Tolerances (elementwise, ``|got-ref| <= rtol*|ref| + atol*max(1, max|ref|)``):
+  bf16 / f16 inputs: rtol = atol = 2e-2 against the oracle run in float32 on the
+                     same (already bf16/f16-representable) values;
+  float32 inputs:    rtol = atol = 1e-5.
+Routing tables are checked bit-exactly on the CPU (tests/test_native_abi.py).
+"""
+
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import op_case
+from oracle import mock_oracle
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = dict(rtol=2e-2, atol=2e-2)
+FP32_TOL = dict(rtol=1e-5, atol=1e-5)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _require_gpu():
+    if not torch.cuda.is_available():
+        pytest.fail("GPU tests need a CUDA device")
+    from lorafusion_b200 import _native
+    _native.lib()
+    yield
+    assert _native.device_error() == 0, "a kernel reported a bounded-wait timeout"
+
+
+def _ops():
+    from lorafusion_b200 import b200_ops
+    return b200_ops
+
+
+def _cfg():
+    from lorafusion_b200.config import AdapterSpec, TileRoute, TileRoutingConfig
+    return AdapterSpec, TileRoute, TileRoutingConfig
+
+
+def _to_torch(case, dtype, dev="cuda"):
+    AdapterSpec, TileRoute, TileRoutingConfig = _cfg()
+    K = case["x"].shape[1]
+    N = case["w"].shape[0]
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device=dev, dtype=dtype)  # noqa: E731
+    ad = {i: AdapterSpec(i, case["ranks"][i], case["alphas"][i], K, N) for i in case["a"]}
+    routing = TileRoutingConfig(16, [TileRoute(s, e, a) for s, e, a in case["routes"]])
+    return (t(case["x"]), t(case["w"]), {i: t(v) for i, v in case["a"].items()},
+            {i: t(v) for i, v in case["b"].items()}, ad, routing, t(case["g"]))
+
+
+def _check(got, ref, tol, what):
+    ok, msg = mock_oracle.allclose_report(got.float().cpu().numpy(), ref, **tol)
+    assert ok, f"{what}: {msg}"
+
+
+def _run_and_compare(case, dtype, tol, backward=True):
+    ops = _ops()
+    x, w, a, b, ad, routing, g = _to_torch(case, dtype)
+    y = ops.fused_lora_forward(x, w, a, b, ad, routing)
+    assert y.dtype == dtype and y.shape == (x.shape[0], w.shape[0])
+    _check(y, case["y"], tol, "forward")
+    if not backward:
+        return
+    gx, ga, gb = ops.fused_lora_backward(g, x, w, a, b, ad, routing)
+    _check(gx, case["gx"], tol, "grad_x")
+    assert list(ga.keys()) == case["grad_keys"] and list(gb.keys()) == case["grad_keys"]
+    for k in case["grad_keys"]:
+        assert ga[k].shape == case["ga"][k].shape and ga[k].is_contiguous()
+        assert gb[k].shape == case["gb"][k].shape and gb[k].is_contiguous()
+        _check(ga[k], case["ga"][k], tol, f"grad_a[{k}]")
+        _check(gb[k], case["gb"][k], tol, f"grad_b[{k}]")
+
+
+@pytest.mark.parametrize("name", ["cfg1", "single_route", "split_adapter", "rank1_one_row_routes", "unused_adapter"])
+def test_fp32_matches_reference_golden(ops_golden, name):
+    _run_and_compare(op_case(ops_golden, name), torch.float32, FP32_TOL)
+
+
+def test_bf16_matches_reference_golden(ops_golden):
+    _run_and_compare(op_case(ops_golden, "bf16_mixed_ranks"), torch.bfloat16, BF16_TOL)
+
+
+def _random_case(seed, T, K, N, routes, ranks, dtype):
+    rng = np.random.default_rng(seed)
+    rnd = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
+    rounder = mock_oracle.bf16_round if dtype == torch.bfloat16 else (
+        (lambda v: v.astype(np.float16).astype(np.float32)) if dtype == torch.float16 else (lambda v: v))
+    case = {"x": rounder(rnd(T, K)), "w": rounder(rnd(N, K) / np.sqrt(K)), "g": rounder(rnd(T, N))}
+    case["a"] = {i: rounder(rnd(r, K) / np.sqrt(K)) for i, r in ranks.items()}
+    case["b"] = {i: rounder(0.02 * rnd(N, r)) for i, r in ranks.items()}
+    case["ranks"] = dict(ranks)
+    case["alphas"] = {i: float(2 * r) for i, r in ranks.items()}
+    case["routes"] = routes
+    sc = {i: case["alphas"][i] / ranks[i] for i in ranks}
+    case["y"] = mock_oracle.fused_lora_forward(case["x"], case["w"], case["a"], case["b"], sc, routes)
+    gx, ga, gb = mock_oracle.fused_lora_backward(case["g"], case["x"], case["w"], case["a"], case["b"], sc, routes)
+    case.update(gx=gx, ga=ga, gb=gb, grad_keys=list(ga.keys()))
+    return case
+
+
+def _routes_from_sizes(sizes, adapters):
+    out, cur = [], 0
+    for n, a in zip(sizes, adapters):
+        out.append((cur, cur + n, a))
+        cur += n
+    return out
+
+
+SHAPES = [
+    # (T, K, N, route sizes, route adapters, ranks)
+    ("aligned_r16", 512, 256, 512, [128, 128, 256], [0, 1, 2], {0: 16, 1: 16, 2: 16}),
+    ("misaligned_r16", 700, 512, 768, [300, 5, 1, 94, 200, 100], [0, 1, 2, 3, 0, 1], {0: 16, 1: 16, 2: 16, 3: 16}),
+    ("rank8_pad", 300, 256, 256, [100, 200], [0, 1], {0: 8, 1: 8}),
+    ("rank32", 384, 256, 512, [150, 234], [1, 0], {0: 32, 1: 32}),
+    ("rank64", 384, 512, 256, [64, 64, 256], [0, 1, 2], {0: 64, 1: 64, 2: 64}),
+    ("mixed_ranks", 640, 384, 384, [200, 37, 3, 150, 250], [0, 1, 2, 3, 1], {0: 8, 1: 16, 2: 32, 3: 64}),
+    ("ragged_k_n", 333, 200, 264, [111, 222], [0, 1], {0: 16, 1: 16}),
+    ("many_small", 256, 256, 256, [4] * 64, list(range(64)), {i: 16 for i in range(64)}),
+    ("tiny", 3, 64, 64, [1, 2], [0, 1], {0: 4, 1: 16}),
+    ("n_small", 130, 64, 8, [65, 65], [0, 1], {0: 16, 1: 16}),
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=[s[0] for s in SHAPES])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32], ids=["bf16", "f16", "f32"])
+def test_random_shapes_match_oracle(shape, dtype):
+    _, T, K, N, sizes, adapters, ranks = shape
+    routes = _routes_from_sizes(sizes, adapters)
+    case = _random_case(zlib.crc32(shape[0].encode()) % 1000, T, K, N, routes, ranks, dtype)
+    _run_and_compare(case, dtype, FP32_TOL if dtype == torch.float32 else BF16_TOL)
+
+
+def test_cfg2_layout_reduced_width_matches_oracle():
+    """The benchmark's routing (cfg2: 4096 tokens, 16 adapters, Zipf 1.1, 128-row bins) at K = N = 512."""
+    from lorafusion_b200.workloads import WORKLOADS, layout
+    from lorafusion_b200.scheduler import build_microbatch
+    wl = WORKLOADS["cfg2_h4096_a16_r16"]
+    reqs, packing = layout(wl)
+    tensors = {r.request_id: torch.zeros(r.num_rows, 1) for r in reqs}
+    _, routing, _ = build_microbatch(reqs, tensors, packing)
+    routes = [(r.row_start, r.row_end, r.adapter_id) for r in routing.routes]
+    case = _random_case(7, 4096, 512, 512, routes, {i: 16 for i in range(16)}, torch.bfloat16)
+    _run_and_compare(case, torch.bfloat16, BF16_TOL)
+
+
+def test_full_size_cfg2_against_torch_fp32():
+    """cfg2 at full size (4096 x 4096 x 4096): forward and backward against a torch fp32
+    reference of the same math computed on the GPU."""
+    from lorafusion_b200.workloads import WORKLOADS, make_problem
+    ops = _ops()
+    pr = make_problem(WORKLOADS["cfg2_h4096_a16_r16"], device="cuda", with_grad=True)
+    y = ops.fused_lora_forward(pr.x, pr.base_weight, pr.lora_a, pr.lora_b, pr.adapters, pr.routing)
+    gx, ga, gb = ops.fused_lora_backward(pr.grad_out, pr.x, pr.base_weight, pr.lora_a, pr.lora_b, pr.adapters,
+                                         pr.routing)
+    x, w, g = pr.x.float(), pr.base_weight.float(), pr.grad_out.float()
+    ref_y = x @ w.t()
+    ref_gx = g @ w
+    ref_ga, ref_gb = {}, {}
+    for r in pr.routing.routes:
+        s = pr.adapters[r.adapter_id].scaling
+        a, b = pr.lora_a[r.adapter_id].float(), pr.lora_b[r.adapter_id].float()
+        xs, gs = x[r.row_start:r.row_end], g[r.row_start:r.row_end]
+        xa = xs @ a.t()
+        ref_y[r.row_start:r.row_end] += s * (xa @ b.t())
+        gxa = s * (gs @ b)
+        ref_gx[r.row_start:r.row_end] += gxa @ a
+        ref_ga[r.adapter_id] = ref_ga.get(r.adapter_id, 0) + gxa.t() @ xs
+        ref_gb[r.adapter_id] = ref_gb.get(r.adapter_id, 0) + s * (gs.t() @ xa)
+    _check(y, ref_y.cpu().numpy(), BF16_TOL, "forward")
+    _check(gx, ref_gx.cpu().numpy(), BF16_TOL, "grad_x")
+    for k in ref_ga:
+        _check(ga[k], ref_ga[k].cpu().numpy(), BF16_TOL, f"grad_a[{k}]")
+        _check(gb[k], ref_gb[k].cpu().numpy(), BF16_TOL, f"grad_b[{k}]")
+    # base part alone: zero B gives exactly the base GEMM, compare with cuBLAS bf16
+    zero_b = {k: torch.zeros_like(v) for k, v in pr.lora_b.items()}
+    y0 = ops.fused_lora_forward(pr.x, pr.base_weight, pr.lora_a, zero_b, pr.adapters, pr.routing)
+    _check(y0, (pr.x @ pr.base_weight.t()).float().cpu().numpy(), BF16_TOL, "base GEMM vs cuBLAS")
+
+
+def test_deterministic_and_repeatable():
+    ops = _ops()
+    routes = _routes_from_sizes([300, 5, 400, 319], [0, 1, 2, 0])
+    case = _random_case(3, 1024, 512, 512, routes, {0: 16, 1: 32, 2: 64}, torch.bfloat16)
+    x, w, a, b, ad, routing, g = _to_torch(case, torch.bfloat16)
+    y1 = ops.fused_lora_forward(x, w, a, b, ad, routing)
+    y2 = ops.fused_lora_forward(x, w, a, b, ad, routing)
+    assert torch.equal(y1, y2)
+    r1 = ops.fused_lora_backward(g, x, w, a, b, ad, routing)
+    r2 = ops.fused_lora_backward(g, x, w, a, b, ad, routing)
+    assert torch.equal(r1[0], r2[0])
+    for k in r1[1]:
+        assert torch.equal(r1[1][k], r2[1][k]) and torch.equal(r1[2][k], r2[2][k])
+
+
+def test_edge_cases():
+    ops = _ops()
+    AdapterSpec, TileRoute, TileRoutingConfig = _cfg()
+    dev = "cuda"
+    # empty batch
+    K, N = 64, 32
+    w = torch.randn(N, K, device=dev)
+    a = {0: torch.randn(4, K, device=dev)}
+    b = {0: torch.randn(N, 4, device=dev)}
+    ad = {0: AdapterSpec(0, 4, 8.0, K, N), 1: AdapterSpec(1, 4, 8.0, K, N)}
+    y = ops.fused_lora_forward(torch.empty(0, K, device=dev), w, a, b, ad, TileRoutingConfig(16, []))
+    assert y.shape == (0, N)
+    # a zero-length route still yields (zero) gradients for its adapter, like the reference
+    x = torch.randn(5, K, device=dev)
+    g = torch.randn(5, N, device=dev)
+    a[1] = torch.randn(4, K, device=dev)
+    b[1] = torch.randn(N, 4, device=dev)
+    rt = TileRoutingConfig(16, [TileRoute(0, 0, 1), TileRoute(0, 5, 0)])
+    gx, ga, gb = ops.fused_lora_backward(g, x, w, a, b, ad, rt)
+    assert list(ga) == [1, 0]
+    assert torch.count_nonzero(ga[1]) == 0 and torch.count_nonzero(gb[1]) == 0
+    # unknown adapter -> KeyError; bad routing -> ValueError
+    with pytest.raises(KeyError):
+        ops.fused_lora_forward(x, w, a, b, ad, TileRoutingConfig(16, [TileRoute(0, 5, 7)]))
+    with pytest.raises(ValueError):
+        ops.fused_lora_forward(x, w, a, b, ad, TileRoutingConfig(16, [TileRoute(0, 4, 0)]))
+    # non-contiguous activations and an fp32 base weight with bf16 activations
+    xb = torch.randn(K, 40, device=dev, dtype=torch.bfloat16).t()
+    ab = {0: a[0].bfloat16(), 1: a[1].bfloat16()}
+    bb = {0: b[0].bfloat16(), 1: b[1].bfloat16()}
+    rt2 = TileRoutingConfig(16, [TileRoute(0, 40, 0)])
+    y = ops.fused_lora_forward(xb, w, ab, bb, ad, rt2)
+    ref = xb.float() @ w.bfloat16().float().t() + 2.0 * (xb.float() @ ab[0].float().t()) @ bb[0].float().t()
+    _check(y, ref.cpu().numpy(), BF16_TOL, "non-contiguous x")
