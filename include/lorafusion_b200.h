@@ -64,7 +64,7 @@ typedef struct lf_plan_info {
   int32_t r_pad;           /* padded rank shared by every slot: 16, 32 or 64 */
   int32_t max_rank;
   int32_t rank_total;      /* sum of slot ranks: rows of the concatenated grad_a blocks */
-  int32_t n_shrink_units;  /* (tile, run of segment tiles) work units of the shrink */
+  int32_t n_shrink_units;  /* (tile, run of <= 64/r_pad segment tiles) work units of the shrink */
   int32_t table_words;     /* int32 words of the table in use */
   /* section offsets */
   int32_t off_tile_st;     /* [n_tiles+1]  CSR: segment tiles of each row tile */
@@ -82,6 +82,14 @@ typedef struct lf_plan_info {
   int32_t off_unit_tile;   /* [n_shrink_units] */
   int32_t off_unit_st0;    /* [n_shrink_units] */
   int32_t off_unit_nst;    /* [n_shrink_units] */
+  /* Row tiles taken two at a time (rows 256p .. 256p+255) by the CTA-pair GEMM: per pair, one
+   * LoRA stage per adapter slot present in either tile, holding each tile's segment tile of
+   * that slot or the all-zero segment tile n_segtiles (the workspace's last block). */
+  int32_t n_pair_lora;     /* LoRA stages over all pairs */
+  int32_t off_pair_lora;   /* [ceil(n_tiles/2)+1] CSR: stages of each pair */
+  int32_t off_pl_a;        /* [n_pair_lora] segment tile of the even row tile */
+  int32_t off_pl_b;        /* [n_pair_lora] segment tile of the odd row tile */
+  int32_t off_pl_slot;     /* [n_pair_lora] adapter slot */
 } lf_plan_info;
 
 /* Upper bound on the int32 words lf_plan_tables needs. */
@@ -145,12 +153,15 @@ LF_API int lf_forward(const lf_problem* prob, const lf_plan_info* info, const in
  *   LF_STAGE_SHRINK   routed shrink: workspace <- s_i x A_i^T, masked per segment tile
  *   LF_STAGE_EXPAND   fused base GEMM + LoRA expand into y (reads the shrink's workspace)
  *   LF_STAGE_BASE     base GEMM only, y = x W^T (the "LoRA disabled" yardstick)
+ *   LF_STAGE_SINGLE_CTA  with EXPAND or BASE: use 128x256 tiles on single CTAs instead of the
+ *                     default 256x256 tiles on CTA pairs (bf16/f16 only; for comparisons)
  * lf_forward == lf_forward_stages(..., LF_STAGE_SHRINK | LF_STAGE_EXPAND).
  * Has no counterpart in the reference (its forward is one call per route).
  */
 #define LF_STAGE_SHRINK 1
 #define LF_STAGE_EXPAND 2
 #define LF_STAGE_BASE 4
+#define LF_STAGE_SINGLE_CTA 8
 LF_API int lf_forward_stages(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, void* y_dev,
                              void* workspace_dev, size_t workspace_bytes, int32_t stages, lf_stream_t stream);
 

@@ -25,7 +25,7 @@ LF_ERR_CAPACITY = 5
 LF_ERR_DEVICE = 6
 
 LF_F32, LF_BF16, LF_F16 = 0, 1, 2
-LF_STAGE_SHRINK, LF_STAGE_EXPAND, LF_STAGE_BASE = 1, 2, 4
+LF_STAGE_SHRINK, LF_STAGE_EXPAND, LF_STAGE_BASE, LF_STAGE_SINGLE_CTA = 1, 2, 4, 8
 TILE_ROWS = 128
 
 _c_i32 = ctypes.c_int32
@@ -38,7 +38,8 @@ class PlanInfo(ctypes.Structure):
         "n_shrink_units", "table_words",
         "off_tile_st", "off_st_tile", "off_st_lo", "off_st_hi", "off_st_slot", "off_st_route", "off_st_scale",
         "off_slot_st", "off_slot_list", "off_slot_rank", "off_rank_prefix", "off_slot_order",
-        "off_unit_tile", "off_unit_st0", "off_unit_nst")]
+        "off_unit_tile", "off_unit_st0", "off_unit_nst",
+        "n_pair_lora", "off_pair_lora", "off_pl_a", "off_pl_b", "off_pl_slot")]
 
 
 class Problem(ctypes.Structure):

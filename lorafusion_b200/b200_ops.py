@@ -30,7 +30,8 @@ from lorafusion_b200 import _native as nat
 
 _DTYPE_CODE = {torch.float32: nat.LF_F32, torch.bfloat16: nat.LF_BF16, torch.float16: nat.LF_F16}
 
-__all__ = ["fused_lora_forward", "fused_lora_backward", "clear_weight_cache", "last_launch_count"]
+__all__ = ["fused_lora_forward", "fused_lora_backward", "prepare_forward", "PreparedForward", "clear_weight_cache",
+           "last_launch_count"]
 
 
 # --------------------------------------------------------------------------- caches
@@ -273,6 +274,48 @@ def fused_lora_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> tor
     nat.check(rc, "lf_forward")
     _last_launches = _LAUNCHES["forward"]
     return y
+
+
+class PreparedForward:
+    """A forward call with routing tables, adapter slabs and workspace resolved once.
+
+    ``launch(y, stages)`` enqueues the selected stages (``LF_STAGE_*`` bits of
+    ``lf_forward_stages``) on the current stream with no Python-side checks,
+    for callers that replay the same batch layout (benchmarks, CUDA graphs).
+    The caller keeps ``x`` and the weights alive and unchanged.
+    """
+
+    def __init__(self, x, base_weight, lora_a, lora_b, adapters, routing):
+        routing.validate(x.shape[0])
+        self.x = _activation(x, "x")
+        self.device = self.x.device
+        self.T, self.K = self.x.shape
+        self.N = base_weight.shape[0]
+        dtype = self.x.dtype
+        self.dtype = dtype
+        self.w = _weight(base_weight, dtype, self.device)
+        self.plan = _plan(routing, self.T, adapters, lora_a, self.device)
+        self.packs = _pack(self.plan, lora_a, lora_b, dtype, self.K, self.N, self.device, backward=False)
+        code = _DTYPE_CODE[dtype]
+        L = nat.lib()
+        ws_bytes = L.lf_forward_workspace_bytes(ctypes.byref(self.plan.info), code)
+        self.ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=self.device)
+        self.prob = _problem(code, self.T, self.K, self.N, self.x, self.w, self.packs)
+
+    def new_output(self) -> torch.Tensor:
+        return torch.empty((self.T, self.N), dtype=self.dtype, device=self.device)
+
+    def launch(self, y: torch.Tensor, stages: int = nat.LF_STAGE_SHRINK | nat.LF_STAGE_EXPAND) -> None:
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        rc = nat.lib().lf_forward_stages(ctypes.byref(self.prob), ctypes.byref(self.plan.info),
+                                         self.plan.table_dev.data_ptr(), y.data_ptr(), self.ws.data_ptr(),
+                                         self.ws.numel(), stages, stream)
+        nat.check(rc, "lf_forward_stages")
+
+
+def prepare_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> PreparedForward:
+    """Resolve a forward call once (see :class:`PreparedForward`)."""
+    return PreparedForward(x, base_weight, lora_a, lora_b, adapters, routing)
 
 
 def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, routing):

@@ -79,8 +79,9 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int to_status(cudaError_t e) { return e == cudaSuccess ? LF_OK : LF_ERR_CUDA; }
 
+// segment tiles plus one all-zero block (index n_segtiles) the pair GEMM pads with
 size_t segtile_elems(const lf_plan_info* info) {
-  return static_cast<size_t>(info->n_segtiles) * LF_TILE_ROWS * static_cast<size_t>(info->r_pad);
+  return static_cast<size_t>(info->n_segtiles + 1) * LF_TILE_ROWS * static_cast<size_t>(info->r_pad);
 }
 
 // one S_ext buffer, sized for f32 so the CUDA-core path can use it too, 256-byte multiple
@@ -123,6 +124,10 @@ Tables make_tables(const lf_plan_info* info, const int32_t* table_dev) {
   t.off_unit_tile = info->off_unit_tile;
   t.off_unit_st0 = info->off_unit_st0;
   t.off_unit_nst = info->off_unit_nst;
+  t.off_pair_lora = info->off_pair_lora;
+  t.off_pl_a = info->off_pl_a;
+  t.off_pl_b = info->off_pl_b;
+  t.off_pl_slot = info->off_pl_slot;
   t.n_tiles = info->n_tiles;
   t.n_segtiles = info->n_segtiles;
   t.n_slots = info->n_slots;
@@ -162,7 +167,7 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
                                  lf_stream_t stream) {
   int rc = check_problem(prob, info, table_dev);
   if (rc != LF_OK) return rc;
-  if (stages <= 0 || stages > 7 || ((stages & LF_STAGE_EXPAND) && (stages & LF_STAGE_BASE))) return LF_ERR_INVALID_ARG;
+  if (stages <= 0 || stages > 15 || ((stages & LF_STAGE_EXPAND) && (stages & LF_STAGE_BASE))) return LF_ERR_INVALID_ARG;
   const int T = prob->T, K = prob->K, N = prob->N;
   if (T == 0 || N == 0) return LF_OK;
   if (!prob->x_dev || !prob->w_dev || !prob->a_pack_dev || !prob->b_pack_dev || !y_dev) return LF_ERR_INVALID_ARG;
@@ -180,25 +185,29 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
   const bool lora = (stages & LF_STAGE_EXPAND) != 0 && info->n_segtiles > 0;
 
   if (tc_eligible(prob, {prob->x_dev, prob->w_dev, prob->a_pack_dev, prob->b_pack_dev, y_dev, workspace_dev})) {
+    const bool single = (stages & LF_STAGE_SINGLE_CTA) != 0;
+    const uint32_t nbox = single ? 256 : 128;  // rows of W / B_i per CTA and tile
     TcMaps maps;
     CUtensorMap a_map;
     const size_t es = 2;
+    const uint64_t s_rows = static_cast<uint64_t>(info->n_segtiles + 1) * LF_TILE_ROWS;
     bool ok = make_map(&maps.p, dt, prob->x_dev, K, T, K * es, 64, 128) &&
-              make_map(&maps.q, dt, prob->w_dev, K, N, K * es, 64, 256) &&
+              make_map(&maps.q, dt, prob->w_dev, K, N, K * es, 64, nbox) &&
               make_map(&a_map, dt, prob->a_pack_dev, K, static_cast<uint64_t>(info->n_slots) * rp, K * es, 64, rp);
     if (info->n_segtiles > 0)
-      ok = ok &&
-           make_map(&maps.s, dt, workspace_dev, rp, static_cast<uint64_t>(info->n_segtiles) * LF_TILE_ROWS, rp * es,
-                    rp, 128) &&
-           make_map(&maps.l, dt, prob->b_pack_dev, rp, static_cast<uint64_t>(info->n_slots) * N, rp * es, rp, 256);
+      ok = ok && make_map(&maps.s, dt, workspace_dev, rp, s_rows, rp * es, rp, 128) &&
+           make_map(&maps.l, dt, prob->b_pack_dev, rp, static_cast<uint64_t>(info->n_slots) * N, rp * es, rp, nbox);
     else
       maps.s = maps.l = maps.p;
+    ok = ok && make_map(&maps.o, dt, y_dev, N, T, N * es, 64, 32);
     if (!ok) return LF_ERR_UNSUPPORTED;
     if (do_shrink) {
       e = tc_shrink(dt, maps.p, a_map, K, tb, workspace_dev, ds->num_sms, st);
       if (e != cudaSuccess) return LF_ERR_CUDA;
     }
-    if (do_gemm) e = tc_gemm(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st);
+    if (do_gemm)
+      e = single ? tc_gemm(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st)
+                 : tc_gemm_pair(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st);
     return to_status(e);
   }
 
@@ -262,9 +271,10 @@ extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, con
       ok = ok &&
            make_map(&a_map, dt, prob->a_pack_dev, K, static_cast<uint64_t>(info->n_slots) * rp, K * es, 64, rp) &&
            make_map(&bt_map, dt, prob->bt_pack_dev, N, static_cast<uint64_t>(info->n_slots) * rp, N * es, 64, rp) &&
-           make_map(&sf_map, dt, s_f, rp, static_cast<uint64_t>(info->n_segtiles) * LF_TILE_ROWS, rp * es, rp, 128) &&
-           make_map(&sb_map, dt, s_b, rp, static_cast<uint64_t>(info->n_segtiles) * LF_TILE_ROWS, rp * es, rp, 128) &&
-           make_map(&dx.l, dt, prob->at_pack_dev, rp, static_cast<uint64_t>(info->n_slots) * K, rp * es, rp, 256);
+           make_map(&sf_map, dt, s_f, rp, static_cast<uint64_t>(info->n_segtiles + 1) * LF_TILE_ROWS, rp * es, rp, 128) &&
+           make_map(&sb_map, dt, s_b, rp, static_cast<uint64_t>(info->n_segtiles + 1) * LF_TILE_ROWS, rp * es, rp, 128) &&
+           make_map(&dx.l, dt, prob->at_pack_dev, rp, static_cast<uint64_t>(info->n_slots) * K, rp * es, rp, 128);
+    ok = ok && make_map(&dx.o, dt, grad_x_dev, K, T, K * es, 64, 32);
     if (!ok) return LF_ERR_UNSUPPORTED;
     dx.p = p_g;
     if (lora) {
@@ -276,7 +286,7 @@ extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, con
     } else {
       dx.s = dx.l = p_g;
     }
-    e = tc_gemm(dt, true, dx, T, K, N, lora, tb, grad_x_dev, K, ds->num_sms, st);
+    e = tc_gemm_pair(dt, true, dx, T, K, N, lora, tb, grad_x_dev, K, ds->num_sms, st);
     if (e != cudaSuccess) return LF_ERR_CUDA;
     if (lora) {
       e = tc_gram(dt, p_g, sf_map, N, tb, grad_b_dev, 0, ds->num_sms, st);

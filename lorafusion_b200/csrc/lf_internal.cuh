@@ -15,6 +15,7 @@ struct Tables {
   int32_t off_tile_st, off_st_tile, off_st_lo, off_st_hi, off_st_slot, off_st_scale;
   int32_t off_slot_st, off_slot_list, off_slot_rank, off_rank_prefix, off_slot_order;
   int32_t off_unit_tile, off_unit_st0, off_unit_nst;
+  int32_t off_pair_lora, off_pl_a, off_pl_b, off_pl_slot;
   int32_t n_tiles, n_segtiles, n_slots, n_units, r_pad;
   int* err;  // device status word for bounded-wait timeouts
 
@@ -32,6 +33,10 @@ struct Tables {
   __device__ __forceinline__ int32_t unit_tile(int u) const { return base[off_unit_tile + u]; }
   __device__ __forceinline__ int32_t unit_st0(int u) const { return base[off_unit_st0 + u]; }
   __device__ __forceinline__ int32_t unit_nst(int u) const { return base[off_unit_nst + u]; }
+  __device__ __forceinline__ int32_t pair_lora(int p) const { return base[off_pair_lora + p]; }
+  __device__ __forceinline__ int32_t pl_a(int i) const { return base[off_pl_a + i]; }
+  __device__ __forceinline__ int32_t pl_b(int i) const { return base[off_pl_b + i]; }
+  __device__ __forceinline__ int32_t pl_slot(int i) const { return base[off_pl_slot + i]; }
 };
 
 Tables make_tables(const lf_plan_info* info, const int32_t* table_dev);
@@ -54,12 +59,17 @@ struct TcMaps {
   CUtensorMap q;   // K-major: [Nout, Kred] box (64, 256);  MN-major: [Kred, Nout] box (64, 64)
   CUtensorMap s;   // S_ext [n_st*128, r_pad] box (r_pad, 128)
   CUtensorMap l;   // L [n_slots*Nout, r_pad] box (r_pad, 256)
+  CUtensorMap o;   // output [T, Nout] box (64, 32), 128-byte swizzle (pair GEMM epilogue stores)
 };
 
 cudaError_t tc_shrink(int dtype, const CUtensorMap& p_map, const CUtensorMap& a_map, int Kred, const Tables& tb,
                       void* s_ext, int num_sms, cudaStream_t st);
 cudaError_t tc_gemm(int dtype, bool q_mn_major, const TcMaps& maps, int T, int Nout, int Kred, bool lora,
                     const Tables& tb, void* out, int64_t ldo, int num_sms, cudaStream_t st);
+// Same product with 256x256 tiles computed by CTA pairs (cta_group::2).  Maps: p box (64,128),
+// q K-major box (64,128) / MN-major box (64,64), s box (r_pad,128), l box (r_pad,128).
+cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, int Nout, int Kred, bool lora,
+                         const Tables& tb, void* out, int64_t ldo, int num_sms, cudaStream_t st);
 cudaError_t tc_gram(int dtype, const CUtensorMap& d_map, const CUtensorMap& s_map, int C, const Tables& tb,
                     void* out, int transpose_out, int num_sms, cudaStream_t st);
 

@@ -27,8 +27,9 @@ extern "C" int32_t lf_plan_table_words(int32_t n_routes, int32_t total_rows, int
   const int64_t n_tiles = (static_cast<int64_t>(total_rows) + LF_TILE_ROWS - 1) / LF_TILE_ROWS;
   // every route adds at most (tiles it spans) segment tiles; sum <= n_routes + n_tiles
   const int64_t n_st = static_cast<int64_t>(n_routes) + n_tiles;
+  const int64_t n_pairs = (n_tiles + 1) / 2;
   const int64_t words = (n_tiles + 1) + 6 * n_st + (n_slots + 1) + n_st + n_slots + (n_slots + 1) + n_slots +
-                        3 * n_st + 16;
+                        3 * n_st + (n_pairs + 1) + 3 * n_st + 16;
   return words > 0x7fffffff ? -1 : static_cast<int32_t>(words);
 }
 
@@ -97,8 +98,8 @@ extern "C" int lf_plan_tables(const int32_t* route_start, const int32_t* route_e
     return (slot_first[a + 1] - slot_first[a]) > (slot_first[b + 1] - slot_first[b]);
   });
 
-  // shrink units: runs of consecutive segment tiles of one row tile, N = run * r_pad <= 128
-  const int32_t group = std::max(1, 128 / r_pad);
+  // shrink units: runs of consecutive segment tiles of one row tile, N = run * r_pad <= 64
+  const int32_t group = std::max(1, 64 / r_pad);
   std::vector<int32_t> u_tile, u_st0, u_nst;
   for (int32_t t = 0; t < n_tiles; ++t) {
     for (int32_t j = tile_first[t]; j < tile_first[t + 1]; j += group) {
@@ -108,6 +109,36 @@ extern "C" int lf_plan_tables(const int32_t* route_start, const int32_t* route_e
     }
   }
   const int32_t n_units = static_cast<int32_t>(u_tile.size());
+
+  // pair LoRA stages: segment tiles of row tiles 2p and 2p+1 matched by slot, in row order
+  const int32_t n_pairs = (n_tiles + 1) / 2;
+  std::vector<int32_t> pair_first(n_pairs + 1, 0), pl_a, pl_b, pl_slot;
+  for (int32_t p = 0; p < n_pairs; ++p) {
+    const int32_t t0 = 2 * p, t1 = 2 * p + 1;
+    const int32_t a_b = tile_first[t0], a_e = tile_first[t0 + 1];
+    const int32_t b_b = t1 < n_tiles ? tile_first[t1] : 0, b_e = t1 < n_tiles ? tile_first[t1 + 1] : 0;
+    std::vector<char> used(static_cast<size_t>(std::max(0, b_e - b_b)), 0);
+    for (int32_t j = a_b; j < a_e; ++j) {
+      int32_t match = n_st;
+      for (int32_t k = b_b; k < b_e; ++k)
+        if (!used[k - b_b] && st_slot[k] == st_slot[j]) {
+          match = k;
+          used[k - b_b] = 1;
+          break;
+        }
+      pl_a.push_back(j);
+      pl_b.push_back(match);
+      pl_slot.push_back(st_slot[j]);
+    }
+    for (int32_t k = b_b; k < b_e; ++k)
+      if (!used[k - b_b]) {
+        pl_a.push_back(n_st);
+        pl_b.push_back(k);
+        pl_slot.push_back(st_slot[k]);
+      }
+    pair_first[p + 1] = static_cast<int32_t>(pl_a.size());
+  }
+  const int32_t n_pl = static_cast<int32_t>(pl_a.size());
 
   // lay out the sections
   int32_t w = 0;
@@ -131,6 +162,10 @@ extern "C" int lf_plan_tables(const int32_t* route_start, const int32_t* route_e
   info->off_unit_tile = take(n_units);
   info->off_unit_st0 = take(n_units);
   info->off_unit_nst = take(n_units);
+  info->off_pair_lora = take(n_pairs + 1);
+  info->off_pl_a = take(n_pl);
+  info->off_pl_b = take(n_pl);
+  info->off_pl_slot = take(n_pl);
   if (w > table_capacity) return LF_ERR_CAPACITY;
 
   auto put = [&](int32_t off, const std::vector<int32_t>& v) {
@@ -154,6 +189,11 @@ extern "C" int lf_plan_tables(const int32_t* route_start, const int32_t* route_e
   put(info->off_unit_tile, u_tile);
   put(info->off_unit_st0, u_st0);
   put(info->off_unit_nst, u_nst);
+  put(info->off_pair_lora, pair_first);
+  put(info->off_pl_a, pl_a);
+  put(info->off_pl_b, pl_b);
+  put(info->off_pl_slot, pl_slot);
+  info->n_pair_lora = n_pl;
 
   info->total_rows = total_rows;
   info->n_routes = n_routes;

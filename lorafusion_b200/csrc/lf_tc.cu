@@ -28,7 +28,7 @@ constexpr int kBK = 64;   // K elements per stage = one 128-byte swizzle row
 constexpr int kThreads = 192;
 constexpr int kGemmBN = 256;
 constexpr int kGemmStages = 4;
-constexpr int kShrStages = 3;
+constexpr int kShrStages = 8;
 constexpr int kGramStages = 4;
 
 template <typename OutT>
@@ -55,12 +55,20 @@ __device__ __forceinline__ __half cvt_out<__half>(float v) {
 // Time-bounded wait used only while unwinding after an abort: ignores the abort flag.
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* err) {
   const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) {
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       record_error(err, kErrTimeoutDrain);
       return;
     }
   }
+}
+
+// Global load issued at this point in program order (an asm volatile is never moved past the
+// other asm statements), so a value needed only after a k-loop is fetched before the loop.
+__device__ __forceinline__ int ld_early(const int32_t* p) {
+  int v;
+  asm volatile("ld.global.nc.b32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
 }
 
 // Bounded wait done by lane 0 and broadcast, so the warp stays converged for tcgen05.ld.
@@ -156,6 +164,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         int m, n;
         gemm_raster(t, prm, m, n);
+        int sb = 0, se = 0, sl[4] = {0, 0, 0, 0};
+        if (prm.lora) {  // the LoRA stages' table entries, fetched while the k-loop runs
+          sb = ld_early(prm.tb.base + prm.tb.off_tile_st + m);
+          se = ld_early(prm.tb.base + prm.tb.off_tile_st + m + 1);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            sl[q] = ld_early(prm.tb.base + prm.tb.off_st_slot + min(sb + q, prm.tb.n_segtiles - 1));
+        }
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, prm.tb.err, kErrTimeoutEmpty)) {
             ok = false;
@@ -179,17 +195,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (!ok || !prm.lora) continue;
-        const int sb = prm.tb.tile_st(m), se = prm.tb.tile_st(m + 1);
         const uint32_t bytes = static_cast<uint32_t>((kBM + kGemmBN) * prm.r_pad * 2);
         for (int j = sb; j < se; ++j) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, prm.tb.err, kErrTimeoutEmpty)) {
             ok = false;
             break;
           }
+          const int jj = j - sb;
+          const int slot = jj == 0 ? sl[0] : jj == 1 ? sl[1] : jj == 2 ? sl[2] : jj == 3 ? sl[3] : prm.tb.st_slot(j);
           mbar_arrive_expect_tx(&full[stage], bytes);
           tma_load_2d(sA + stage * kGemmABytes, &map_s, &full[stage], 0, j * kBM);
-          tma_load_2d(sB + stage * kGemmBBytes, &map_l, &full[stage], 0,
-                      prm.tb.st_slot(j) * prm.Nout + n * kGemmBN);
+          tma_load_2d(sB + stage * kGemmBBytes, &map_l, &full[stage], 0, slot * prm.Nout + n * kGemmBN);
           issued_mask |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == kGemmStages) {
@@ -222,6 +238,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(buf * kGemmBN);
+        int n_lora = 0;
+        if (prm.lora)
+          n_lora = ld_early(prm.tb.base + prm.tb.off_tile_st + m + 1) - ld_early(prm.tb.base + prm.tb.off_tile_st + m);
         uint32_t acc = 0;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, prm.tb.err, kErrTimeoutFull)) {
@@ -246,8 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (ok && prm.lora) {
-          const int sb = prm.tb.tile_st(m), se = prm.tb.tile_st(m + 1);
-          for (int j = sb; j < se; ++j) {
+          for (int j = 0; j < n_lora; ++j) {
             if (!mbar_wait(&full[stage], phase, abort_flag, prm.tb.err, kErrTimeoutFull)) {
               ok = false;
               break;
@@ -322,6 +340,310 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ========================================================================== pair GEMM
+// Same product as tc_gemm_kernel with 256x256 output tiles computed by a CTA pair
+// (cluster of 2, tcgen05 cta_group::2).  CTA r of the pair loads rows [128r, 128r+128) of the
+// tile's P rows and the N-half [128r, 128r+128) of Q into its own shared memory; the even CTA
+// issues M=256/N=256 MMAs that read both CTAs' tiles, and each CTA's TMEM receives its 128
+// rows.  Per CTA and k-block this moves 32 KB for 2x the FLOPs of the 48 KB single-CTA stage.
+// Every TMA completes on the even CTA's `full` barrier; the MMA thread commits to the `empty`
+// and `tfull` barriers of both CTAs; both CTAs' epilogue warps arrive on the even CTA's `tempty`.
+constexpr int kPairStages = 6;
+constexpr int kPairABytes = kBM * kBK * 2;   // 16 KB: this CTA's 128 rows of P
+constexpr int kPairBBytes = 128 * kBK * 2;   // 16 KB: this CTA's 128-row half of Q
+constexpr int kPairOutBytes = 4 * 2 * 32 * 64 * 2;  // epilogue staging: 4 warps x 2 buffers x (32 rows x 64 cols)
+constexpr int kPairSmem = 1024 + kPairStages * (kPairABytes + kPairBBytes) + kPairOutBytes + 256;
+
+struct PairParams {
+  void* out;
+  int64_t ldo;
+  int T, Nout, Kred;
+  int n_mpairs, n_ntiles, group_m;
+  int lora, r_pad;
+  uint32_t idesc_main, idesc_lora;
+  uint32_t lora_layout, lora_sbo;
+  Tables tb;
+};
+
+__device__ __forceinline__ void pair_raster(int t, const PairParams& p, int& mp, int& n) {
+  const int per_group = p.group_m * p.n_ntiles;
+  const int g = t / per_group;
+  const int first = g * p.group_m;
+  const int gsize = min(p.n_mpairs - first, p.group_m);
+  const int r = t - g * per_group;
+  mp = first + r % gsize;
+  n = r / gsize;
+}
+
+template <bool kQMN, typename OutT>
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_q,
+                        const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_l,
+                        const __grid_constant__ CUtensorMap map_o, const PairParams prm) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kPairStages * kPairABytes;
+  uint8_t* sOut = sB + kPairStages * kPairBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + kPairOutBytes);
+  uint64_t* empty = full + kPairStages;
+  uint64_t* tfull = empty + kPairStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();  // 0: issues the MMAs
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int n_pairs = static_cast<int>(gridDim.x >> 1);
+  const int total = prm.n_mpairs * prm.n_ntiles;
+  const int nkb = (prm.Kred + kBK - 1) / kBK;
+  const Tables& tb = prm.tb;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // one arrive per epilogue warp of both CTAs
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&map_p);
+    tma_prefetch_desc(&map_q);
+    tma_prefetch_desc(&map_o);
+    if (prm.lora) {
+      tma_prefetch_desc(&map_s);
+      tma_prefetch_desc(&map_l);
+    }
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer's barriers exist before anyone signals them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t full_lead = map_to_cta(smem_u32(full), 0);
+  const uint32_t tempty_lead = map_to_cta(smem_u32(tempty), 0);
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, issued_mask = 0, last_parity = 0;
+      bool ok = true;
+      const uint32_t main_bytes = 2u * (kPairABytes + kPairBBytes);
+      const uint32_t lora_bytes = static_cast<uint32_t>(2 * 2 * kBM * prm.r_pad * 2);
+      for (int t = pair; t < total && ok; t += n_pairs) {
+        int mp, n;
+        pair_raster(t, prm, mp, n);
+        const int mtile = 2 * mp + static_cast<int>(crank);
+        int pb = 0, pe = 0, sl[4] = {0, 0, 0, 0}, ss[4] = {0, 0, 0, 0};
+        const int32_t* st_of = tb.base + (crank ? tb.off_pl_b : tb.off_pl_a);
+        if (prm.lora) {  // fetched while the k-loop runs
+          pb = ld_early(tb.base + tb.off_pair_lora + mp);
+          pe = ld_early(tb.base + tb.off_pair_lora + mp + 1);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int i = min(pb + q, max(pe - 1, 0));
+            sl[q] = ld_early(tb.base + tb.off_pl_slot + i);
+            ss[q] = ld_early(st_of + i);
+          }
+        }
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, tb.err, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          if (crank == 0) mbar_arrive_expect_tx(&full[stage], main_bytes);
+          const uint32_t fb = full_lead + static_cast<uint32_t>(stage * 8);
+          tma_load_2d_pair(sA + stage * kPairABytes, &map_p, fb, kb * kBK, mtile * kBM);
+          if (kQMN) {
+            tma_load_2d_pair(sB + stage * kPairBBytes, &map_q, fb, n * 256 + static_cast<int>(crank) * 128, kb * kBK);
+            tma_load_2d_pair(sB + stage * kPairBBytes + 64 * kBK * 2, &map_q, fb,
+                             n * 256 + static_cast<int>(crank) * 128 + 64, kb * kBK);
+          } else {
+            tma_load_2d_pair(sB + stage * kPairBBytes, &map_q, fb, kb * kBK, n * 256 + static_cast<int>(crank) * 128);
+          }
+          issued_mask |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok || !prm.lora) continue;
+        for (int i = pb; i < pe; ++i) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, tb.err, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          const int q = i - pb;
+          const int slot = q == 0 ? sl[0] : q == 1 ? sl[1] : q == 2 ? sl[2] : q == 3 ? sl[3] : tb.pl_slot(i);
+          const int st = q == 0 ? ss[0] : q == 1 ? ss[1] : q == 2 ? ss[2] : q == 3 ? ss[3] : st_of[i];
+          if (crank == 0) mbar_arrive_expect_tx(&full[stage], lora_bytes);
+          const uint32_t fb = full_lead + static_cast<uint32_t>(stage * 8);
+          tma_load_2d_pair(sA + stage * kPairABytes, &map_s, fb, 0, st * kBM);
+          tma_load_2d_pair(sB + stage * kPairBBytes, &map_l, fb, 0,
+                           slot * prm.Nout + n * 256 + static_cast<int>(crank) * 128);
+          issued_mask |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok && crank == 0)  // copies of both CTAs complete on the even CTA's barriers
+        for (int s = 0; s < kPairStages; ++s)
+          if (issued_mask & (1u << s)) drain_wait(&full[s], (last_parity >> s) & 1u, tb.err);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && crank == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true, issued_any = false;
+      const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
+      const uint32_t empty_self = map_to_cta(smem_u32(empty), 0), empty_peer = map_to_cta(smem_u32(empty), 1);
+      const uint32_t tfull_self = map_to_cta(smem_u32(tfull), 0), tfull_peer = map_to_cta(smem_u32(tfull), 1);
+      int it = 0;
+      for (int t = pair; t < total && ok; t += n_pairs, ++it) {
+        int mp, n;
+        pair_raster(t, prm, mp, n);
+        const int buf = it & 1;
+        int n_lora = 0;
+        if (prm.lora) n_lora = ld_early(tb.base + tb.off_pair_lora + mp + 1) - ld_early(tb.base + tb.off_pair_lora + mp);
+        if (!mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1, abort_flag, tb.err, kErrTimeoutAcc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * 256);
+        uint32_t acc = 0;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, tb.err, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = a_base + stage * kPairABytes, b0 = b_base + stage * kPairBBytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t adesc = umma_sdesc(a0 + k * 32, 16, 1024, 2);
+            const uint64_t bdesc = kQMN ? umma_sdesc(b0 + k * 2048, 64 * kBK * 2, 1024, 2)
+                                        : umma_sdesc(b0 + k * 32, 16, 1024, 2);
+            umma_f16_pair(d, adesc, bdesc, prm.idesc_main, acc);
+            acc = 1;
+          }
+          issued_any = true;
+          umma_commit_pair(empty_self + stage * 8);
+          umma_commit_pair(empty_peer + stage * 8);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        for (int j = 0; ok && j < n_lora; ++j) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, tb.err, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = a_base + stage * kPairABytes, b0 = b_base + stage * kPairBBytes;
+          for (int k = 0; k < prm.r_pad / 16; ++k) {
+            const uint64_t adesc = umma_sdesc(a0 + k * 32, 16, prm.lora_sbo, prm.lora_layout);
+            const uint64_t bdesc = umma_sdesc(b0 + k * 32, 16, prm.lora_sbo, prm.lora_layout);
+            umma_f16_pair(d, adesc, bdesc, prm.idesc_lora, acc);
+            acc = 1;
+          }
+          issued_any = true;
+          umma_commit_pair(empty_self + stage * 8);
+          umma_commit_pair(empty_peer + stage * 8);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull_self + buf * 8);
+        umma_commit_pair(tfull_peer + buf * 8);
+      }
+      if (!ok && issued_any) {
+        umma_commit_pair(map_to_cta(smem_u32(drain), 0));
+        drain_wait(drain, 0, tb.err);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    int it = 0;
+    int n_stores = 0;
+    for (int t = pair; t < total; t += n_pairs, ++it) {
+      int mp, n;
+      pair_raster(t, prm, mp, n);
+      const int buf = it & 1;
+      if (!warp_wait(&tfull[buf], (it >> 1) & 1, abort_flag, tb.err, kErrTimeoutAcc)) break;
+      tc_fence_after();
+      // rows [row0, row0+32) of this CTA's tile: TMEM -> registers -> swizzled staging -> TMA store
+      const int row0 = (2 * mp + static_cast<int>(crank)) * kBM + q * 32;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * 256);
+      uint8_t* stage_w = sOut + (warp - 2) * (2 * 32 * 64 * 2);
+#pragma unroll 1
+      for (int c = 0; c < 256 / 64; ++c) {
+        uint32_t v[64];
+        tmem_ld32(tbase + c * 64, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(tbase + c * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_wait_ld();
+        if (c == 256 / 64 - 1) {  // accumulator fully read: hand it back to the MMA thread
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(tempty_lead + buf * 8);
+        }
+        const int col0 = n * 256 + c * 64;
+        if (row0 >= prm.T || col0 >= prm.Nout) continue;
+        uint8_t* sbuf = stage_w + (n_stores & 1) * (32 * 64 * 2);
+        if (lane == 0) bulk_wait_read<1>();  // the store that used this buffer has read it
+        __syncwarp();
+        uint8_t* rowp = sbuf + lane * 128;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {  // 16-byte granule g of the row goes to slot g ^ (row % 8)
+          uint4 pk;
+          pk.x = pack2<OutT>(__uint_as_float(v[g * 8 + 0]), __uint_as_float(v[g * 8 + 1]));
+          pk.y = pack2<OutT>(__uint_as_float(v[g * 8 + 2]), __uint_as_float(v[g * 8 + 3]));
+          pk.z = pack2<OutT>(__uint_as_float(v[g * 8 + 4]), __uint_as_float(v[g * 8 + 5]));
+          pk.w = pack2<OutT>(__uint_as_float(v[g * 8 + 6]), __uint_as_float(v[g * 8 + 7]));
+          *reinterpret_cast<uint4*>(rowp + ((g ^ (lane & 7)) << 4)) = pk;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&map_o, sbuf, col0, row0);
+          bulk_commit();
+        }
+        ++n_stores;
+      }
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 512);
+  }
+}
+
 // ========================================================================== shrink
 struct ShrinkParams {
   void* s_ext;
@@ -334,13 +656,14 @@ struct ShrinkParams {
 };
 
 constexpr int kShrABytes = kBM * kBK * 2;    // 16 KB
-constexpr int kShrBBytes = 128 * kBK * 2;    // N <= 128 rows
+constexpr int kShrBBytes = 64 * kBK * 2;     // N <= 64 rows (unit = <= 64 / r_pad segment tiles)
 constexpr int kShrSmem = 1024 + kShrStages * (kShrABytes + kShrBBytes) + 256;
 constexpr int kPartLd = kBM + 1;             // column-major partial sums, odd stride
-static_assert(128 * kPartLd * 4 <= kShrStages * (kShrABytes + kShrBBytes), "partials must fit the stage area");
+constexpr int kMaxShrCluster = 4;             // K split across at most 4 CTAs (all resident at once)
+static_assert(64 * kPartLd * 4 <= kShrStages * (kShrABytes + kShrBBytes), "partials must fit the stage area");
 
 template <typename OutT>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, 1)
     tc_shrink_kernel(const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_a,
                      const ShrinkParams prm) {
   extern __shared__ uint8_t smem_raw[];
@@ -354,6 +677,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* drain = tfull + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* seg_lo = reinterpret_cast<int*>(tmem_slot + 2);  // per segment tile of the unit (<= 4)
+  int* seg_hi = seg_lo + 8;
+  float* seg_scale = reinterpret_cast<float*>(seg_hi + 8);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Tables& tb = prm.tb;
@@ -379,8 +705,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     tma_prefetch_desc(&map_p);
     tma_prefetch_desc(&map_a);
   }
+  if (threadIdx.x >= 32 && threadIdx.x < 32 + nst) {  // segment bounds for the reduction step
+    const int j = threadIdx.x - 32;
+    seg_lo[j] = tb.st_lo(st0 + j);
+    seg_hi[j] = tb.st_hi(st0 + j);
+    seg_scale[j] = tb.st_scale(st0 + j);
+  }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 128);
+    __syncwarp();
+    tmem_alloc(tmem_slot, 64);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -394,6 +727,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       uint32_t phase = 0, issued_mask = 0, last_parity = 0;
       bool ok = true;
       const uint32_t bytes = static_cast<uint32_t>(kShrABytes + N * kBK * 2);
+      int arow[4];  // first packed-A row of every segment's adapter, read once
+#pragma unroll
+      for (int j = 0; j < 4; ++j) arow[j] = j < nst ? tb.st_slot(st0 + j) * r_pad : 0;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, prm.tb.err, kErrTimeoutEmpty)) {
           ok = false;
@@ -401,9 +737,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         }
         mbar_arrive_expect_tx(&full[stage], bytes);
         tma_load_2d(sA + stage * kShrABytes, &map_p, &full[stage], kb * kBK, tile * kBM);
-        for (int j = 0; j < nst; ++j)
-          tma_load_2d(sB + stage * kShrBBytes + j * r_pad * (kBK * 2), &map_a, &full[stage], kb * kBK,
-                      tb.st_slot(st0 + j) * r_pad);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (j < nst)
+            tma_load_2d(sB + stage * kShrBBytes + j * r_pad * (kBK * 2), &map_a, &full[stage], kb * kBK, arow[j]);
         issued_mask |= 1u << stage;
         last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
         if (++stage == kShrStages) {
@@ -484,21 +821,31 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int e = threadIdx.x; e < total; e += kThreads) {
       const int row = r0 + e / N, col = e % N;
       const uint32_t off = static_cast<uint32_t>((col * kPartLd + row) * 4);
+      float part[kMaxShrCluster];
+#pragma unroll
+      for (int qr = 0; qr < kMaxShrCluster; ++qr)  // issue every peer load before summing
+        part[qr] = qr < prm.cluster ? ld_cluster_f32(map_to_cta(part_base + off, qr)) : 0.f;
       float sum = 0.f;
-      for (int qr = 0; qr < prm.cluster; ++qr) sum += ld_cluster_f32(map_to_cta(part_base + off, qr));
+#pragma unroll
+      for (int qr = 0; qr < kMaxShrCluster; ++qr) sum += part[qr];
       const int j = col / r_pad, jj = col - j * r_pad;
       const int st = st0 + j;
-      const bool in = row >= tb.st_lo(st) && row < tb.st_hi(st);
-      const float v = in ? tb.st_scale(st) * sum : 0.f;
+      const bool in = row >= seg_lo[j] && row < seg_hi[j];
+      const float v = in ? seg_scale[j] * sum : 0.f;
       out[(static_cast<int64_t>(st) * kBM + row) * r_pad + jj] = cvt_out<OutT>(v);
     }
+  }
+
+  if (blockIdx.x == 0) {  // the all-zero segment tile the pair GEMM pads odd row tiles with
+    OutT* zero = reinterpret_cast<OutT*>(prm.s_ext) + static_cast<int64_t>(tb.n_segtiles) * kBM * r_pad;
+    for (int e = threadIdx.x; e < kBM * r_pad; e += kThreads) zero[e] = cvt_out<OutT>(0.f);
   }
 
   // keep this CTA's shared memory alive until every peer has read it
   cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 128);
+    tmem_dealloc(tmem_base, 64);
   }
 }
 
@@ -516,7 +863,25 @@ struct GramParams {
 
 constexpr int kGramDBytes = kBM * 128 * 2;  // 128 rows x 128 columns
 constexpr int kGramSBytes = kBM * 64 * 2;   // 128 rows x r_pad (<= 64)
-constexpr int kGramSmem = 1024 + kGramStages * (kGramDBytes + kGramSBytes) + 256;
+constexpr int kGramSmem = 1024 + kGramStages * (kGramDBytes + kGramSBytes) + 24 * 128 + 256;
+
+// Work units of one CTA (slot, column block), staged in shared memory once so no role
+// waits on a dependent table load per unit.  Units past kGramMaxUnits read the table directly.
+constexpr int kGramMaxUnits = 128;
+struct GramUnit {
+  int slot, b, e, rank, rank_prefix, cb;
+};
+
+__device__ __forceinline__ GramUnit gram_unit_from_table(const Tables& tb, int u, int n_cblk) {
+  GramUnit g;
+  g.slot = tb.slot_order(u / n_cblk);
+  g.cb = u % n_cblk;
+  g.b = tb.slot_st(g.slot);
+  g.e = tb.slot_st(g.slot + 1);
+  g.rank = tb.slot_rank(g.slot);
+  g.rank_prefix = tb.rank_prefix(g.slot);
+  return g;
+}
 
 template <typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -526,7 +891,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sD = smem;
   uint8_t* sS = smem + kGramStages * kGramDBytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sS + kGramStages * kGramSBytes);
+  GramUnit* units = reinterpret_cast<GramUnit*>(sS + kGramStages * kGramSBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(units + kGramMaxUnits);
   uint64_t* empty = full + kGramStages;
   uint64_t* tfull = empty + kGramStages;
   uint64_t* tempty = tfull + 2;
@@ -537,6 +903,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Tables& tb = prm.tb;
   const int total = tb.n_slots * prm.n_cblk;
+  const int n_mine = total > static_cast<int>(blockIdx.x)
+                         ? (total - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) / gridDim.x
+                         : 0;
   const int r_pad = prm.r_pad;
 
   if (threadIdx.x == 0) {
@@ -554,7 +923,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&map_d);
     tma_prefetch_desc(&map_s);
   }
+  if (warp >= 2) {  // stage this CTA's unit schedule
+    for (int k = threadIdx.x - 64; k < n_mine && k < kGramMaxUnits; k += kThreads - 64)
+      units[k] = gram_unit_from_table(tb, static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x), prm.n_cblk);
+  }
   if (warp == 1) {
+    __syncwarp();
     tmem_alloc(tmem_slot, 128);
     tmem_relinquish();
   }
@@ -562,27 +936,45 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  auto unit = [&](int k) -> GramUnit {
+    return k < kGramMaxUnits ? units[k]
+                             : gram_unit_from_table(tb, static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x),
+                                                    prm.n_cblk);
+  };
 
   if (warp == 0) {
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0, issued_mask = 0, last_parity = 0;
-      bool ok = true;
-      const uint32_t bytes = static_cast<uint32_t>(kGramDBytes + kBM * r_pad * 2);
-      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-        const int slot = tb.slot_order(u / prm.n_cblk);
-        const int cb = u % prm.n_cblk;
-        for (int i = tb.slot_st(slot); i < tb.slot_st(slot + 1); ++i) {
-          const int st = tb.slot_list(i);
-          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, prm.tb.err, kErrTimeoutEmpty)) {
+    // The whole warp walks the segment-tile lists 32 entries at a time; lane 0 issues the copies.
+    int stage = 0;
+    uint32_t phase = 0, issued_mask = 0, last_parity = 0;
+    bool ok = true;
+    const uint32_t bytes = static_cast<uint32_t>(kGramDBytes + kBM * r_pad * 2);
+    for (int k = 0; k < n_mine && ok; ++k) {
+      const GramUnit g = unit(k);
+      for (int i0 = g.b; i0 < g.e && ok; i0 += 32) {
+        int st = 0, row0 = 0;
+        if (i0 + lane < g.e) {
+          st = tb.slot_list(i0 + lane);
+          row0 = tb.st_tile(st) * kBM;
+        }
+        const int cnt = min(32, g.e - i0);
+        for (int q = 0; q < cnt; ++q) {
+          const int st_q = __shfl_sync(0xffffffffu, st, q);
+          const int row_q = __shfl_sync(0xffffffffu, row0, q);
+          int go = 1;
+          if (lane == 0) {
+            go = mbar_wait(&empty[stage], phase ^ 1, abort_flag, prm.tb.err, kErrTimeoutEmpty) ? 1 : 0;
+            if (go) {
+              mbar_arrive_expect_tx(&full[stage], bytes);
+              tma_load_2d(sD + stage * kGramDBytes, &map_d, &full[stage], g.cb * 128, row_q);
+              tma_load_2d(sD + stage * kGramDBytes + kGramDBytes / 2, &map_d, &full[stage], g.cb * 128 + 64, row_q);
+              tma_load_2d(sS + stage * kGramSBytes, &map_s, &full[stage], 0, st_q * kBM);
+            }
+          }
+          go = __shfl_sync(0xffffffffu, go, 0);
+          if (!go) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], bytes);
-          const int row0 = tb.st_tile(st) * kBM;
-          tma_load_2d(sD + stage * kGramDBytes, &map_d, &full[stage], cb * 128, row0);
-          tma_load_2d(sD + stage * kGramDBytes + kGramDBytes / 2, &map_d, &full[stage], cb * 128 + 64, row0);
-          tma_load_2d(sS + stage * kGramSBytes, &map_s, &full[stage], 0, st * kBM);
           issued_mask |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == kGramStages) {
@@ -591,10 +983,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (!ok)
-        for (int s = 0; s < kGramStages; ++s)
-          if (issued_mask & (1u << s)) drain_wait(&full[s], (last_parity >> s) & 1u, prm.tb.err);
     }
+    if (!ok && lane == 0)
+      for (int s = 0; s < kGramStages; ++s)
+        if (issued_mask & (1u << s)) drain_wait(&full[s], (last_parity >> s) & 1u, prm.tb.err);
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
@@ -603,10 +995,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true, issued_any = false;
       const uint32_t d_base = smem_u32(sD), s_base = smem_u32(sS);
       int it = 0;
-      for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
-        const int slot = tb.slot_order(u / prm.n_cblk);
-        const int b = tb.slot_st(slot), e = tb.slot_st(slot + 1);
-        if (b == e) continue;  // adapter with only empty routes: epilogue writes zeros
+      for (int k = 0; k < n_mine && ok; ++k) {
+        const GramUnit g = unit(k);
+        if (g.b == g.e) continue;  // adapter with only empty routes: epilogue writes zeros
         const int buf = it & 1;
         if (!mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1, abort_flag, prm.tb.err, kErrTimeoutAcc)) {
           ok = false;
@@ -615,7 +1006,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t dt = tmem_base + static_cast<uint32_t>(buf * 64);
         uint32_t acc = 0;
-        for (int i = b; i < e; ++i) {
+        for (int i = g.b; i < g.e; ++i) {
           if (!mbar_wait(&full[stage], phase, abort_flag, prm.tb.err, kErrTimeoutFull)) {
             ok = false;
             break;
@@ -623,9 +1014,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t a0 = d_base + stage * kGramDBytes, b0 = s_base + stage * kGramSBytes;
 #pragma unroll
-          for (int k = 0; k < kBM / 16; ++k) {
-            const uint64_t adesc = umma_sdesc(a0 + k * 2048, kGramDBytes / 2, 1024, 2);
-            const uint64_t bdesc = umma_sdesc(b0 + k * prm.s_kstep, kBM * r_pad * 2, prm.s_sbo, prm.s_layout);
+          for (int kk = 0; kk < kBM / 16; ++kk) {
+            const uint64_t adesc = umma_sdesc(a0 + kk * 2048, kGramDBytes / 2, 1024, 2);
+            const uint64_t bdesc = umma_sdesc(b0 + kk * prm.s_kstep, kBM * r_pad * 2, prm.s_sbo, prm.s_layout);
             umma_f16(dt, adesc, bdesc, prm.idesc, acc);
             acc = 1;
           }
@@ -650,14 +1041,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     int it = 0;
     OutT* out = reinterpret_cast<OutT*>(prm.out);
-    for (int u = blockIdx.x; u < total; u += gridDim.x) {
-      const int slot = tb.slot_order(u / prm.n_cblk);
-      const int cb = u % prm.n_cblk;
-      const int c = cb * 128 + q * 32 + lane;
-      const int rank = tb.slot_rank(slot);
-      OutT* o = out + static_cast<int64_t>(tb.rank_prefix(slot)) * prm.C;
-      const bool empty_slot = tb.slot_st(slot) == tb.slot_st(slot + 1);
-      if (empty_slot) {
+    for (int k = 0; k < n_mine; ++k) {
+      const GramUnit g = unit(k);
+      const int c = g.cb * 128 + q * 32 + lane;
+      const int rank = g.rank;
+      OutT* o = out + static_cast<int64_t>(g.rank_prefix) * prm.C;
+      if (g.b == g.e) {
         if (c < prm.C)
           for (int j = 0; j < rank; ++j) {
             if (prm.transpose_out)
@@ -772,13 +1161,72 @@ cudaError_t tc_gemm(int dtype, bool q_mn_major, const TcMaps& maps, int T, int N
   return cudaGetLastError();
 }
 
+cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, int Nout, int Kred, bool lora,
+                         const Tables& tb, void* out, int64_t ldo, int num_sms, cudaStream_t st) {
+  PairParams p{};
+  p.out = out;
+  p.ldo = ldo;
+  p.T = T;
+  p.Nout = Nout;
+  p.Kred = Kred;
+  const int n_mtiles = (T + kBM - 1) / kBM;
+  p.n_mpairs = (n_mtiles + 1) / 2;
+  p.n_ntiles = (Nout + 255) / 256;
+  p.group_m = 8;
+  p.lora = lora ? 1 : 0;
+  p.r_pad = tb.r_pad;
+  const int fmt = dtype == LF_BF16 ? 1 : 0;
+  p.idesc_main = umma_idesc_f16(256, 256, fmt, 0, q_mn_major ? 1 : 0);
+  p.idesc_lora = umma_idesc_f16(256, 256, fmt, 0, 0);
+  p.lora_layout = umma_layout_for_span(tb.r_pad * 2);
+  p.lora_sbo = sw_sbo(tb.r_pad);
+  p.tb = tb;
+  const int total = p.n_mpairs * p.n_ntiles;
+  if (total == 0) return cudaSuccess;
+  const int pairs = total < num_sms / 2 ? total : num_sms / 2;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPairSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
+#define LF_LAUNCH_PAIR(QMN, OT)                                                                  \
+  e = ensure_smem(tc_gemm_pair_kernel<QMN, OT>, kPairSmem);                                     \
+  if (e != cudaSuccess) return e;                                                               \
+  e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<QMN, OT>, maps.p, maps.q, maps.s, maps.l, maps.o, p);
+  if (dtype == LF_BF16) {
+    if (q_mn_major) {
+      LF_LAUNCH_PAIR(true, __nv_bfloat16)
+    } else {
+      LF_LAUNCH_PAIR(false, __nv_bfloat16)
+    }
+  } else {
+    if (q_mn_major) {
+      LF_LAUNCH_PAIR(true, __half)
+    } else {
+      LF_LAUNCH_PAIR(false, __half)
+    }
+  }
+#undef LF_LAUNCH_PAIR
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
 cudaError_t tc_shrink(int dtype, const CUtensorMap& p_map, const CUtensorMap& a_map, int Kred, const Tables& tb,
                       void* s_ext, int num_sms, cudaStream_t st) {
   if (tb.n_units == 0) return cudaSuccess;
   const int nkb = (Kred + kBK - 1) / kBK;
-  // split K across a cluster until there are about two CTAs per SM
+  // split K across a cluster while every CTA still fits on the GPU at once (one per SM)
+  // and each keeps at least four k-blocks
   int cluster = 1;
-  while (cluster < 8 && tb.n_units * cluster * 2 <= 2 * num_sms && nkb >= 2 * cluster * 2) cluster *= 2;
+  while (cluster < kMaxShrCluster && tb.n_units * cluster * 2 <= num_sms && nkb >= 4 * cluster * 2) cluster *= 2;
   ShrinkParams p{};
   p.s_ext = s_ext;
   p.ab_fmt = dtype == LF_BF16 ? 1 : 0;

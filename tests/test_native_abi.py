@@ -105,9 +105,9 @@ def test_tables_round_trip_reference_routes(layout_golden):
         for s in range(info.n_slots):
             part = lst[slot_st[s]:slot_st[s + 1]]
             assert np.all(np.diff(part) > 0)
-        # shrink units cover each tile's segment tiles in runs of <= 128 / r_pad
+        # shrink units cover each tile's segment tiles in runs of <= 64 / r_pad
         nst = _sec(info, table, "unit_nst", info.n_shrink_units)
-        assert nst.sum() == info.n_segtiles and nst.max(initial=1) <= 128 // info.r_pad
+        assert nst.sum() == info.n_segtiles and nst.max(initial=1) <= 64 // info.r_pad
 
 
 def test_tables_errors_and_padding():

@@ -231,3 +231,21 @@ def test_edge_cases():
     y = ops.fused_lora_forward(xb, w, ab, bb, ad, rt2)
     ref = xb.float() @ w.bfloat16().float().t() + 2.0 * (xb.float() @ ab[0].float().t()) @ bb[0].float().t()
     _check(y, ref.cpu().numpy(), BF16_TOL, "non-contiguous x")
+
+
+@pytest.mark.parametrize("single_cta", [False, True], ids=["cta_pair", "single_cta"])
+def test_gemm_tilings_match_oracle(single_cta):
+    """Both GEMM tilings (256x256 on CTA pairs, 128x256 on single CTAs), odd row-tile count."""
+    from lorafusion_b200 import _native as nat
+    ops = _ops()
+    routes = _routes_from_sizes([130, 3, 250, 97, 160], [0, 1, 2, 0, 3])  # 640 rows = 5 row tiles
+    case = _random_case(11, 640, 320, 520, routes, {0: 16, 1: 8, 2: 32, 3: 16}, torch.bfloat16)
+    x, w, a, b, ad, routing, _ = _to_torch(case, torch.bfloat16)
+    prep = ops.prepare_forward(x, w, a, b, ad, routing)
+    y = prep.new_output()
+    stages = nat.LF_STAGE_SHRINK | nat.LF_STAGE_EXPAND | (nat.LF_STAGE_SINGLE_CTA if single_cta else 0)
+    prep.launch(y, stages)
+    _check(y, case["y"], BF16_TOL, "forward")
+    y0 = prep.new_output()
+    prep.launch(y0, nat.LF_STAGE_BASE | (nat.LF_STAGE_SINGLE_CTA if single_cta else 0))
+    _check(y0, case["x"] @ case["w"].T, BF16_TOL, "base GEMM only")
