@@ -1,0 +1,130 @@
+"""Row sharding across ranks: bin assignment, local layouts and the gradient all-reduce of
+adapters that span ranks, checked on CPU with world-size-2 gloo process groups."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from lorafusion_b200.scheduler import Request, bucket_by_adapter, build_microbatch, greedy_pack
+from lorafusion_b200.sharding import allreduce_spanning_grads, assign_bins, local_layout
+from lorafusion_b200.workloads import WORKLOADS, row_counts
+
+
+def _packing(counts, cap):
+    reqs = [Request(i, i, c) for i, c in enumerate(counts)]
+    groups = bucket_by_adapter(reqs)
+    return reqs, greedy_pack({g.adapter_id: g.total_rows for g in groups}, cap)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+@pytest.mark.parametrize("name", ["cfg2_h4096_a16_r16", "cfg4_decode_skew_a512", "cfg5_70b_a256_r64"])
+def test_assignment_covers_every_bin_and_balances(name, world):
+    wl = WORKLOADS[name]
+    _, packing = _packing(row_counts(wl, wl.total_rows * world), wl.tile_capacity)
+    plan = assign_bins(packing.bins, world)
+    assert plan == assign_bins(packing.bins, world)  # deterministic
+    assert len(plan.bin_rank) == len(packing.bins) and set(plan.bin_rank) <= set(range(world))
+    loads = [plan.rank_rows(r) for r in range(world)]
+    assert sum(loads) == sum(sum(n for _, n in b) for b in packing.bins)
+    share = sum(loads) / world
+    assert max(loads) <= share + 2 * wl.tile_capacity  # within two bins of an even split
+    owners = {}
+    for b, entries in enumerate(packing.bins):
+        for a, _ in entries:
+            owners.setdefault(a, set()).add(plan.bin_rank[b])
+    assert plan.spanning == sorted(a for a, r in owners.items() if len(r) > 1)
+    if world == 1:
+        assert plan.spanning == []
+
+
+def test_local_layouts_partition_the_global_batch():
+    wl = WORKLOADS["cfg2_h4096_a16_r16"]
+    world = 3
+    reqs, packing = _packing(row_counts(wl, 4096 * world), wl.tile_capacity)
+    tensors = {r.request_id: torch.arange(r.num_rows, dtype=torch.float64)[:, None] + 1e6 * r.request_id
+               for r in reqs}
+    fused, routing, _ = build_microbatch(reqs, tensors, packing)
+    plan = assign_bins(packing.bins, world)
+    seen = []
+    for rank in range(world):
+        rows, local = local_layout(plan, packing.bins, rank, wl.tile_capacity)
+        local.validate(len(rows))
+        seen.extend(rows)
+        # every local route is a global route shifted to local row numbers
+        glob = {(r.row_start, r.row_end, r.adapter_id) for r in routing.routes}
+        for lr in local.routes:
+            g0 = rows[lr.row_start]
+            assert (g0, g0 + lr.num_rows, lr.adapter_id) in glob
+            assert rows[lr.row_end - 1] == g0 + lr.num_rows - 1
+    assert sorted(seen) == list(range(fused.shape[0]))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, result_q):
+    import torch.distributed as dist
+    from oracle import mock_oracle
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        K, N = 48, 40
+        counts = [300, 90, 60, 33, 20, 9]
+        reqs, packing = _packing(counts, 64)
+        plan = assign_bins(packing.bins, world)
+        rng = np.random.default_rng(0)
+        ranks = {i: [4, 8, 4, 16, 8, 4][i] for i in range(len(counts))}
+        x_g = rng.standard_normal((sum(counts), K)).astype(np.float32)
+        g_g = rng.standard_normal((sum(counts), N)).astype(np.float32)
+        w = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float32)
+        a = {i: (rng.standard_normal((r, K)) / np.sqrt(K)).astype(np.float32) for i, r in ranks.items()}
+        b = {i: (0.02 * rng.standard_normal((N, r))).astype(np.float32) for i, r in ranks.items()}
+        sc = {i: 2.0 for i in ranks}
+        rows, local = local_layout(plan, packing.bins, rank, 64)
+        lroutes = [(r.row_start, r.row_end, r.adapter_id) for r in local.routes]
+        _, ga, gb = mock_oracle.fused_lora_backward(g_g[rows], x_g[rows], w, a, b, sc, lroutes)
+        ga_t = {k: torch.from_numpy(v.copy()) for k, v in ga.items()}
+        gb_t = {k: torch.from_numpy(v.copy()) for k, v in gb.items()}
+        allreduce_spanning_grads(plan, ga_t, gb_t, ranks, K, N, torch.device("cpu"))
+        # full-batch reference
+        groutes, cur = [], 0
+        for entries in packing.bins:
+            for aid, n in entries:
+                groutes.append((cur, cur + n, aid))
+                cur += n
+        _, ga_ref, gb_ref = mock_oracle.fused_lora_backward(g_g, x_g, w, a, b, sc, groutes)
+        ok = bool(plan.spanning)
+        for aid in plan.spanning:
+            ok &= np.allclose(ga_t[aid].numpy(), ga_ref[aid], rtol=1e-4, atol=1e-4)
+            ok &= np.allclose(gb_t[aid].numpy(), gb_ref[aid], rtol=1e-4, atol=1e-4)
+        for aid in ga_t:
+            if aid not in plan.spanning:  # whole on this rank already
+                ok &= np.allclose(ga_t[aid].numpy(), ga_ref[aid], rtol=1e-4, atol=1e-4)
+        result_q.put((rank, ok, list(plan.spanning)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_spanning_gradients_allreduce_gloo():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(ok for _, ok, _ in results), results
+    assert results[0][2] and results[0][2] == results[1][2]
