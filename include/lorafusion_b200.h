@@ -176,6 +176,23 @@ LF_API int lf_backward(const lf_problem* prob, const lf_plan_info* info, const i
                 void* workspace_dev, size_t workspace_bytes, lf_stream_t stream);
 
 /*
+ * Forward for callers that cannot allocate device memory: same inputs, output and result as
+ * lf_forward, but no workspace argument.  The scratch lives in a fixed array of
+ * LF_NOALLOC_SCRATCH_BYTES that the library declares in device memory; every GPU that loads the
+ * library holds that array until the process exits.  No counterpart in the reference (its ops
+ * allocate freely through torch).
+ *  - Returns LF_ERR_CAPACITY when lf_forward_workspace_bytes(info, dtype) exceeds the array.
+ *  - Allocates nothing: no cudaMalloc/cudaFree and no allocating library call.
+ *  - The first call on each device looks up the array's device address (with that device
+ *    current); make that first call before any stream capture.
+ *  - All calls on a device share the one array: calls whose work overlaps on the GPU (other
+ *    streams, other host threads) race on it and must be serialized by the caller.
+ */
+#define LF_NOALLOC_SCRATCH_BYTES (16u << 20)
+LF_API int lf_forward_noalloc(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
+                              void* y_dev, lf_stream_t stream);
+
+/*
  * Read and clear the device-side error word (bounded-wait timeouts inside kernels).
  * Synchronizes the current device.  *code = 0 when no kernel reported a problem.
  */
