@@ -90,6 +90,7 @@ typedef struct lf_plan_info {
   int32_t off_pl_a;        /* [n_pair_lora] segment tile of the even row tile */
   int32_t off_pl_b;        /* [n_pair_lora] segment tile of the odd row tile */
   int32_t off_pl_slot;     /* [n_pair_lora] adapter slot */
+  int32_t off_tile_unit;   /* [n_tiles+1]  CSR: shrink units of each row tile */
 } lf_plan_info;
 
 /* Upper bound on the int32 words lf_plan_tables needs. */
@@ -164,6 +165,13 @@ LF_API int lf_forward(const lf_problem* prob, const lf_plan_info* info, const in
 #define LF_STAGE_SINGLE_CTA 8
 LF_API int lf_forward_stages(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, void* y_dev,
                              void* workspace_dev, size_t workspace_bytes, int32_t stages, lf_stream_t stream);
+
+/*
+ * Kernel launches lf_forward makes for this problem on the current device: 1 when the routed
+ * shrink runs on CTA pairs the fused GEMM's round count leaves idle (same launch), else 2.
+ * Returns a negative lf_status on bad arguments.  No counterpart in the reference.
+ */
+LF_API int lf_forward_launch_count(const lf_problem* prob, const lf_plan_info* info);
 
 /*
  * Backward: grad_x [T,K]; grad_a = concatenated [r_s, K] blocks and grad_b = concatenated

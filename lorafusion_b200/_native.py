@@ -39,7 +39,7 @@ class PlanInfo(ctypes.Structure):
         "off_tile_st", "off_st_tile", "off_st_lo", "off_st_hi", "off_st_slot", "off_st_route", "off_st_scale",
         "off_slot_st", "off_slot_list", "off_slot_rank", "off_rank_prefix", "off_slot_order",
         "off_unit_tile", "off_unit_st0", "off_unit_nst",
-        "n_pair_lora", "off_pair_lora", "off_pl_a", "off_pl_b", "off_pl_slot")]
+        "n_pair_lora", "off_pair_lora", "off_pl_a", "off_pl_b", "off_pl_slot", "off_tile_unit")]
 
 
 class Problem(ctypes.Structure):
@@ -72,6 +72,8 @@ def _declare(L: ctypes.CDLL) -> None:
     L.lf_forward.restype = ctypes.c_int
     L.lf_forward_stages.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, ctypes.c_size_t, _c_i32, _c_p]
     L.lf_forward_stages.restype = ctypes.c_int
+    L.lf_forward_launch_count.argtypes = [P(Problem), P(PlanInfo)]
+    L.lf_forward_launch_count.restype = ctypes.c_int
     L.lf_backward.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_size_t, _c_p]
     L.lf_backward.restype = ctypes.c_int
     L.lf_forward_noalloc.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p]

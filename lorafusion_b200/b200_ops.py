@@ -272,7 +272,7 @@ def fused_lora_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> tor
     rc = L.lf_forward(ctypes.byref(prob), ctypes.byref(plan.info), plan.table_dev.data_ptr(), y.data_ptr(),
                       ws.data_ptr(), ws.numel(), stream)
     nat.check(rc, "lf_forward")
-    _last_launches = _LAUNCHES["forward"]
+    _last_launches = int(L.lf_forward_launch_count(ctypes.byref(prob), ctypes.byref(plan.info)))
     return y
 
 
@@ -301,6 +301,10 @@ class PreparedForward:
         ws_bytes = L.lf_forward_workspace_bytes(ctypes.byref(self.plan.info), code)
         self.ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=self.device)
         self.prob = _problem(code, self.T, self.K, self.N, self.x, self.w, self.packs)
+
+    def launch_count(self) -> int:
+        """Kernel launches of the default forward (1: shrink co-scheduled in the GEMM launch)."""
+        return int(nat.lib().lf_forward_launch_count(ctypes.byref(self.prob), ctypes.byref(self.plan.info)))
 
     def new_output(self) -> torch.Tensor:
         return torch.empty((self.T, self.N), dtype=self.dtype, device=self.device)

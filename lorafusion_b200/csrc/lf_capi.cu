@@ -3,6 +3,8 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <chrono>
 #include <cstring>
 #include <mutex>
 
@@ -87,6 +89,20 @@ size_t segtile_elems(const lf_plan_info* info) {
 // one S_ext buffer, sized for f32 so the CUDA-core path can use it too, 256-byte multiple
 size_t sext_bytes(const lf_plan_info* info) { return (segtile_elems(info) * 4 + 255) & ~size_t(255); }
 
+// ready flags of the shrink units when the shrink runs inside the GEMM launch
+size_t flag_bytes(const lf_plan_info* info) {
+  return (static_cast<size_t>(info->n_shrink_units) * 8 + 255) & ~size_t(255);
+}
+
+// Per-launch flag value: unique within the process, so flags left in a reused workspace by an
+// earlier launch never read as ready; a stray equal 64-bit value in fresh memory is the only
+// (negligible) collision.
+uint64_t next_generation() {
+  static std::atomic<uint64_t> gen{
+      (static_cast<uint64_t>(std::chrono::steady_clock::now().time_since_epoch().count()) << 1) | 1u};
+  return gen.fetch_add(2, std::memory_order_relaxed) + 2;
+}
+
 int check_problem(const lf_problem* p, const lf_plan_info* info, const int32_t* table_dev) {
   if (!p || !info || (!table_dev && info->table_words > 0)) return LF_ERR_INVALID_ARG;
   if (p->dtype != LF_F32 && p->dtype != LF_BF16 && p->dtype != LF_F16) return LF_ERR_INVALID_ARG;
@@ -128,6 +144,7 @@ Tables make_tables(const lf_plan_info* info, const int32_t* table_dev) {
   t.off_pl_a = info->off_pl_a;
   t.off_pl_b = info->off_pl_b;
   t.off_pl_slot = info->off_pl_slot;
+  t.off_tile_unit = info->off_tile_unit;
   t.n_tiles = info->n_tiles;
   t.n_segtiles = info->n_segtiles;
   t.n_slots = info->n_slots;
@@ -143,12 +160,12 @@ using namespace lf;
 
 extern "C" size_t lf_forward_workspace_bytes(const lf_plan_info* info, int32_t dtype) {
   (void)dtype;
-  return info ? sext_bytes(info) : 0;
+  return info ? sext_bytes(info) + flag_bytes(info) : 0;
 }
 
 extern "C" size_t lf_backward_workspace_bytes(const lf_plan_info* info, int32_t dtype) {
   (void)dtype;
-  return info ? 2 * sext_bytes(info) : 0;
+  return info ? 2 * sext_bytes(info) + flag_bytes(info) : 0;
 }
 
 extern "C" int lf_pack_adapters(int32_t src_dtype, int32_t dst_dtype, const uint64_t* src_ptrs_dev,
@@ -171,7 +188,7 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
   const int T = prob->T, K = prob->K, N = prob->N;
   if (T == 0 || N == 0) return LF_OK;
   if (!prob->x_dev || !prob->w_dev || !prob->a_pack_dev || !prob->b_pack_dev || !y_dev) return LF_ERR_INVALID_ARG;
-  if (workspace_bytes < sext_bytes(info) || (!workspace_dev && sext_bytes(info) > 0)) return LF_ERR_CAPACITY;
+  if (workspace_bytes < lf_forward_workspace_bytes(info, prob->dtype) || !workspace_dev) return LF_ERR_CAPACITY;
   DeviceState* ds = nullptr;
   cudaError_t e = device_state(&ds);
   if (e != cudaSuccess) return LF_ERR_CUDA;
@@ -201,6 +218,18 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
       maps.s = maps.l = maps.p;
     ok = ok && make_map(&maps.o, dt, y_dev, N, T, N * es, 64, 32);
     if (!ok) return LF_ERR_UNSUPPORTED;
+    // Shrink and expand requested together: run the shrink on CTA pairs the GEMM's round count
+    // leaves idle, inside the same launch, when there are enough of them.
+    const int spare = (!single && do_shrink && lora) ? pair_spare_pairs(T, N, ds->num_sms, info->n_shrink_units) : 0;
+    if (spare > 0) {
+      PairShrink sh;
+      sh.a_map = a_map;
+      sh.s_ext = workspace_dev;
+      sh.unit_ready = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace_dev) + sext_bytes(info));
+      sh.gen = next_generation();
+      sh.n_pairs = spare;
+      return to_status(tc_gemm_pair(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st, &sh));
+    }
     if (do_shrink) {
       e = tc_shrink(dt, maps.p, a_map, K, tb, workspace_dev, ds->num_sms, st);
       if (e != cudaSuccess) return LF_ERR_CUDA;
@@ -222,6 +251,17 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
   return to_status(e);
 }
 
+extern "C" int lf_forward_launch_count(const lf_problem* prob, const lf_plan_info* info) {
+  if (!prob || !info) return -LF_ERR_INVALID_ARG;
+  if (prob->T == 0 || prob->N == 0) return 0;
+  DeviceState* ds = nullptr;
+  if (device_state(&ds) != cudaSuccess) return -LF_ERR_CUDA;
+  const bool tc = prob->dtype != LF_F32 && prob->K > 0 && prob->K % 8 == 0 && prob->N % 8 == 0;
+  if (tc && info->n_segtiles > 0 && pair_spare_pairs(prob->T, prob->N, ds->num_sms, info->n_shrink_units) > 0)
+    return 1;
+  return 2;
+}
+
 extern "C" int lf_forward(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, void* y_dev,
                           void* workspace_dev, size_t workspace_bytes, lf_stream_t stream) {
   return lf_forward_stages(prob, info, table_dev, y_dev, workspace_dev, workspace_bytes,
@@ -235,7 +275,7 @@ extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, con
   if (rc != LF_OK) return rc;
   const int T = prob->T, K = prob->K, N = prob->N;
   const size_t sb = sext_bytes(info);
-  if (workspace_bytes < 2 * sb || (!workspace_dev && sb > 0)) return LF_ERR_CAPACITY;
+  if (workspace_bytes < lf_backward_workspace_bytes(info, prob->dtype) || !workspace_dev) return LF_ERR_CAPACITY;
   DeviceState* ds = nullptr;
   cudaError_t e = device_state(&ds);
   if (e != cudaSuccess) return LF_ERR_CUDA;

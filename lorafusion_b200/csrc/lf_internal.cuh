@@ -15,7 +15,7 @@ struct Tables {
   int32_t off_tile_st, off_st_tile, off_st_lo, off_st_hi, off_st_slot, off_st_scale;
   int32_t off_slot_st, off_slot_list, off_slot_rank, off_rank_prefix, off_slot_order;
   int32_t off_unit_tile, off_unit_st0, off_unit_nst;
-  int32_t off_pair_lora, off_pl_a, off_pl_b, off_pl_slot;
+  int32_t off_pair_lora, off_pl_a, off_pl_b, off_pl_slot, off_tile_unit;
   int32_t n_tiles, n_segtiles, n_slots, n_units, r_pad;
   int* err;  // device status word for bounded-wait timeouts
 
@@ -37,6 +37,7 @@ struct Tables {
   __device__ __forceinline__ int32_t pl_a(int i) const { return base[off_pl_a + i]; }
   __device__ __forceinline__ int32_t pl_b(int i) const { return base[off_pl_b + i]; }
   __device__ __forceinline__ int32_t pl_slot(int i) const { return base[off_pl_slot + i]; }
+  __device__ __forceinline__ int32_t tile_unit(int t) const { return base[off_tile_unit + t]; }
 };
 
 Tables make_tables(const lf_plan_info* info, const int32_t* table_dev);
@@ -68,8 +69,19 @@ cudaError_t tc_gemm(int dtype, bool q_mn_major, const TcMaps& maps, int T, int N
                     const Tables& tb, void* out, int64_t ldo, int num_sms, cudaStream_t st);
 // Same product with 256x256 tiles computed by CTA pairs (cta_group::2).  Maps: p box (64,128),
 // q K-major box (64,128) / MN-major box (64,64), s box (r_pad,128), l box (r_pad,128).
+// Optional routed shrink run by spare CTA pairs of the same launch (S_ext = s.P.A_slot^T).
+struct PairShrink {
+  CUtensorMap a_map;     // packed A slab [n_slots*r_pad, Kred] box (64, r_pad)
+  void* s_ext;           // written by the launch
+  uint64_t* unit_ready;  // [n_units] ready flags
+  uint64_t gen;          // value the flags take in this launch
+  int n_pairs;           // CTA pairs given to the shrink
+};
+// CTA pairs the pair GEMM can leave to a co-scheduled shrink without adding a round (0: none).
+int pair_spare_pairs(int T, int Nout, int num_sms, int n_units);
 cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, int Nout, int Kred, bool lora,
-                         const Tables& tb, void* out, int64_t ldo, int num_sms, cudaStream_t st);
+                         const Tables& tb, void* out, int64_t ldo, int num_sms, cudaStream_t st,
+                         const PairShrink* shrink = nullptr);
 cudaError_t tc_gram(int dtype, const CUtensorMap& d_map, const CUtensorMap& s_map, int C, const Tables& tb,
                     void* out, int transpose_out, int num_sms, cudaStream_t st);
 

@@ -16,6 +16,7 @@ enum DeviceErr : int {
   kErrTimeoutEmpty = 0x102,   // producer waited too long for a free stage
   kErrTimeoutAcc = 0x103,     // waits on the accumulator hand-off
   kErrTimeoutDrain = 0x104,
+  kErrTimeoutFlag = 0x105,    // waited too long for another CTA's ready flag
 };
 
 // ~1 s of wall time: far above any legitimate wait in these kernels.
@@ -91,6 +92,25 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       return false;
     }
   }
+}
+
+// ---------------------------------------------------------------- inter-CTA flags
+__device__ __forceinline__ uint64_t ld_acquire_u64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_u64(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Orders this thread's generic-proxy view of global memory before its later async-proxy (TMA)
+// accesses, after it has synchronized with a writer.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Barrier among `count` threads (multiple of 32) of this CTA on hardware barrier `id` (1..15).
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // ---------------------------------------------------------------- fences

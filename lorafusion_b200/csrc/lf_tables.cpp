@@ -29,7 +29,7 @@ extern "C" int32_t lf_plan_table_words(int32_t n_routes, int32_t total_rows, int
   const int64_t n_st = static_cast<int64_t>(n_routes) + n_tiles;
   const int64_t n_pairs = (n_tiles + 1) / 2;
   const int64_t words = (n_tiles + 1) + 6 * n_st + (n_slots + 1) + n_st + n_slots + (n_slots + 1) + n_slots +
-                        3 * n_st + (n_pairs + 1) + 3 * n_st + 16;
+                        3 * n_st + (n_pairs + 1) + 3 * n_st + (n_tiles + 1) + 16;
   return words > 0x7fffffff ? -1 : static_cast<int32_t>(words);
 }
 
@@ -100,8 +100,9 @@ extern "C" int lf_plan_tables(const int32_t* route_start, const int32_t* route_e
 
   // shrink units: runs of consecutive segment tiles of one row tile, N = run * r_pad <= 64
   const int32_t group = std::max(1, 64 / r_pad);
-  std::vector<int32_t> u_tile, u_st0, u_nst;
+  std::vector<int32_t> u_tile, u_st0, u_nst, tile_unit(n_tiles + 1, 0);
   for (int32_t t = 0; t < n_tiles; ++t) {
+    tile_unit[t] = static_cast<int32_t>(u_tile.size());
     for (int32_t j = tile_first[t]; j < tile_first[t + 1]; j += group) {
       u_tile.push_back(t);
       u_st0.push_back(j);
@@ -109,6 +110,7 @@ extern "C" int lf_plan_tables(const int32_t* route_start, const int32_t* route_e
     }
   }
   const int32_t n_units = static_cast<int32_t>(u_tile.size());
+  tile_unit[n_tiles] = n_units;
 
   // pair LoRA stages: segment tiles of row tiles 2p and 2p+1 matched by slot, in row order
   const int32_t n_pairs = (n_tiles + 1) / 2;
@@ -166,6 +168,7 @@ extern "C" int lf_plan_tables(const int32_t* route_start, const int32_t* route_e
   info->off_pl_a = take(n_pl);
   info->off_pl_b = take(n_pl);
   info->off_pl_slot = take(n_pl);
+  info->off_tile_unit = take(n_tiles + 1);
   if (w > table_capacity) return LF_ERR_CAPACITY;
 
   auto put = [&](int32_t off, const std::vector<int32_t>& v) {
@@ -193,6 +196,7 @@ extern "C" int lf_plan_tables(const int32_t* route_start, const int32_t* route_e
   put(info->off_pl_a, pl_a);
   put(info->off_pl_b, pl_b);
   put(info->off_pl_slot, pl_slot);
+  put(info->off_tile_unit, tile_unit);
   info->n_pair_lora = n_pl;
 
   info->total_rows = total_rows;

@@ -362,6 +362,13 @@ struct PairParams {
   int lora, r_pad;
   uint32_t idesc_main, idesc_lora;
   uint32_t lora_layout, lora_sbo;
+  // co-scheduled shrink: the first 2*n_shrink_pairs CTAs compute S_ext (P . A_slot^T) and publish
+  // one ready flag per shrink unit; 0 = S_ext was produced by an earlier launch
+  int n_shrink_pairs;
+  int ab_fmt;
+  void* s_ext;
+  uint64_t* unit_ready;
+  uint64_t gen;
   Tables tb;
 };
 
@@ -375,11 +382,225 @@ __device__ __forceinline__ void pair_raster(int t, const PairParams& p, int& mp,
   n = r / gsize;
 }
 
+// Bounded wait until ready[u] == gen for every u in [u0, u1) (acquire).
+__device__ __forceinline__ bool wait_units_ready(const uint64_t* ready, int u0, int u1, uint64_t gen,
+                                                 volatile int* abort_flag, int* err) {
+  for (int u = u0; u < u1; ++u) {
+    if (ld_acquire_u64(ready + u) == gen) continue;
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_u64(ready + u) != gen) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+        record_error(err, kErrTimeoutFlag);
+        *abort_flag = 1;
+        return false;
+      }
+      __nanosleep(200);
+    }
+  }
+  return true;
+}
+
+// Shrink role of the co-scheduled pair kernel, run by CTAs [0, 2*n_shrink_pairs): whole shrink
+// units (row tile, <= 64/r_pad segment tiles, full K) on single CTAs, S written straight from TMEM
+// (scaled, masked per segment, bf16/f16), then the unit's ready flag is released.  The epilogue
+// warps of CTA 0 also write the all-zero block before releasing unit 0.
+template <typename OutT>
+__device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CUtensorMap& map_p,
+                                                 const CUtensorMap& map_a, uint8_t* sA, uint8_t* sB, uint64_t* full,
+                                                 uint64_t* empty, uint64_t* tfull, uint64_t* tempty, uint64_t* drain,
+                                                 uint64_t* pub, uint32_t* tmem_slot, volatile int* abort_flag) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Tables& tb = prm.tb;
+  const int me = static_cast<int>(blockIdx.x), n_me = 2 * prm.n_shrink_pairs;
+  const int r_pad = prm.r_pad;
+  const int nkb = (prm.Kred + kBK - 1) / kBK;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(drain, 1);
+    mbar_init(pub, 4);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&map_p);
+    tma_prefetch_desc(&map_a);
+  }
+  if (warp == 1) {
+    __syncwarp();
+    tmem_alloc(tmem_slot, 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, issued_mask = 0, last_parity = 0;
+      bool ok = true;
+      for (int u = me; u < tb.n_units && ok; u += n_me) {
+        const int tile = tb.unit_tile(u), st0 = tb.unit_st0(u), nst = tb.unit_nst(u);
+        int arow[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) arow[j] = j < nst ? tb.st_slot(st0 + j) * r_pad : 0;
+        const uint32_t bytes = static_cast<uint32_t>(kPairABytes + nst * r_pad * kBK * 2);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, tb.err, kErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], bytes);
+          tma_load_2d(sA + stage * kPairABytes, &map_p, &full[stage], kb * kBK, tile * kBM);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (j < nst)
+              tma_load_2d(sB + stage * kPairBBytes + j * r_pad * (kBK * 2), &map_a, &full[stage], kb * kBK, arow[j]);
+          issued_mask |= 1u << stage;
+          last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok)
+        for (int s = 0; s < kPairStages; ++s)
+          if (issued_mask & (1u << s)) drain_wait(&full[s], (last_parity >> s) & 1u, tb.err);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true, issued_any = false;
+      const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
+      int it = 0;
+      for (int u = me; u < tb.n_units && ok; u += n_me, ++it) {
+        const int N = tb.unit_nst(u) * r_pad;
+        const uint32_t idesc = umma_idesc_f16(kBM, N, prm.ab_fmt, 0, 0);
+        const int buf = it & 1;
+        if (!mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1, abort_flag, tb.err, kErrTimeoutAcc)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * 64);
+        uint32_t acc = 0;
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, tb.err, kErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = a_base + stage * kPairABytes, b0 = b_base + stage * kPairBBytes;
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            umma_f16(d, umma_sdesc(a0 + k * 32, 16, 1024, 2), umma_sdesc(b0 + k * 32, 16, 1024, 2), idesc, acc);
+            acc = 1;
+          }
+          issued_any = true;
+          umma_commit(&empty[stage]);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[buf]);
+      }
+      if (!ok && issued_any) {  // wait for in-flight MMAs before TMEM is released
+        umma_commit(drain);
+        drain_wait(drain, 0, tb.err);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    OutT* s_ext = reinterpret_cast<OutT*>(prm.s_ext);
+    if (me == 0)  // the all-zero segment tile, published with unit 0
+      for (int e = threadIdx.x - 64; e < kBM * r_pad; e += 128)
+        s_ext[static_cast<int64_t>(tb.n_segtiles) * kBM * r_pad + e] = cvt_out<OutT>(0.f);
+    int it = 0;
+    for (int u = me; u < tb.n_units; u += n_me, ++it) {
+      const int st0 = tb.unit_st0(u), nst = tb.unit_nst(u);
+      int lo[4], hi[4];
+      float sc[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int st = st0 + min(j, nst - 1);
+        lo[j] = tb.st_lo(st);
+        hi[j] = tb.st_hi(st);
+        sc[j] = tb.st_scale(st);
+      }
+      const int buf = it & 1;
+      if (!warp_wait(&tfull[buf], (it >> 1) & 1, abort_flag, tb.err, kErrTimeoutAcc)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * 64);
+      for (int j = 0; j < nst; ++j) {
+        const bool in = row >= (j == 0 ? lo[0] : j == 1 ? lo[1] : j == 2 ? lo[2] : lo[3]) &&
+                        row < (j == 0 ? hi[0] : j == 1 ? hi[1] : j == 2 ? hi[2] : hi[3]);
+        const float scale = j == 0 ? sc[0] : j == 1 ? sc[1] : j == 2 ? sc[2] : sc[3];
+        OutT* dst = s_ext + (static_cast<int64_t>(st0 + j) * kBM + row) * r_pad;
+        for (int c = 0; c < r_pad; c += 16) {
+          uint32_t v[16];
+          tmem_ld16(tbase + j * r_pad + c, v);
+          tmem_wait_ld();
+          uint4 pk[2];
+          uint32_t* w32 = reinterpret_cast<uint32_t*>(pk);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            w32[e] = pack2<OutT>(in ? scale * __uint_as_float(v[2 * e]) : 0.f,
+                                 in ? scale * __uint_as_float(v[2 * e + 1]) : 0.f);
+          *reinterpret_cast<uint4*>(dst + c) = pk[0];
+          *reinterpret_cast<uint4*>(dst + c + 8) = pk[1];
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[buf]);
+      // publish: each warp orders its stores, then thread 64 sees all four warps and releases
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pub);
+      if (warp == 2) {
+        int ok = 1;
+        if (lane == 0) {
+          ok = mbar_wait(pub, static_cast<uint32_t>(it) & 1u, abort_flag, tb.err, kErrTimeoutAcc) ? 1 : 0;
+          if (ok) {
+            __threadfence();
+            fence_proxy_async_global();
+            st_release_u64(prm.unit_ready + u, prm.gen);
+          }
+        }
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 128);
+  }
+}
+
 template <bool kQMN, typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_q,
                         const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_l,
-                        const __grid_constant__ CUtensorMap map_o, const PairParams prm) {
+                        const __grid_constant__ CUtensorMap map_o, const __grid_constant__ CUtensorMap map_a,
+                        const PairParams prm) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -390,13 +611,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tfull = empty + kPairStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* pub = drain + 1;  // shrink role: all epilogue warps finished writing a unit
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pub + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (static_cast<int>(blockIdx.x) < 2 * prm.n_shrink_pairs) {
+    pair_shrink_role<OutT>(prm, map_p, map_a, sA, sB, full, empty, tfull, tempty, drain, pub, tmem_slot,
+                           abort_flag);
+    return;
+  }
   const uint32_t crank = cluster_ctarank();  // 0: issues the MMAs
-  const int pair = static_cast<int>(blockIdx.x >> 1);
-  const int n_pairs = static_cast<int>(gridDim.x >> 1);
+  const int pair = static_cast<int>(blockIdx.x >> 1) - prm.n_shrink_pairs;
+  const int n_pairs = static_cast<int>(gridDim.x >> 1) - prm.n_shrink_pairs;
   const int total = prm.n_mpairs * prm.n_ntiles;
   const int nkb = (prm.Kred + kBK - 1) / kBK;
   const Tables& tb = prm.tb;
@@ -480,6 +707,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (!ok || !prm.lora) continue;
+        if (prm.n_shrink_pairs > 0 && pe > pb) {  // S_ext of both row tiles (and the zero block) published?
+          const int u0 = tb.tile_unit(2 * mp), u1 = tb.tile_unit(min(2 * mp + 2, tb.n_tiles));
+          if (!wait_units_ready(prm.unit_ready, 0, 1, prm.gen, abort_flag, tb.err) ||
+              !wait_units_ready(prm.unit_ready, u0, u1, prm.gen, abort_flag, tb.err)) {
+            ok = false;
+            break;
+          }
+          fence_proxy_async_global();
+        }
         for (int i = pb; i < pe; ++i) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, tb.err, kErrTimeoutEmpty)) {
             ok = false;
@@ -1161,8 +1397,20 @@ cudaError_t tc_gemm(int dtype, bool q_mn_major, const TcMaps& maps, int T, int N
   return cudaGetLastError();
 }
 
+int pair_spare_pairs(int T, int Nout, int num_sms, int n_units) {
+  const int n_mtiles = (T + kBM - 1) / kBM;
+  const int total = ((n_mtiles + 1) / 2) * ((Nout + 255) / 256);
+  const int pairs = num_sms / 2;
+  if (total == 0 || n_units == 0) return 0;
+  const int rounds = (total + pairs - 1) / pairs;
+  const int gemm_pairs = (total + rounds - 1) / rounds;
+  const int spare = pairs - gemm_pairs;
+  return spare >= 4 ? spare : 0;  // below 8 SMs the shrink would hold up the first round
+}
+
 cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, int Nout, int Kred, bool lora,
-                         const Tables& tb, void* out, int64_t ldo, int num_sms, cudaStream_t st) {
+                         const Tables& tb, void* out, int64_t ldo, int num_sms, cudaStream_t st,
+                         const PairShrink* shrink) {
   PairParams p{};
   p.out = out;
   p.ldo = ldo;
@@ -1176,6 +1424,7 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
   p.lora = lora ? 1 : 0;
   p.r_pad = tb.r_pad;
   const int fmt = dtype == LF_BF16 ? 1 : 0;
+  p.ab_fmt = fmt;
   p.idesc_main = umma_idesc_f16(256, 256, fmt, 0, q_mn_major ? 1 : 0);
   p.idesc_lora = umma_idesc_f16(256, 256, fmt, 0, 0);
   p.lora_layout = umma_layout_for_span(tb.r_pad * 2);
@@ -1183,24 +1432,38 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
   p.tb = tb;
   const int total = p.n_mpairs * p.n_ntiles;
   if (total == 0) return cudaSuccess;
-  const int pairs = total < num_sms / 2 ? total : num_sms / 2;
+  const int all_pairs = num_sms / 2;
+  int gemm_pairs = total < all_pairs ? total : all_pairs;
+  const CUtensorMap* a_map = &maps.p;  // unused unless a shrink is co-scheduled
+  if (shrink != nullptr && shrink->n_pairs > 0) {
+    p.n_shrink_pairs = shrink->n_pairs;
+    p.s_ext = shrink->s_ext;
+    p.unit_ready = shrink->unit_ready;
+    p.gen = shrink->gen;
+    a_map = &shrink->a_map;
+    const int rounds = (total + all_pairs - 1) / all_pairs;
+    gemm_pairs = (total + rounds - 1) / rounds;
+  }
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(2 * pairs);
+  cfg.gridDim = dim3(2 * (gemm_pairs + p.n_shrink_pairs));
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kPairSmem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // GEMM pairs wait on the shrink CTAs' flags: all CTAs must be resident at once
+  attr[1].id = cudaLaunchAttributeCooperative;
+  attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = p.n_shrink_pairs > 0 ? 2 : 1;
   cudaError_t e;
 #define LF_LAUNCH_PAIR(QMN, OT)                                                                  \
   e = ensure_smem(tc_gemm_pair_kernel<QMN, OT>, kPairSmem);                                     \
   if (e != cudaSuccess) return e;                                                               \
-  e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<QMN, OT>, maps.p, maps.q, maps.s, maps.l, maps.o, p);
+  e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<QMN, OT>, maps.p, maps.q, maps.s, maps.l, maps.o, *a_map, p);
   if (dtype == LF_BF16) {
     if (q_mn_major) {
       LF_LAUNCH_PAIR(true, __nv_bfloat16)
