@@ -86,12 +86,13 @@ size_t segtile_elems(const lf_plan_info* info) {
   return static_cast<size_t>(info->n_segtiles + 1) * LF_TILE_ROWS * static_cast<size_t>(info->r_pad);
 }
 
-// one S_ext buffer, sized for f32 so the CUDA-core path can use it too, 256-byte multiple
+// one S_ext buffer, 256-byte multiple: f32 for the CUDA-core path, or two bf16/f16 planes (the
+// K-half partial products of the co-scheduled shrink) for the tensor-core path
 size_t sext_bytes(const lf_plan_info* info) { return (segtile_elems(info) * 4 + 255) & ~size_t(255); }
 
-// ready flags of the shrink units when the shrink runs inside the GEMM launch
+// ready flags of the (unit, K half) items when the shrink runs inside the GEMM launch
 size_t flag_bytes(const lf_plan_info* info) {
-  return (static_cast<size_t>(info->n_shrink_units) * 8 + 255) & ~size_t(255);
+  return (static_cast<size_t>(info->n_shrink_units) * 2 * 8 + 255) & ~size_t(255);
 }
 
 // Per-launch flag value: unique within the process, so flags left in a reused workspace by an
@@ -207,7 +208,7 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
     TcMaps maps;
     CUtensorMap a_map;
     const size_t es = 2;
-    const uint64_t s_rows = static_cast<uint64_t>(info->n_segtiles + 1) * LF_TILE_ROWS;
+    const uint64_t s_rows = 2 * static_cast<uint64_t>(info->n_segtiles + 1) * LF_TILE_ROWS;  // two planes
     bool ok = make_map(&maps.p, dt, prob->x_dev, K, T, K * es, 64, 128) &&
               make_map(&maps.q, dt, prob->w_dev, K, N, K * es, 64, nbox) &&
               make_map(&a_map, dt, prob->a_pack_dev, K, static_cast<uint64_t>(info->n_slots) * rp, K * es, 64, rp);

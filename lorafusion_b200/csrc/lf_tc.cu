@@ -352,7 +352,14 @@ constexpr int kPairStages = 6;
 constexpr int kPairABytes = kBM * kBK * 2;   // 16 KB: this CTA's 128 rows of P
 constexpr int kPairBBytes = 128 * kBK * 2;   // 16 KB: this CTA's 128-row half of Q
 constexpr int kPairOutBytes = 4 * 2 * 32 * 64 * 2;  // epilogue staging: 4 warps x 2 buffers x (32 rows x 64 cols)
-constexpr int kPairSmem = 1024 + kPairStages * (kPairABytes + kPairBBytes) + kPairOutBytes + 256;
+// The shrink role lays the same shared memory out as deeper stages of one x tile (16 KB) plus
+// <= 64 rows of packed A (8 KB): more bytes in flight per SM while it competes with the GEMM.
+constexpr int kRoleStageBytes = kPairABytes + 64 * kBK * 2;
+constexpr int kRoleStages = 9;
+constexpr int kPairBars = kRoleStages;  // barrier array length shared by both roles
+static_assert(kRoleStages * kRoleStageBytes <= kPairStages * (kPairABytes + kPairBBytes) + kPairOutBytes,
+              "shrink-role stages must fit the pair kernel's shared memory");
+constexpr int kPairSmem = 1024 + kPairStages * (kPairABytes + kPairBBytes) + kPairOutBytes + 384;
 
 struct PairParams {
   void* out;
@@ -367,8 +374,11 @@ struct PairParams {
   int n_shrink_pairs;
   int ab_fmt;
   void* s_ext;
-  uint64_t* unit_ready;
+  uint64_t* unit_ready;  // one flag per (unit, K half) item
   uint64_t gen;
+  // S_ext planes the LoRA stages sum: 1 = the full product; 2 = two K-half partial products
+  // (written by the co-scheduled shrink), plane p starting at S map row p * s_plane_rows
+  int s_planes, s_plane_rows;
   Tables tb;
 };
 
@@ -415,8 +425,11 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
   const int me = static_cast<int>(blockIdx.x), n_me = 2 * prm.n_shrink_pairs;
   const int r_pad = prm.r_pad;
   const int nkb = (prm.Kred + kBK - 1) / kBK;
+  const int nkb_half = (nkb + 1) / 2;
+  const int n_items = 2 * tb.n_units;  // item = (unit, K half): half h covers k-blocks [h*nkb_half, ...)
+  const int64_t plane_elems = static_cast<int64_t>(prm.s_plane_rows) * r_pad;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kPairStages; ++s) {
+    for (int s = 0; s < kRoleStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -447,33 +460,36 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
       int stage = 0;
       uint32_t phase = 0, issued_mask = 0, last_parity = 0;
       bool ok = true;
-      for (int u = me; u < tb.n_units && ok; u += n_me) {
+      for (int item = me; item < n_items && ok; item += n_me) {
+        const int u = item >> 1, h = item & 1;
         const int tile = tb.unit_tile(u), st0 = tb.unit_st0(u), nst = tb.unit_nst(u);
         int arow[4];
 #pragma unroll
         for (int j = 0; j < 4; ++j) arow[j] = j < nst ? tb.st_slot(st0 + j) * r_pad : 0;
         const uint32_t bytes = static_cast<uint32_t>(kPairABytes + nst * r_pad * kBK * 2);
-        for (int kb = 0; kb < nkb; ++kb) {
+        const int kb_end = min(nkb, (h + 1) * nkb_half);
+        for (int kb = h * nkb_half; kb < kb_end; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, tb.err, kErrTimeoutEmpty)) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&full[stage], bytes);
-          tma_load_2d(sA + stage * kPairABytes, &map_p, &full[stage], kb * kBK, tile * kBM);
+          uint8_t* sx = sA + stage * kRoleStageBytes;
+          tma_load_2d(sx, &map_p, &full[stage], kb * kBK, tile * kBM);
 #pragma unroll
           for (int j = 0; j < 4; ++j)
             if (j < nst)
-              tma_load_2d(sB + stage * kPairBBytes + j * r_pad * (kBK * 2), &map_a, &full[stage], kb * kBK, arow[j]);
+              tma_load_2d(sx + kPairABytes + j * r_pad * (kBK * 2), &map_a, &full[stage], kb * kBK, arow[j]);
           issued_mask |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == kPairStages) {
+          if (++stage == kRoleStages) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
       if (!ok)
-        for (int s = 0; s < kPairStages; ++s)
+        for (int s = 0; s < kRoleStages; ++s)
           if (issued_mask & (1u << s)) drain_wait(&full[s], (last_parity >> s) & 1u, tb.err);
     }
     __syncwarp();
@@ -482,9 +498,10 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true, issued_any = false;
-      const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
+      const uint32_t a_base = smem_u32(sA);
       int it = 0;
-      for (int u = me; u < tb.n_units && ok; u += n_me, ++it) {
+      for (int item = me; item < n_items && ok; item += n_me, ++it) {
+        const int u = item >> 1, h = item & 1;
         const int N = tb.unit_nst(u) * r_pad;
         const uint32_t idesc = umma_idesc_f16(kBM, N, prm.ab_fmt, 0, 0);
         const int buf = it & 1;
@@ -495,13 +512,14 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(buf * 64);
         uint32_t acc = 0;
-        for (int kb = 0; kb < nkb; ++kb) {
+        const int kb_end = min(nkb, (h + 1) * nkb_half);
+        for (int kb = h * nkb_half; kb < kb_end; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, tb.err, kErrTimeoutFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = a_base + stage * kPairABytes, b0 = b_base + stage * kPairBBytes;
+          const uint32_t a0 = a_base + stage * kRoleStageBytes, b0 = a0 + kPairABytes;
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             umma_f16(d, umma_sdesc(a0 + k * 32, 16, 1024, 2), umma_sdesc(b0 + k * 32, 16, 1024, 2), idesc, acc);
@@ -509,7 +527,7 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
           }
           issued_any = true;
           umma_commit(&empty[stage]);
-          if (++stage == kPairStages) {
+          if (++stage == kRoleStages) {
             stage = 0;
             phase ^= 1;
           }
@@ -527,11 +545,15 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
     const int q = warp & 3;
     const int row = q * 32 + lane;
     OutT* s_ext = reinterpret_cast<OutT*>(prm.s_ext);
-    if (me == 0)  // the all-zero segment tile, published with unit 0
-      for (int e = threadIdx.x - 64; e < kBM * r_pad; e += 128)
+    if (me == 0)  // the all-zero segment tile of both planes, published with item 0
+      for (int e = threadIdx.x - 64; e < kBM * r_pad; e += 128) {
         s_ext[static_cast<int64_t>(tb.n_segtiles) * kBM * r_pad + e] = cvt_out<OutT>(0.f);
+        s_ext[plane_elems + static_cast<int64_t>(tb.n_segtiles) * kBM * r_pad + e] = cvt_out<OutT>(0.f);
+      }
     int it = 0;
-    for (int u = me; u < tb.n_units; u += n_me, ++it) {
+    for (int item = me; item < n_items; item += n_me, ++it) {
+      const int u = item >> 1, h = item & 1;
+      const bool has_k = h * nkb_half < nkb;  // an empty K half contributes zeros
       const int st0 = tb.unit_st0(u), nst = tb.unit_nst(u);
       int lo[4], hi[4];
       float sc[4];
@@ -547,10 +569,10 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * 64);
       for (int j = 0; j < nst; ++j) {
-        const bool in = row >= (j == 0 ? lo[0] : j == 1 ? lo[1] : j == 2 ? lo[2] : lo[3]) &&
+        const bool in = has_k && row >= (j == 0 ? lo[0] : j == 1 ? lo[1] : j == 2 ? lo[2] : lo[3]) &&
                         row < (j == 0 ? hi[0] : j == 1 ? hi[1] : j == 2 ? hi[2] : hi[3]);
         const float scale = j == 0 ? sc[0] : j == 1 ? sc[1] : j == 2 ? sc[2] : sc[3];
-        OutT* dst = s_ext + (static_cast<int64_t>(st0 + j) * kBM + row) * r_pad;
+        OutT* dst = s_ext + h * plane_elems + (static_cast<int64_t>(st0 + j) * kBM + row) * r_pad;
         for (int c = 0; c < r_pad; c += 16) {
           uint32_t v[16];
           tmem_ld16(tbase + j * r_pad + c, v);
@@ -578,7 +600,7 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
           if (ok) {
             __threadfence();
             fence_proxy_async_global();
-            st_release_u64(prm.unit_ready + u, prm.gen);
+            st_release_u64(prm.unit_ready + item, prm.gen);
           }
         }
         if (!__shfl_sync(0xffffffffu, ok, 0)) break;
@@ -607,8 +629,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sB = smem + kPairStages * kPairABytes;
   uint8_t* sOut = sB + kPairStages * kPairBBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(sOut + kPairOutBytes);
-  uint64_t* empty = full + kPairStages;
-  uint64_t* tfull = empty + kPairStages;
+  uint64_t* empty = full + kPairBars;
+  uint64_t* tfull = empty + kPairBars;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint64_t* pub = drain + 1;  // shrink role: all epilogue warps finished writing a unit
@@ -674,6 +696,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int mtile = 2 * mp + static_cast<int>(crank);
         int pb = 0, pe = 0, sl[4] = {0, 0, 0, 0}, ss[4] = {0, 0, 0, 0};
         const int32_t* st_of = tb.base + (crank ? tb.off_pl_b : tb.off_pl_a);
+        // ready flags this tile's LoRA stages need, read early (relaxed) while the k-loop runs
+        int it0 = 0, it1 = 0;
+        uint64_t fl[9];
+        if (prm.lora && prm.n_shrink_pairs > 0) {
+          it0 = 2 * ld_early(tb.base + tb.off_tile_unit + 2 * mp);
+          it1 = 2 * ld_early(tb.base + tb.off_tile_unit + min(2 * mp + 2, tb.n_tiles));
+          fl[0] = ld_relaxed_u64(prm.unit_ready);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) fl[q + 1] = it0 + q < it1 ? ld_relaxed_u64(prm.unit_ready + it0 + q) : prm.gen;
+        }
         if (prm.lora) {  // fetched while the k-loop runs
           pb = ld_early(tb.base + tb.off_pair_lora + mp);
           pe = ld_early(tb.base + tb.off_pair_lora + mp + 1);
@@ -708,25 +740,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok || !prm.lora) continue;
         if (prm.n_shrink_pairs > 0 && pe > pb) {  // S_ext of both row tiles (and the zero block) published?
-          const int u0 = tb.tile_unit(2 * mp), u1 = tb.tile_unit(min(2 * mp + 2, tb.n_tiles));
-          if (!wait_units_ready(prm.unit_ready, 0, 1, prm.gen, abort_flag, tb.err) ||
-              !wait_units_ready(prm.unit_ready, u0, u1, prm.gen, abort_flag, tb.err)) {
+          bool seen = it1 - it0 <= 8;
+#pragma unroll
+          for (int q = 0; q < 9; ++q) seen = seen && fl[q] == prm.gen;
+          if (seen) {
+            fence_acquire_gpu();  // the early loads saw every release: acquire them
+          } else if (!wait_units_ready(prm.unit_ready, 0, 1, prm.gen, abort_flag, tb.err) ||
+                     !wait_units_ready(prm.unit_ready, it0, it1, prm.gen, abort_flag, tb.err)) {
             ok = false;
             break;
           }
           fence_proxy_async_global();
         }
-        for (int i = pb; i < pe; ++i) {
+        for (int i = pb; i < pe && ok; ++i) {
+          const int q = i - pb;
+          const int slot = q == 0 ? sl[0] : q == 1 ? sl[1] : q == 2 ? sl[2] : q == 3 ? sl[3] : tb.pl_slot(i);
+          const int st = q == 0 ? ss[0] : q == 1 ? ss[1] : q == 2 ? ss[2] : q == 3 ? ss[3] : st_of[i];
+          for (int pl = 0; pl < prm.s_planes; ++pl) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, tb.err, kErrTimeoutEmpty)) {
             ok = false;
             break;
           }
-          const int q = i - pb;
-          const int slot = q == 0 ? sl[0] : q == 1 ? sl[1] : q == 2 ? sl[2] : q == 3 ? sl[3] : tb.pl_slot(i);
-          const int st = q == 0 ? ss[0] : q == 1 ? ss[1] : q == 2 ? ss[2] : q == 3 ? ss[3] : st_of[i];
           if (crank == 0) mbar_arrive_expect_tx(&full[stage], lora_bytes);
           const uint32_t fb = full_lead + static_cast<uint32_t>(stage * 8);
-          tma_load_2d_pair(sA + stage * kPairABytes, &map_s, fb, 0, st * kBM);
+          tma_load_2d_pair(sA + stage * kPairABytes, &map_s, fb, 0, pl * prm.s_plane_rows + st * kBM);
           tma_load_2d_pair(sB + stage * kPairBBytes, &map_l, fb, 0,
                            slot * prm.Nout + n * 256 + static_cast<int>(crank) * 128);
           issued_mask |= 1u << stage;
@@ -734,6 +771,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (++stage == kPairStages) {
             stage = 0;
             phase ^= 1;
+          }
           }
         }
       }
@@ -756,7 +794,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         pair_raster(t, prm, mp, n);
         const int buf = it & 1;
         int n_lora = 0;
-        if (prm.lora) n_lora = ld_early(tb.base + tb.off_pair_lora + mp + 1) - ld_early(tb.base + tb.off_pair_lora + mp);
+        if (prm.lora)
+          n_lora = (ld_early(tb.base + tb.off_pair_lora + mp + 1) - ld_early(tb.base + tb.off_pair_lora + mp)) *
+                   prm.s_planes;
         if (!mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1, abort_flag, tb.err, kErrTimeoutAcc)) {
           ok = false;
           break;
@@ -1420,11 +1460,13 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
   const int n_mtiles = (T + kBM - 1) / kBM;
   p.n_mpairs = (n_mtiles + 1) / 2;
   p.n_ntiles = (Nout + 255) / 256;
-  p.group_m = 8;
+  p.group_m = 4;  // the first round touches few row tiles: their shrink units are ready first
   p.lora = lora ? 1 : 0;
   p.r_pad = tb.r_pad;
   const int fmt = dtype == LF_BF16 ? 1 : 0;
   p.ab_fmt = fmt;
+  p.s_planes = 1;
+  p.s_plane_rows = (tb.n_segtiles + 1) * kBM;
   p.idesc_main = umma_idesc_f16(256, 256, fmt, 0, q_mn_major ? 1 : 0);
   p.idesc_lora = umma_idesc_f16(256, 256, fmt, 0, 0);
   p.lora_layout = umma_layout_for_span(tb.r_pad * 2);
@@ -1437,6 +1479,7 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
   const CUtensorMap* a_map = &maps.p;  // unused unless a shrink is co-scheduled
   if (shrink != nullptr && shrink->n_pairs > 0) {
     p.n_shrink_pairs = shrink->n_pairs;
+    p.s_planes = 2;
     p.s_ext = shrink->s_ext;
     p.unit_ready = shrink->unit_ready;
     p.gen = shrink->gen;
