@@ -8,10 +8,12 @@ the op needs to run one process per GPU:
   bins and routes, bit for bit.
 * :func:`assign_bins` gives each rank whole bins.  Runs of consecutive
   single-adapter bins form bundles so an adapter's rows stay on one rank where
-  possible; bundles larger than a rank's share are cut; bundles go to ranks by
-  longest-processing-time (largest first, to the least-loaded rank, lowest
-  rank on ties).  Deterministic, so every rank computes the same assignment
-  without communicating.
+  possible; bundles larger than a rank's share are cut.  Every rank gets a
+  capacity of its even share rounded up to whole 256-row tile pairs; bundles,
+  largest first, go to the rank they fit best (a bundle that fits nowhere is
+  placed bin by bin, and a bin that fits nowhere goes to the least-loaded
+  rank).  Deterministic, so every rank computes the same assignment without
+  communicating.
 * :func:`local_layout` turns a rank's bins into its own fused row ranges and a
   rebased :class:`TileRoutingConfig`.
 * The forward needs no communication (base weight replicated, adapters
@@ -27,6 +29,8 @@ from dataclasses import dataclass
 import torch
 
 from lorafusion_b200.config import TileRoute, TileRoutingConfig
+
+TILE_PAIR_ROWS = 256  # rows of one CTA-pair tile of the fused GEMM
 
 
 @dataclass(frozen=True)
@@ -76,15 +80,33 @@ def assign_bins(bins: list[list[tuple[int, int]]], world_size: int) -> ShardPlan
         starts.append((cur, cur + r))
         cur += r
     share = max(1, -(-cur // world_size))
+    # Each rank's capacity is its share rounded up to whole 256-row tile pairs (the fused GEMM's
+    # row granularity), so an even split costs no extra, mostly empty, row of tiles.
+    cap = -(-share // TILE_PAIR_ROWS) * TILE_PAIR_ROWS
     bundles = _bundles(bins, share)
     order = sorted(range(len(bundles)), key=lambda i: -sum(rows[b] for b in bundles[i]))
     load = [0] * world_size
     bin_rank = [0] * len(bins)
-    for i in order:
-        r = min(range(world_size), key=lambda k: (load[k], k))
-        for b in bundles[i]:
+
+    def place(members: list[int]) -> bool:
+        n = sum(rows[b] for b in members)
+        fits = [k for k in range(world_size) if load[k] + n <= cap]
+        if not fits:
+            return False
+        r = min(fits, key=lambda k: (cap - load[k] - n, k))  # best fit
+        for b in members:
             bin_rank[b] = r
-        load[r] += sum(rows[b] for b in bundles[i])
+        load[r] += n
+        return True
+
+    for i in order:
+        if place(bundles[i]):
+            continue
+        for b in sorted(bundles[i], key=lambda b: (-rows[b], b)):  # split the bundle into its bins
+            if not place([b]):
+                r = min(range(world_size), key=lambda k: (load[k], k))
+                bin_rank[b] = r
+                load[r] += rows[b]
     owners: dict[int, set[int]] = {}
     for b, entries in enumerate(bins):
         for a, n in entries:
