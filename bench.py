@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-fwd-bwd", action="store_true")
+    ap.add_argument("--separate-launches", action="store_true",
+                    help="shrink and fused GEMM as two ordinary launches (profilers refuse the cooperative one)")
     return ap.parse_args()
 
 
@@ -287,6 +289,8 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    if args.separate_launches:
+        b200_ops.use_cooperative_launch(False)
     wl = WORKLOADS[args.workload]
     pr = local_problem(wl, world, rank, device)
     T, K, N = pr["T"], pr["K"], pr["N"]
@@ -310,10 +314,12 @@ def run_ours(args):
         barrier()
         return [[ev[i][j].elapsed_time(ev[i][j + 1]) for j in range(n_events - 1)] for i in range(steps)]
 
+    default_stages = SH | EX | (nat.LF_STAGE_SEPARATE if args.separate_launches else 0)
+
     def fwd_default(ev):
         if ev:
             ev[0].record()
-        prep.launch(y, SH | EX)
+        prep.launch(y, default_stages)
         if ev:
             ev[1].record()
 
@@ -327,11 +333,11 @@ def run_ours(args):
         if ev:
             ev[2].record()
 
-    n_launch = prep.launch_count()
     sampler = ClockSampler(local_rank)
     sampler.start()
     t = timed(fwd_default, args.steps, args.warmup, 2)
     clocks = sampler.stop()
+    n_launch = 2 if args.separate_launches else prep.launch_count()  # reflects the path actually taken
     step_local_ms = statistics.mean(s[0] for s in t)
     step_ms = rank_max(step_local_ms)
     value = pr["global_T"] / (step_ms / 1e3)
@@ -397,7 +403,10 @@ def run_ours(args):
         dom_flops, dom_ms = counts["gemm_flops"], gemm_ms
     gemm_tflops = dom_flops / (dom_ms / 1e3) / 1e12
     shrink_gbs = counts["shrink_bytes"] / (shrink_ms / 1e3) / 1e9
-    traffic = load_traffic("tc_gemm_pair_kernel", args.workload)
+    # ncu cannot capture the co-scheduled (cooperative) launch; its DRAM traffic is unmeasured and
+    # the two-launch path's capture of the fused GEMM is reported beside it
+    pair_traffic = load_traffic("tc_gemm_pair_kernel", args.workload)
+    traffic = pair_traffic if n_launch == 2 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -421,7 +430,8 @@ def run_ours(args):
                          "achieved": gemm_tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": gemm_tflops / peaks["bf16_tflops"], "traffic": traffic,
                          "peak_source": f"{peaks['source']} bf16 dense (burst)",
-                         "flops_per_launch": dom_flops, "ms_per_launch": dom_ms, "launches_per_step": n_launch},
+                         "flops_per_launch": dom_flops, "ms_per_launch": dom_ms, "launches_per_step": n_launch,
+                         "traffic_two_launch_gemm": pair_traffic},
             "split_launches": {"shrink_ms": shrink_ms, "gemm_ms": gemm_ms, "total_ms": shrink_ms + gemm_ms},
             "shrink_roofline": {"kernel": "tc_shrink_kernel (standalone launch)", "bound": "hbm", "achieved": shrink_gbs,
                                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": shrink_gbs / peaks["hbm_gbs"],

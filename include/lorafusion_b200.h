@@ -156,6 +156,9 @@ LF_API int lf_forward(const lf_problem* prob, const lf_plan_info* info, const in
  *   LF_STAGE_BASE     base GEMM only, y = x W^T (the "LoRA disabled" yardstick)
  *   LF_STAGE_SINGLE_CTA  with EXPAND or BASE: use 128x256 tiles on single CTAs instead of the
  *                     default 256x256 tiles on CTA pairs (bf16/f16 only; for comparisons)
+ *   LF_STAGE_SEPARATE with SHRINK|EXPAND: run them as two ordinary launches instead of one
+ *                     cooperative launch (for profilers and SM-partitioned GPUs, which refuse
+ *                     cooperative launches)
  * lf_forward == lf_forward_stages(..., LF_STAGE_SHRINK | LF_STAGE_EXPAND).
  * Has no counterpart in the reference (its forward is one call per route).
  */
@@ -163,6 +166,7 @@ LF_API int lf_forward(const lf_problem* prob, const lf_plan_info* info, const in
 #define LF_STAGE_EXPAND 2
 #define LF_STAGE_BASE 4
 #define LF_STAGE_SINGLE_CTA 8
+#define LF_STAGE_SEPARATE 16
 LF_API int lf_forward_stages(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, void* y_dev,
                              void* workspace_dev, size_t workspace_bytes, int32_t stages, lf_stream_t stream);
 

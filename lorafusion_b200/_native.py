@@ -25,7 +25,7 @@ LF_ERR_CAPACITY = 5
 LF_ERR_DEVICE = 6
 
 LF_F32, LF_BF16, LF_F16 = 0, 1, 2
-LF_STAGE_SHRINK, LF_STAGE_EXPAND, LF_STAGE_BASE, LF_STAGE_SINGLE_CTA = 1, 2, 4, 8
+LF_STAGE_SHRINK, LF_STAGE_EXPAND, LF_STAGE_BASE, LF_STAGE_SINGLE_CTA, LF_STAGE_SEPARATE = 1, 2, 4, 8, 16
 TILE_ROWS = 128
 
 _c_i32 = ctypes.c_int32

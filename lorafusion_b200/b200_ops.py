@@ -31,7 +31,7 @@ from lorafusion_b200 import _native as nat
 _DTYPE_CODE = {torch.float32: nat.LF_F32, torch.bfloat16: nat.LF_BF16, torch.float16: nat.LF_F16}
 
 __all__ = ["fused_lora_forward", "fused_lora_backward", "prepare_forward", "PreparedForward", "clear_weight_cache",
-           "last_launch_count"]
+           "last_launch_count", "use_cooperative_launch"]
 
 
 # --------------------------------------------------------------------------- caches
@@ -42,6 +42,18 @@ _WEIGHT_CACHE: dict[tuple, tuple] = {}
 _CACHE_MAX = 256
 _LAUNCHES = {"forward": 2, "backward": 5}
 _last_launches = 0
+_COOPERATIVE = True
+
+
+def use_cooperative_launch(enabled: bool) -> None:
+    """Allow (default) or forbid the single cooperative launch of the forward.
+
+    When allowed, the routed shrink runs inside the fused GEMM launch on CTA pairs the GEMM
+    leaves idle.  Profilers and SM-partitioned GPUs refuse cooperative launches; forbid it
+    there and the forward runs as two ordinary launches.
+    """
+    global _COOPERATIVE
+    _COOPERATIVE = bool(enabled)
 
 
 def clear_weight_cache() -> None:
@@ -269,10 +281,12 @@ def fused_lora_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> tor
     ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=device)
     prob = _problem(code, T, K, N, x, w, packs)
     stream = torch.cuda.current_stream(device).cuda_stream
-    rc = L.lf_forward(ctypes.byref(prob), ctypes.byref(plan.info), plan.table_dev.data_ptr(), y.data_ptr(),
-                      ws.data_ptr(), ws.numel(), stream)
+    stages = nat.LF_STAGE_SHRINK | nat.LF_STAGE_EXPAND | (0 if _COOPERATIVE else nat.LF_STAGE_SEPARATE)
+    rc = L.lf_forward_stages(ctypes.byref(prob), ctypes.byref(plan.info), plan.table_dev.data_ptr(), y.data_ptr(),
+                             ws.data_ptr(), ws.numel(), stages, stream)
     nat.check(rc, "lf_forward")
-    _last_launches = int(L.lf_forward_launch_count(ctypes.byref(prob), ctypes.byref(plan.info)))
+    _last_launches = int(L.lf_forward_launch_count(ctypes.byref(prob), ctypes.byref(plan.info))) \
+        if _COOPERATIVE else 2
     return y
 
 

@@ -24,7 +24,8 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 struct DeviceState {
   bool ready = false;
   int num_sms = 0;
-  int* status = nullptr;  // address of g_device_status on this device
+  int* status = nullptr;      // address of g_device_status on this device
+  bool no_cosched = false;    // the co-scheduled (cooperative) launch was refused here once
 };
 
 std::mutex g_mu;
@@ -185,7 +186,7 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
                                  lf_stream_t stream) {
   int rc = check_problem(prob, info, table_dev);
   if (rc != LF_OK) return rc;
-  if (stages <= 0 || stages > 15 || ((stages & LF_STAGE_EXPAND) && (stages & LF_STAGE_BASE))) return LF_ERR_INVALID_ARG;
+  if (stages <= 0 || stages > 31 || ((stages & LF_STAGE_EXPAND) && (stages & LF_STAGE_BASE))) return LF_ERR_INVALID_ARG;
   const int T = prob->T, K = prob->K, N = prob->N;
   if (T == 0 || N == 0) return LF_OK;
   if (!prob->x_dev || !prob->w_dev || !prob->a_pack_dev || !prob->b_pack_dev || !y_dev) return LF_ERR_INVALID_ARG;
@@ -221,7 +222,10 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
     if (!ok) return LF_ERR_UNSUPPORTED;
     // Shrink and expand requested together: run the shrink on CTA pairs the GEMM's round count
     // leaves idle, inside the same launch, when there are enough of them.
-    const int spare = (!single && do_shrink && lora) ? pair_spare_pairs(T, N, ds->num_sms, info->n_shrink_units) : 0;
+    const bool separate = (stages & LF_STAGE_SEPARATE) != 0;
+    const int spare = (!single && !separate && do_shrink && lora && !ds->no_cosched)
+                          ? pair_spare_pairs(T, N, ds->num_sms, info->n_shrink_units)
+                          : 0;
     if (spare > 0) {
       PairShrink sh;
       sh.a_map = a_map;
@@ -229,7 +233,12 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
       sh.unit_ready = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace_dev) + sext_bytes(info));
       sh.gen = next_generation();
       sh.n_pairs = spare;
-      return to_status(tc_gemm_pair(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st, &sh));
+      e = tc_gemm_pair(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st, &sh);
+      if (e == cudaSuccess) return LF_OK;
+      // The cooperative launch was refused (e.g. other work holds SMs, or a profiler
+      // serializes launches): nothing ran; use the two-launch path from now on.
+      (void)cudaGetLastError();
+      ds->no_cosched = true;
     }
     if (do_shrink) {
       e = tc_shrink(dt, maps.p, a_map, K, tb, workspace_dev, ds->num_sms, st);
@@ -258,7 +267,8 @@ extern "C" int lf_forward_launch_count(const lf_problem* prob, const lf_plan_inf
   DeviceState* ds = nullptr;
   if (device_state(&ds) != cudaSuccess) return -LF_ERR_CUDA;
   const bool tc = prob->dtype != LF_F32 && prob->K > 0 && prob->K % 8 == 0 && prob->N % 8 == 0;
-  if (tc && info->n_segtiles > 0 && pair_spare_pairs(prob->T, prob->N, ds->num_sms, info->n_shrink_units) > 0)
+  if (tc && info->n_segtiles > 0 && !ds->no_cosched &&
+      pair_spare_pairs(prob->T, prob->N, ds->num_sms, info->n_shrink_units) > 0)
     return 1;
   return 2;
 }
