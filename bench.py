@@ -337,7 +337,7 @@ def run_ours(args):
     sampler.start()
     t = timed(fwd_default, args.steps, args.warmup, 2)
     clocks = sampler.stop()
-    n_launch = 2 if args.separate_launches else prep.launch_count()  # reflects the path actually taken
+    n_launch = prep.launch_count()  # reflects the path actually taken (co-scheduling switch included)
     step_local_ms = statistics.mean(s[0] for s in t)
     step_ms = rank_max(step_local_ms)
     value = pr["global_T"] / (step_ms / 1e3)
@@ -389,7 +389,9 @@ def run_ours(args):
 
         tfb = timed(fb, max(5, args.steps // 2), 2, 2)
         fb_ms = rank_max(statistics.mean(s[0] for s in tfb))
+        bwd_launches = b200_ops.last_launch_count()
         fwd_bwd = {"value": pr["global_T"] / (fb_ms / 1e3), "unit": "tokens/s", "ms_per_step": fb_ms,
+                   "launches_per_step": n_launch + bwd_launches,
                    "tflops": counts["fwdbwd_flops"] * world / (fb_ms / 1e3) / 1e12,
                    "spanning_adapters": len(pr["plan"].spanning)}
 

@@ -178,6 +178,23 @@ LF_API int lf_forward_stages(const lf_problem* prob, const lf_plan_info* info, c
 LF_API int lf_forward_launch_count(const lf_problem* prob, const lf_plan_info* info);
 
 /*
+ * Kernel launches lf_backward makes for this problem on the current device: 3 when both routed
+ * shrinks run on CTA pairs the grad_x GEMM leaves idle (GEMM + two grams), 5 when they run as
+ * launches of their own, 1 with no routed rows.  Negative lf_status on bad arguments.
+ * No counterpart in the reference.
+ */
+LF_API int lf_backward_launch_count(const lf_problem* prob, const lf_plan_info* info);
+
+/*
+ * Process-wide switch for the co-scheduled launches (default on): with 0, lf_forward and
+ * lf_backward run each routed shrink as an ordinary launch of its own instead of inside the
+ * GEMM's cooperative launch.  For profilers and SM-partitioned GPUs, which refuse cooperative
+ * launches (a refused launch also turns co-scheduling off for that device by itself).
+ * No counterpart in the reference.
+ */
+LF_API int lf_set_co_scheduling(int32_t enable);
+
+/*
  * Backward: grad_x [T,K]; grad_a = concatenated [r_s, K] blocks and grad_b = concatenated
  * [N, r_s] blocks, slot after slot (slot s starts at rank_prefix[s]*K and rank_prefix[s]*N).
  * Replaces triton_ops.fused_lora_backward (triton_ops.py:412-468) and

@@ -74,6 +74,10 @@ def _declare(L: ctypes.CDLL) -> None:
     L.lf_forward_stages.restype = ctypes.c_int
     L.lf_forward_launch_count.argtypes = [P(Problem), P(PlanInfo)]
     L.lf_forward_launch_count.restype = ctypes.c_int
+    L.lf_backward_launch_count.argtypes = [P(Problem), P(PlanInfo)]
+    L.lf_backward_launch_count.restype = ctypes.c_int
+    L.lf_set_co_scheduling.argtypes = [_c_i32]
+    L.lf_set_co_scheduling.restype = ctypes.c_int
     L.lf_backward.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_size_t, _c_p]
     L.lf_backward.restype = ctypes.c_int
     L.lf_forward_noalloc.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p]

@@ -40,20 +40,18 @@ _PLAN_CACHE: dict[tuple, "_Plan"] = {}
 _PACK_CACHE: dict[tuple, dict] = {}
 _WEIGHT_CACHE: dict[tuple, tuple] = {}
 _CACHE_MAX = 256
-_LAUNCHES = {"forward": 2, "backward": 5}
 _last_launches = 0
-_COOPERATIVE = True
 
 
 def use_cooperative_launch(enabled: bool) -> None:
-    """Allow (default) or forbid the single cooperative launch of the forward.
+    """Allow (default) or forbid the co-scheduled cooperative launches (process-wide).
 
-    When allowed, the routed shrink runs inside the fused GEMM launch on CTA pairs the GEMM
-    leaves idle.  Profilers and SM-partitioned GPUs refuse cooperative launches; forbid it
-    there and the forward runs as two ordinary launches.
+    When allowed, the routed shrinks run inside the GEMM's launch on CTA pairs the GEMM
+    leaves idle (forward: 1 launch; backward: 3).  Profilers and SM-partitioned GPUs refuse
+    cooperative launches; forbid them there and every shrink runs as a launch of its own
+    (forward: 2 launches; backward: 5).
     """
-    global _COOPERATIVE
-    _COOPERATIVE = bool(enabled)
+    nat.check(nat.lib().lf_set_co_scheduling(1 if enabled else 0), "lf_set_co_scheduling")
 
 
 def clear_weight_cache() -> None:
@@ -281,12 +279,10 @@ def fused_lora_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> tor
     ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=device)
     prob = _problem(code, T, K, N, x, w, packs)
     stream = torch.cuda.current_stream(device).cuda_stream
-    stages = nat.LF_STAGE_SHRINK | nat.LF_STAGE_EXPAND | (0 if _COOPERATIVE else nat.LF_STAGE_SEPARATE)
-    rc = L.lf_forward_stages(ctypes.byref(prob), ctypes.byref(plan.info), plan.table_dev.data_ptr(), y.data_ptr(),
-                             ws.data_ptr(), ws.numel(), stages, stream)
+    rc = L.lf_forward(ctypes.byref(prob), ctypes.byref(plan.info), plan.table_dev.data_ptr(), y.data_ptr(),
+                      ws.data_ptr(), ws.numel(), stream)
     nat.check(rc, "lf_forward")
-    _last_launches = int(L.lf_forward_launch_count(ctypes.byref(prob), ctypes.byref(plan.info))) \
-        if _COOPERATIVE else 2
+    _last_launches = int(L.lf_forward_launch_count(ctypes.byref(prob), ctypes.byref(plan.info)))
     return y
 
 
@@ -377,7 +373,7 @@ def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, rout
     rc = L.lf_backward(ctypes.byref(prob), ctypes.byref(info), plan.table_dev.data_ptr(), g.data_ptr(),
                        grad_x.data_ptr(), ga_flat.data_ptr(), gb_flat.data_ptr(), ws.data_ptr(), ws.numel(), stream)
     nat.check(rc, "lf_backward")
-    _last_launches = _LAUNCHES["backward"] if T > 0 else 0
+    _last_launches = max(0, int(L.lf_backward_launch_count(ctypes.byref(prob), ctypes.byref(info))))
     grad_a: dict[int, torch.Tensor] = {}
     grad_b: dict[int, torch.Tensor] = {}
     off = 0

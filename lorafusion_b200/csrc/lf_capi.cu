@@ -6,6 +6,7 @@
 #include <atomic>
 #include <chrono>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 
 #include "lf_internal.cuh"
@@ -30,6 +31,9 @@ struct DeviceState {
 
 std::mutex g_mu;
 DeviceState g_dev[64];
+std::atomic<bool> g_cosched_enabled{true};  // process-wide switch (lf_set_co_scheduling)
+
+bool cosched_allowed(const DeviceState* ds) { return !ds->no_cosched && g_cosched_enabled.load(); }
 EncodeTiledFn g_encode = nullptr;
 
 int elem_bytes(int dtype) { return dtype == LF_F32 ? 4 : 2; }
@@ -91,9 +95,10 @@ size_t segtile_elems(const lf_plan_info* info) {
 // K-half partial products of the co-scheduled shrink) for the tensor-core path
 size_t sext_bytes(const lf_plan_info* info) { return (segtile_elems(info) * 4 + 255) & ~size_t(255); }
 
-// ready flags of the (unit, K half) items when the shrink runs inside the GEMM launch
-size_t flag_bytes(const lf_plan_info* info) {
-  return (static_cast<size_t>(info->n_shrink_units) * 2 * 8 + 255) & ~size_t(255);
+// ready flags of the (job, unit, K half) items when shrinks run inside the GEMM launch
+// (one job in the forward, two in the backward)
+size_t flag_bytes(const lf_plan_info* info, int jobs = 1) {
+  return (static_cast<size_t>(info->n_shrink_units) * 2 * 8 * jobs + 255) & ~size_t(255);
 }
 
 // Per-launch flag value: unique within the process, so flags left in a reused workspace by an
@@ -167,7 +172,7 @@ extern "C" size_t lf_forward_workspace_bytes(const lf_plan_info* info, int32_t d
 
 extern "C" size_t lf_backward_workspace_bytes(const lf_plan_info* info, int32_t dtype) {
   (void)dtype;
-  return info ? 2 * sext_bytes(info) + flag_bytes(info) : 0;
+  return info ? 2 * sext_bytes(info) + flag_bytes(info, 2) : 0;
 }
 
 extern "C" int lf_pack_adapters(int32_t src_dtype, int32_t dst_dtype, const uint64_t* src_ptrs_dev,
@@ -223,11 +228,11 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
     // Shrink and expand requested together: run the shrink on CTA pairs the GEMM's round count
     // leaves idle, inside the same launch, when there are enough of them.
     const bool separate = (stages & LF_STAGE_SEPARATE) != 0;
-    const int spare = (!single && !separate && do_shrink && lora && !ds->no_cosched)
+    const int spare = (!single && !separate && do_shrink && lora && cosched_allowed(ds))
                           ? pair_spare_pairs(T, N, ds->num_sms, info->n_shrink_units)
                           : 0;
     if (spare > 0) {
-      PairShrink sh;
+      PairShrink sh{};
       sh.a_map = a_map;
       sh.s_ext = workspace_dev;
       sh.unit_ready = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace_dev) + sext_bytes(info));
@@ -267,10 +272,27 @@ extern "C" int lf_forward_launch_count(const lf_problem* prob, const lf_plan_inf
   DeviceState* ds = nullptr;
   if (device_state(&ds) != cudaSuccess) return -LF_ERR_CUDA;
   const bool tc = prob->dtype != LF_F32 && prob->K > 0 && prob->K % 8 == 0 && prob->N % 8 == 0;
-  if (tc && info->n_segtiles > 0 && !ds->no_cosched &&
+  if (tc && info->n_segtiles > 0 && cosched_allowed(ds) &&
       pair_spare_pairs(prob->T, prob->N, ds->num_sms, info->n_shrink_units) > 0)
     return 1;
   return 2;
+}
+
+extern "C" int lf_backward_launch_count(const lf_problem* prob, const lf_plan_info* info) {
+  if (!prob || !info) return -LF_ERR_INVALID_ARG;
+  if (prob->T == 0) return 0;
+  DeviceState* ds = nullptr;
+  if (device_state(&ds) != cudaSuccess) return -LF_ERR_CUDA;
+  const bool tc = prob->dtype != LF_F32 && prob->K > 0 && prob->K % 8 == 0 && prob->N % 8 == 0;
+  const bool lora = info->n_segtiles > 0 && info->n_slots > 0;
+  if (!tc) return 5;
+  if (!lora) return 1;
+  return (cosched_allowed(ds) && pair_spare_pairs(prob->T, prob->K, ds->num_sms, info->n_shrink_units) > 0) ? 3 : 5;
+}
+
+extern "C" int lf_set_co_scheduling(int32_t enable) {
+  g_cosched_enabled.store(enable != 0);
+  return LF_OK;
 }
 
 extern "C" int lf_forward(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, void* y_dev,
@@ -314,6 +336,7 @@ extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, con
                          grad_out_dev, grad_x_dev, workspace_dev})) {
     CUtensorMap p_x, p_g, a_map, bt_map, sf_map, sb_map;
     TcMaps dx;
+    const uint64_t s_rows = 2 * static_cast<uint64_t>(info->n_segtiles + 1) * LF_TILE_ROWS;  // two planes
     bool ok = make_map(&p_x, dt, prob->x_dev, K, T, K * es, 64, 128) &&
               make_map(&p_g, dt, grad_out_dev, N, T, N * es, 64, 128) &&
               make_map(&dx.q, dt, prob->w_dev, K, N, K * es, 64, 64);
@@ -322,27 +345,57 @@ extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, con
       ok = ok &&
            make_map(&a_map, dt, prob->a_pack_dev, K, static_cast<uint64_t>(info->n_slots) * rp, K * es, 64, rp) &&
            make_map(&bt_map, dt, prob->bt_pack_dev, N, static_cast<uint64_t>(info->n_slots) * rp, N * es, 64, rp) &&
-           make_map(&sf_map, dt, s_f, rp, static_cast<uint64_t>(info->n_segtiles + 1) * LF_TILE_ROWS, rp * es, rp, 128) &&
-           make_map(&sb_map, dt, s_b, rp, static_cast<uint64_t>(info->n_segtiles + 1) * LF_TILE_ROWS, rp * es, rp, 128) &&
+           make_map(&sf_map, dt, s_f, rp, s_rows, rp * es, rp, 128) &&
+           make_map(&sb_map, dt, s_b, rp, s_rows, rp * es, rp, 128) &&
            make_map(&dx.l, dt, prob->at_pack_dev, rp, static_cast<uint64_t>(info->n_slots) * K, rp * es, rp, 128);
     ok = ok && make_map(&dx.o, dt, grad_x_dev, K, T, K * es, 64, 32);
     if (!ok) return LF_ERR_UNSUPPORTED;
     dx.p = p_g;
+    int planes = 1;  // S_ext planes the grams sum
+    bool gemm_done = false;
     if (lora) {
       dx.s = sb_map;
-      e = tc_shrink(dt, p_x, a_map, K, tb, s_f, ds->num_sms, st);
-      if (e != cudaSuccess) return LF_ERR_CUDA;
-      e = tc_shrink(dt, p_g, bt_map, N, tb, s_b, ds->num_sms, st);
-      if (e != cudaSuccess) return LF_ERR_CUDA;
+      // Both shrinks inside the dX GEMM launch, on CTA pairs its round count leaves idle:
+      // job 1 = S_b (g . B_i, needed by the dX tiles), job 2 = S_f (x . A_i^T, read by the dB gram).
+      const int spare = cosched_allowed(ds) ? pair_spare_pairs(T, K, ds->num_sms, info->n_shrink_units) : 0;
+      if (spare > 0) {
+        PairShrink sh{};
+        sh.a_map = bt_map;
+        sh.s_ext = s_b;
+        sh.unit_ready = reinterpret_cast<uint64_t*>(ws + 2 * sb);
+        sh.gen = next_generation();
+        sh.n_pairs = spare;
+        sh.job2 = true;
+        sh.p2_map = p_x;
+        sh.a2_map = a_map;
+        sh.s_ext2 = s_f;
+        sh.K2 = K;
+        e = tc_gemm_pair(dt, true, dx, T, K, N, lora, tb, grad_x_dev, K, ds->num_sms, st, &sh);
+        if (e == cudaSuccess) {
+          planes = 2;
+          gemm_done = true;
+        } else {
+          (void)cudaGetLastError();  // cooperative launch refused: nothing ran
+          ds->no_cosched = true;
+        }
+      }
+      if (!gemm_done) {
+        e = tc_shrink(dt, p_x, a_map, K, tb, s_f, ds->num_sms, st);
+        if (e != cudaSuccess) return LF_ERR_CUDA;
+        e = tc_shrink(dt, p_g, bt_map, N, tb, s_b, ds->num_sms, st);
+        if (e != cudaSuccess) return LF_ERR_CUDA;
+      }
     } else {
       dx.s = dx.l = p_g;
     }
-    e = tc_gemm_pair(dt, true, dx, T, K, N, lora, tb, grad_x_dev, K, ds->num_sms, st);
-    if (e != cudaSuccess) return LF_ERR_CUDA;
-    if (lora) {
-      e = tc_gram(dt, p_g, sf_map, N, tb, grad_b_dev, 0, ds->num_sms, st);
+    if (!gemm_done) {
+      e = tc_gemm_pair(dt, true, dx, T, K, N, lora, tb, grad_x_dev, K, ds->num_sms, st);
       if (e != cudaSuccess) return LF_ERR_CUDA;
-      e = tc_gram(dt, p_x, sb_map, K, tb, grad_a_dev, 1, ds->num_sms, st);
+    }
+    if (lora) {
+      e = tc_gram(dt, p_g, sf_map, N, tb, grad_b_dev, 0, ds->num_sms, st, planes);
+      if (e != cudaSuccess) return LF_ERR_CUDA;
+      e = tc_gram(dt, p_x, sb_map, K, tb, grad_a_dev, 1, ds->num_sms, st, planes);
       if (e != cudaSuccess) return LF_ERR_CUDA;
     }
     return LF_OK;

@@ -70,20 +70,29 @@ cudaError_t tc_gemm(int dtype, bool q_mn_major, const TcMaps& maps, int T, int N
 // Same product with 256x256 tiles computed by CTA pairs (cta_group::2).  Maps: p box (64,128),
 // q K-major box (64,128) / MN-major box (64,64), s box (r_pad,128), l box (r_pad,128).
 // Optional routed shrink run by spare CTA pairs of the same launch (S_ext = s.P.A_slot^T).
+// The GEMM's own LoRA operand comes from the first job (P = the GEMM's P); an optional second
+// job (its own P, slab and K) is computed afterwards for a later launch (the backward's x.A^T).
 struct PairShrink {
-  CUtensorMap a_map;     // packed A slab [n_slots*r_pad, Kred] box (64, r_pad)
-  void* s_ext;           // written by the launch
-  uint64_t* unit_ready;  // [n_units] ready flags
+  CUtensorMap a_map;     // packed slab [n_slots*r_pad, Kred] box (64, r_pad), job 1
+  void* s_ext;           // two K-half planes written by the launch, job 1
+  uint64_t* unit_ready;  // [2*n_units] ready flags of job 1 (then [2*n_units] of job 2)
   uint64_t gen;          // value the flags take in this launch
   int n_pairs;           // CTA pairs given to the shrink
+  bool job2;             // second job present
+  CUtensorMap p2_map;    // job 2 activations [T, K2] box (64, 128)
+  CUtensorMap a2_map;    // job 2 slab [n_slots*r_pad, K2] box (64, r_pad)
+  void* s_ext2;
+  int K2;
 };
 // CTA pairs the pair GEMM can leave to a co-scheduled shrink without adding a round (0: none).
 int pair_spare_pairs(int T, int Nout, int num_sms, int n_units);
 cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, int Nout, int Kred, bool lora,
                          const Tables& tb, void* out, int64_t ldo, int num_sms, cudaStream_t st,
                          const PairShrink* shrink = nullptr);
+// planes: S_ext planes to sum (1, or 2 when the K-half partial products of the co-scheduled
+// shrink are read); s_map must then cover both planes.
 cudaError_t tc_gram(int dtype, const CUtensorMap& d_map, const CUtensorMap& s_map, int C, const Tables& tb,
-                    void* out, int transpose_out, int num_sms, cudaStream_t st);
+                    void* out, int transpose_out, int num_sms, cudaStream_t st, int planes = 1);
 
 // --------------------------------------------------------------- packing
 cudaError_t pack_adapters(int src_dtype, int dst_dtype, const uint64_t* src_ptrs, const int32_t* ranks,

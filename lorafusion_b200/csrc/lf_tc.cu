@@ -29,7 +29,7 @@ constexpr int kThreads = 192;
 constexpr int kGemmBN = 256;
 constexpr int kGemmStages = 4;
 constexpr int kShrStages = 8;
-constexpr int kGramStages = 4;
+constexpr int kGramStages = 3;
 
 template <typename OutT>
 __device__ __forceinline__ uint32_t pack2(float a, float b);
@@ -379,6 +379,9 @@ struct PairParams {
   // S_ext planes the LoRA stages sum: 1 = the full product; 2 = two K-half partial products
   // (written by the co-scheduled shrink), plane p starting at S map row p * s_plane_rows
   int s_planes, s_plane_rows;
+  // optional second shrink job (own activations/slab/K), items after the first job's
+  int job2, Kred2;
+  void* s_ext2;
   Tables tb;
 };
 
@@ -417,17 +420,18 @@ __device__ __forceinline__ bool wait_units_ready(const uint64_t* ready, int u0, 
 // warps of CTA 0 also write the all-zero block before releasing unit 0.
 template <typename OutT>
 __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CUtensorMap& map_p,
-                                                 const CUtensorMap& map_a, uint8_t* sA, uint8_t* sB, uint64_t* full,
+                                                 const CUtensorMap& map_a, const CUtensorMap& map_p2,
+                                                 const CUtensorMap& map_a2, uint8_t* sA, uint8_t* sB, uint64_t* full,
                                                  uint64_t* empty, uint64_t* tfull, uint64_t* tempty, uint64_t* drain,
                                                  uint64_t* pub, uint32_t* tmem_slot, volatile int* abort_flag) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Tables& tb = prm.tb;
   const int me = static_cast<int>(blockIdx.x), n_me = 2 * prm.n_shrink_pairs;
   const int r_pad = prm.r_pad;
-  const int nkb = (prm.Kred + kBK - 1) / kBK;
-  const int nkb_half = (nkb + 1) / 2;
-  const int n_items = 2 * tb.n_units;  // item = (unit, K half): half h covers k-blocks [h*nkb_half, ...)
+  // item = (job, unit, K half): half h of a job covers its k-blocks [h*half, min(nkb, (h+1)*half))
+  const int n_items = (prm.job2 ? 4 : 2) * tb.n_units;
   const int64_t plane_elems = static_cast<int64_t>(prm.s_plane_rows) * r_pad;
+  auto job_nkb = [&](int job) { return ((job ? prm.Kred2 : prm.Kred) + kBK - 1) / kBK; };
   if (threadIdx.x == 0) {
     for (int s = 0; s < kRoleStages; ++s) {
       mbar_init(&full[s], 1);
@@ -443,6 +447,10 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
     fence_mbar_init();
     tma_prefetch_desc(&map_p);
     tma_prefetch_desc(&map_a);
+    if (prm.job2) {
+      tma_prefetch_desc(&map_p2);
+      tma_prefetch_desc(&map_a2);
+    }
   }
   if (warp == 1) {
     __syncwarp();
@@ -461,7 +469,11 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
       uint32_t phase = 0, issued_mask = 0, last_parity = 0;
       bool ok = true;
       for (int item = me; item < n_items && ok; item += n_me) {
-        const int u = item >> 1, h = item & 1;
+        const int job = item >= 2 * tb.n_units ? 1 : 0;
+        const int u = (item - job * 2 * tb.n_units) >> 1, h = item & 1;
+        const CUtensorMap* mp = job ? &map_p2 : &map_p;
+        const CUtensorMap* ma = job ? &map_a2 : &map_a;
+        const int nkb = job_nkb(job), nkb_half = (nkb + 1) / 2;
         const int tile = tb.unit_tile(u), st0 = tb.unit_st0(u), nst = tb.unit_nst(u);
         int arow[4];
 #pragma unroll
@@ -475,11 +487,11 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
           }
           mbar_arrive_expect_tx(&full[stage], bytes);
           uint8_t* sx = sA + stage * kRoleStageBytes;
-          tma_load_2d(sx, &map_p, &full[stage], kb * kBK, tile * kBM);
+          tma_load_2d(sx, mp, &full[stage], kb * kBK, tile * kBM);
 #pragma unroll
           for (int j = 0; j < 4; ++j)
             if (j < nst)
-              tma_load_2d(sx + kPairABytes + j * r_pad * (kBK * 2), &map_a, &full[stage], kb * kBK, arow[j]);
+              tma_load_2d(sx + kPairABytes + j * r_pad * (kBK * 2), ma, &full[stage], kb * kBK, arow[j]);
           issued_mask |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == kRoleStages) {
@@ -501,7 +513,9 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
       const uint32_t a_base = smem_u32(sA);
       int it = 0;
       for (int item = me; item < n_items && ok; item += n_me, ++it) {
-        const int u = item >> 1, h = item & 1;
+        const int job = item >= 2 * tb.n_units ? 1 : 0;
+        const int u = (item - job * 2 * tb.n_units) >> 1, h = item & 1;
+        const int nkb = job_nkb(job), nkb_half = (nkb + 1) / 2;
         const int N = tb.unit_nst(u) * r_pad;
         const uint32_t idesc = umma_idesc_f16(kBM, N, prm.ab_fmt, 0, 0);
         const int buf = it & 1;
@@ -552,8 +566,11 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
       }
     int it = 0;
     for (int item = me; item < n_items; item += n_me, ++it) {
-      const int u = item >> 1, h = item & 1;
+      const int job = item >= 2 * tb.n_units ? 1 : 0;
+      const int u = (item - job * 2 * tb.n_units) >> 1, h = item & 1;
+      const int nkb = job_nkb(job), nkb_half = (nkb + 1) / 2;
       const bool has_k = h * nkb_half < nkb;  // an empty K half contributes zeros
+      OutT* s_out = reinterpret_cast<OutT*>(job ? prm.s_ext2 : prm.s_ext);
       const int st0 = tb.unit_st0(u), nst = tb.unit_nst(u);
       int lo[4], hi[4];
       float sc[4];
@@ -572,7 +589,7 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
         const bool in = has_k && row >= (j == 0 ? lo[0] : j == 1 ? lo[1] : j == 2 ? lo[2] : lo[3]) &&
                         row < (j == 0 ? hi[0] : j == 1 ? hi[1] : j == 2 ? hi[2] : hi[3]);
         const float scale = j == 0 ? sc[0] : j == 1 ? sc[1] : j == 2 ? sc[2] : sc[3];
-        OutT* dst = s_ext + h * plane_elems + (static_cast<int64_t>(st0 + j) * kBM + row) * r_pad;
+        OutT* dst = s_out + h * plane_elems + (static_cast<int64_t>(st0 + j) * kBM + row) * r_pad;
         for (int c = 0; c < r_pad; c += 16) {
           uint32_t v[16];
           tmem_ld16(tbase + j * r_pad + c, v);
@@ -622,6 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap map_p, const __grid_constant__ CUtensorMap map_q,
                         const __grid_constant__ CUtensorMap map_s, const __grid_constant__ CUtensorMap map_l,
                         const __grid_constant__ CUtensorMap map_o, const __grid_constant__ CUtensorMap map_a,
+                        const __grid_constant__ CUtensorMap map_p2, const __grid_constant__ CUtensorMap map_a2,
                         const PairParams prm) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -639,8 +657,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (static_cast<int>(blockIdx.x) < 2 * prm.n_shrink_pairs) {
-    pair_shrink_role<OutT>(prm, map_p, map_a, sA, sB, full, empty, tfull, tempty, drain, pub, tmem_slot,
-                           abort_flag);
+    pair_shrink_role<OutT>(prm, map_p, map_a, map_p2, map_a2, sA, sB, full, empty, tfull, tempty, drain, pub,
+                           tmem_slot, abort_flag);
     return;
   }
   const uint32_t crank = cluster_ctarank();  // 0: issues the MMAs
@@ -1131,6 +1149,7 @@ struct GramParams {
   int C;
   int n_cblk;
   int transpose_out;
+  int planes, s_plane_rows;  // S_ext planes summed (2: K-half partial products)
   int r_pad;
   uint32_t idesc;
   uint32_t s_layout, s_sbo, s_kstep;
@@ -1138,7 +1157,7 @@ struct GramParams {
 };
 
 constexpr int kGramDBytes = kBM * 128 * 2;  // 128 rows x 128 columns
-constexpr int kGramSBytes = kBM * 64 * 2;   // 128 rows x r_pad (<= 64)
+constexpr int kGramSBytes = 2 * kBM * 64 * 2;  // up to two planes of 128 rows x r_pad (<= 64)
 constexpr int kGramSmem = 1024 + kGramStages * (kGramDBytes + kGramSBytes) + 24 * 128 + 256;
 
 // Work units of one CTA (slot, column block), staged in shared memory once so no role
@@ -1223,7 +1242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int stage = 0;
     uint32_t phase = 0, issued_mask = 0, last_parity = 0;
     bool ok = true;
-    const uint32_t bytes = static_cast<uint32_t>(kGramDBytes + kBM * r_pad * 2);
+    const uint32_t bytes = static_cast<uint32_t>(kGramDBytes + prm.planes * kBM * r_pad * 2);
     for (int k = 0; k < n_mine && ok; ++k) {
       const GramUnit g = unit(k);
       for (int i0 = g.b; i0 < g.e && ok; i0 += 32) {
@@ -1243,7 +1262,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               mbar_arrive_expect_tx(&full[stage], bytes);
               tma_load_2d(sD + stage * kGramDBytes, &map_d, &full[stage], g.cb * 128, row_q);
               tma_load_2d(sD + stage * kGramDBytes + kGramDBytes / 2, &map_d, &full[stage], g.cb * 128 + 64, row_q);
-              tma_load_2d(sS + stage * kGramSBytes, &map_s, &full[stage], 0, st_q * kBM);
+              for (int pl = 0; pl < prm.planes; ++pl)
+                tma_load_2d(sS + stage * kGramSBytes + pl * (kGramSBytes / 2), &map_s, &full[stage], 0,
+                            pl * prm.s_plane_rows + st_q * kBM);
             }
           }
           go = __shfl_sync(0xffffffffu, go, 0);
@@ -1288,13 +1309,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = d_base + stage * kGramDBytes, b0 = s_base + stage * kGramSBytes;
+          const uint32_t a0 = d_base + stage * kGramDBytes;
+          for (int pl = 0; pl < prm.planes; ++pl) {
+            const uint32_t b0 = s_base + stage * kGramSBytes + pl * (kGramSBytes / 2);
 #pragma unroll
-          for (int kk = 0; kk < kBM / 16; ++kk) {
-            const uint64_t adesc = umma_sdesc(a0 + kk * 2048, kGramDBytes / 2, 1024, 2);
-            const uint64_t bdesc = umma_sdesc(b0 + kk * prm.s_kstep, kBM * r_pad * 2, prm.s_sbo, prm.s_layout);
-            umma_f16(dt, adesc, bdesc, prm.idesc, acc);
-            acc = 1;
+            for (int kk = 0; kk < kBM / 16; ++kk) {
+              const uint64_t adesc = umma_sdesc(a0 + kk * 2048, kGramDBytes / 2, 1024, 2);
+              const uint64_t bdesc = umma_sdesc(b0 + kk * prm.s_kstep, kBM * r_pad * 2, prm.s_sbo, prm.s_layout);
+              umma_f16(dt, adesc, bdesc, prm.idesc, acc);
+              acc = 1;
+            }
           }
           issued_any = true;
           umma_commit(&empty[stage]);
@@ -1477,6 +1501,8 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
   const int all_pairs = num_sms / 2;
   int gemm_pairs = total < all_pairs ? total : all_pairs;
   const CUtensorMap* a_map = &maps.p;  // unused unless a shrink is co-scheduled
+  const CUtensorMap* p2_map = &maps.p;
+  const CUtensorMap* a2_map = &maps.p;
   if (shrink != nullptr && shrink->n_pairs > 0) {
     p.n_shrink_pairs = shrink->n_pairs;
     p.s_planes = 2;
@@ -1484,6 +1510,13 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
     p.unit_ready = shrink->unit_ready;
     p.gen = shrink->gen;
     a_map = &shrink->a_map;
+    if (shrink->job2) {
+      p.job2 = 1;
+      p.Kred2 = shrink->K2;
+      p.s_ext2 = shrink->s_ext2;
+      p2_map = &shrink->p2_map;
+      a2_map = &shrink->a2_map;
+    }
     const int rounds = (total + all_pairs - 1) / all_pairs;
     gemm_pairs = (total + rounds - 1) / rounds;
   }
@@ -1506,7 +1539,8 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
 #define LF_LAUNCH_PAIR(QMN, OT)                                                                  \
   e = ensure_smem(tc_gemm_pair_kernel<QMN, OT>, kPairSmem);                                     \
   if (e != cudaSuccess) return e;                                                               \
-  e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<QMN, OT>, maps.p, maps.q, maps.s, maps.l, maps.o, *a_map, p);
+  e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<QMN, OT>, maps.p, maps.q, maps.s, maps.l, maps.o, *a_map, *p2_map, \
+                         *a2_map, p);
   if (dtype == LF_BF16) {
     if (q_mn_major) {
       LF_LAUNCH_PAIR(true, __nv_bfloat16)
@@ -1568,12 +1602,14 @@ cudaError_t tc_shrink(int dtype, const CUtensorMap& p_map, const CUtensorMap& a_
 }
 
 cudaError_t tc_gram(int dtype, const CUtensorMap& d_map, const CUtensorMap& s_map, int C, const Tables& tb, void* out,
-                    int transpose_out, int num_sms, cudaStream_t st) {
+                    int transpose_out, int num_sms, cudaStream_t st, int planes) {
   GramParams p{};
   p.out = out;
   p.C = C;
   p.n_cblk = (C + 127) / 128;
   p.transpose_out = transpose_out;
+  p.planes = planes;
+  p.s_plane_rows = (tb.n_segtiles + 1) * kBM;
   p.r_pad = tb.r_pad;
   const int fmt = dtype == LF_BF16 ? 1 : 0;
   p.idesc = umma_idesc_f16(kBM, tb.r_pad, fmt, 1, 1);

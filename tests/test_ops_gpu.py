@@ -249,3 +249,28 @@ def test_gemm_tilings_match_oracle(single_cta):
     y0 = prep.new_output()
     prep.launch(y0, nat.LF_STAGE_BASE | (nat.LF_STAGE_SINGLE_CTA if single_cta else 0))
     _check(y0, case["x"] @ case["w"].T, BF16_TOL, "base GEMM only")
+
+
+@pytest.mark.parametrize("co_scheduled", [True, False], ids=["one_launch_shrinks", "separate_shrinks"])
+def test_co_scheduling_switch_matches_oracle(co_scheduled):
+    """Forward and backward with the routed shrinks inside the GEMM launch (forward 1 launch,
+    backward 3) and as launches of their own (2 and 5); both match the oracle."""
+    ops = _ops()
+    routes = _routes_from_sizes([300, 5, 1, 94, 200, 100, 324], [0, 1, 2, 3, 0, 1, 2])  # 1024 rows
+    case = _random_case(23, 1024, 512, 768, routes, {0: 16, 1: 8, 2: 32, 3: 64}, torch.bfloat16)
+    ops.use_cooperative_launch(co_scheduled)
+    try:
+        x, w, a, b, ad, routing, g = _to_torch(case, torch.bfloat16)
+        y = ops.fused_lora_forward(x, w, a, b, ad, routing)
+        assert ops.last_launch_count() == (1 if co_scheduled else 2)
+        gx, ga, gb = ops.fused_lora_backward(g, x, w, a, b, ad, routing)
+        assert ops.last_launch_count() == (3 if co_scheduled else 5)
+    finally:
+        ops.use_cooperative_launch(True)
+    _check(y, case["y"], BF16_TOL, "forward")
+    _check(gx, case["gx"], BF16_TOL, "grad_x")
+    for k in case["grad_keys"]:
+        _check(ga[k], case["ga"][k], BF16_TOL, f"grad_a[{k}]")
+        _check(gb[k], case["gb"][k], BF16_TOL, f"grad_b[{k}]")
+    from lorafusion_b200 import _native as nat
+    assert nat.device_error() == 0
