@@ -275,6 +275,16 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
                : "memory");
 }
+// Same completion, signalled with ONE commit on the mbarrier at CTA-local address `bar` in both
+// CTAs of the pair (CTA mask 0b11).  Every tcgen05 operation the issuing thread adds costs
+// tensor-pipe time, so one commit replaces a commit per CTA.
+__device__ __forceinline__ void umma_commit_pair_both(uint32_t bar) {
+  const uint16_t mask = 3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
 // Plain arrive on an mbarrier of another CTA of the cluster.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");

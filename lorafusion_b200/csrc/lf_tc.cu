@@ -804,8 +804,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true, issued_any = false;
       const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
-      const uint32_t empty_self = map_to_cta(smem_u32(empty), 0), empty_peer = map_to_cta(smem_u32(empty), 1);
-      const uint32_t tfull_self = map_to_cta(smem_u32(tfull), 0), tfull_peer = map_to_cta(smem_u32(tfull), 1);
+      const uint32_t empty_local = smem_u32(empty), tfull_local = smem_u32(tfull);  // same offsets in both CTAs
       int it = 0;
       for (int t = pair; t < total && ok; t += n_pairs, ++it) {
         int mp, n;
@@ -838,8 +837,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc = 1;
           }
           issued_any = true;
-          umma_commit_pair(empty_self + stage * 8);
-          umma_commit_pair(empty_peer + stage * 8);
+          umma_commit_pair_both(empty_local + stage * 8);
           if (++stage == kPairStages) {
             stage = 0;
             phase ^= 1;
@@ -859,16 +857,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             acc = 1;
           }
           issued_any = true;
-          umma_commit_pair(empty_self + stage * 8);
-          umma_commit_pair(empty_peer + stage * 8);
+          umma_commit_pair_both(empty_local + stage * 8);
           if (++stage == kPairStages) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        umma_commit_pair(tfull_self + buf * 8);
-        umma_commit_pair(tfull_peer + buf * 8);
+        umma_commit_pair_both(tfull_local + buf * 8);
       }
       if (!ok && issued_any) {
         umma_commit_pair(map_to_cta(smem_u32(drain), 0));
