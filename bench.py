@@ -374,6 +374,33 @@ def run_ours(args):
     te = timed(e2e, max(5, args.steps // 2), 2, 2)
     e2e_ms = rank_max(statistics.mean(s[0] for s in te))
 
+    # requests in, per-request results out (one device): C++ packing, lf_copy_rows gather,
+    # fused forward, lf_copy_rows scatter
+    coordinator = None
+    if world == 1:
+        from lorafusion_b200.coordinator import Coordinator
+        from lorafusion_b200.scheduler import Request
+        from lorafusion_b200.workloads import row_counts
+        reqs = [Request(i, i, c) for i, c in enumerate(row_counts(wl, wl.total_rows))]
+        gq = torch.Generator(device=device).manual_seed(7)
+        req_x = {r.request_id: torch.randn(r.num_rows, K, device=device, generator=gq).to(torch.bfloat16)
+                 for r in reqs}
+        coord = Coordinator(pr["w"], pr["adapters"], pr["lora_a"], pr["lora_b"], tile_capacity=wl.tile_capacity)
+
+        def cstep(ev):
+            if ev:
+                ev[0].record()
+            coord.run_batch(reqs, req_x)
+            if ev:
+                ev[1].record()
+
+        tco = timed(cstep, max(5, args.steps // 2), 2, 2)
+        co_ms = statistics.mean(s[0] for s in tco)
+        coordinator = {"value": sum(r.num_rows for r in reqs) / (co_ms / 1e3), "unit": "tokens/s", "ms_per_step": co_ms,
+                       "requests": len(reqs),
+                       "path": "Coordinator.run_batch: greedy_pack (C++), lf_copy_rows gather, fused forward, "
+                               "lf_copy_rows scatter; request tensors resident on the device"}
+
     # forward + backward (with the all-reduce of spanning adapter gradients when N > 1)
     fwd_bwd = None
     if not args.no_fwd_bwd:
@@ -445,6 +472,7 @@ def run_ours(args):
                     "h2d_bytes_per_step": T * K * 2, "d2h_bytes_per_step": T * N * 2,
                     "path": "b200_ops.fused_lora_forward with pinned host x/y"},
             "fwd_bwd": fwd_bwd,
+            "coordinator": coordinator,
             "cpu_baseline": cpu,
             "clocks": clocks,
             "gpu_launches": gpu_launches,

@@ -222,6 +222,56 @@ LF_API int lf_forward_noalloc(const lf_problem* prob, const lf_plan_info* info, 
                               void* y_dev, lf_stream_t stream);
 
 /*
+ * One run of lf_copy_rows.  Flattened row g of the copy belongs to the run with the largest
+ * row0 <= g; runs are sorted by row0, and a run covers flattened rows [row0, row0 + rows).
+ */
+typedef struct lf_row_run {
+  uint64_t src;       /* device address of the run's first source row */
+  uint64_t dst;       /* device address of the run's first destination row */
+  int64_t src_stride; /* bytes between consecutive source rows */
+  int64_t dst_stride; /* bytes between consecutive destination rows */
+  int64_t rows;       /* rows in the run */
+  int64_t row0;       /* flattened index of the run's first row (running sum of `rows`) */
+} lf_row_run;
+
+/*
+ * Copy the rows of every run (row_bytes bytes each, byte-exact) in one launch; `runs_dev` is
+ * device memory holding n_runs entries and total_rows = sum of their rows.  Gathers request rows
+ * into the fused batch (replaces the torch.cat of lorafusion/scheduler/data_batcher.py:61-80)
+ * and splits fused output rows back per request (replaces the per-row loop of
+ * data_batcher.py:90-103).  Enqueued on `stream`; never synchronizes.
+ */
+LF_API int lf_copy_rows(const lf_row_run* runs_dev, int32_t n_runs, int64_t row_bytes, int64_t total_rows,
+                        lf_stream_t stream);
+
+/*
+ * First-fit-decreasing packing of per-adapter row counts (host only), identical to greedy_pack
+ * (lorafusion/scheduler/milp_packer.py:36-72): adapters in the given order are cut into chunks of
+ * at most tile_capacity rows, the chunks are stably sorted by size, largest first, and each goes
+ * into the first bin with room, else into a new bin at the end.  Adapters with rows <= 0 give no
+ * chunk.  Result (CSR): bin b holds entries [bin_start[b], bin_start[b+1]) of
+ * entry_adapter / entry_rows in insertion order; *n_entries and *n_bins are set.  Needs
+ * max_entries >= the chunk count (bin_start has max_entries + 1 slots); otherwise returns
+ * LF_ERR_CAPACITY with *n_entries = the chunk count.  tile_capacity <= 0: LF_ERR_INVALID_ARG.
+ */
+LF_API int lf_greedy_pack(const int32_t* adapter_ids, const int32_t* rows, int32_t n_adapters, int32_t tile_capacity,
+                          int32_t max_entries, int32_t* bin_start, int32_t* entry_adapter, int32_t* entry_rows,
+                          int32_t* n_entries, int32_t* n_bins);
+
+/*
+ * Bin -> rank assignment for one process per GPU (host only).  No counterpart in the reference
+ * (it runs on one device).  Consecutive bins holding one and the same adapter form bundles (at
+ * most ceil(total/world) rows; a bin with several adapters is a bundle of its own).  Each rank
+ * may hold its even share rounded up to whole `granule_rows` (the fused GEMM's row tile); bundles,
+ * largest first (ties in bundle order), go to the rank they fit best (least room left, then
+ * lowest rank); a bundle that fits nowhere is placed bin by bin, largest first, and a bin that
+ * fits nowhere goes to the least-loaded rank.  Deterministic: every rank computes the same
+ * bin_rank[n_bins] without communicating.  Inputs are the CSR packing of lf_greedy_pack.
+ */
+LF_API int lf_assign_bins(const int32_t* bin_start, const int32_t* entry_adapter, const int32_t* entry_rows,
+                          int32_t n_bins, int32_t world_size, int32_t granule_rows, int32_t* bin_rank);
+
+/*
  * Read and clear the device-side error word (bounded-wait timeouts inside kernels).
  * Synchronizes the current device.  *code = 0 when no kernel reported a problem.
  */

@@ -50,6 +50,11 @@ class Problem(ctypes.Structure):
     ]
 
 
+class RowRun(ctypes.Structure):
+    _fields_ = [("src", ctypes.c_uint64), ("dst", ctypes.c_uint64), ("src_stride", ctypes.c_int64),
+                ("dst_stride", ctypes.c_int64), ("rows", ctypes.c_int64), ("row0", ctypes.c_int64)]
+
+
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
 
@@ -68,6 +73,13 @@ def _declare(L: ctypes.CDLL) -> None:
     L.lf_pack_adapters.argtypes = [_c_i32, _c_i32, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
                                    _c_p, _c_p]
     L.lf_pack_adapters.restype = ctypes.c_int
+    L.lf_copy_rows.argtypes = [_c_p, _c_i32, ctypes.c_int64, ctypes.c_int64, _c_p]
+    L.lf_copy_rows.restype = ctypes.c_int
+    L.lf_greedy_pack.argtypes = [P(_c_i32), P(_c_i32), _c_i32, _c_i32, _c_i32, P(_c_i32), P(_c_i32), P(_c_i32),
+                                 P(_c_i32), P(_c_i32)]
+    L.lf_greedy_pack.restype = ctypes.c_int
+    L.lf_assign_bins.argtypes = [P(_c_i32), P(_c_i32), P(_c_i32), _c_i32, _c_i32, _c_i32, P(_c_i32)]
+    L.lf_assign_bins.restype = ctypes.c_int
     L.lf_forward.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, ctypes.c_size_t, _c_p]
     L.lf_forward.restype = ctypes.c_int
     L.lf_forward_stages.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, ctypes.c_size_t, _c_i32, _c_p]

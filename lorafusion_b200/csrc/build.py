@@ -23,7 +23,7 @@ REPO = os.path.dirname(PKG)
 OBJ_DIR = os.path.join(PKG, "_build")
 LIB_DIR = os.path.join(PKG, "_lib")
 LIB_NAME = "liblorafusion_b200.so"
-SOURCES = ["lf_tables.cpp", "lf_simt.cu", "lf_tc.cu", "lf_capi.cu", "lf_noalloc.cu"]
+SOURCES = ["lf_tables.cpp", "lf_sched.cpp", "lf_simt.cu", "lf_tc.cu", "lf_rows.cu", "lf_capi.cu", "lf_noalloc.cu"]
 HEADERS = ["lf_ptx.cuh", "lf_internal.cuh", os.path.join("..", "..", "include", "lorafusion_b200.h")]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -11,14 +11,22 @@ same inputs (same bins, same route order, same ``row_order``):
 * ``build_microbatch``/``scatter_outputs`` follow
   ``lorafusion/scheduler/data_batcher.py:18-103``.
 
-``scatter_outputs`` gathers each request's rows with one indexed copy instead
-of stacking single rows; the result holds the same values in the same order.
+Where the reference loops in Python, this module hands the work to the native
+library: ``greedy_pack`` runs ``lf_greedy_pack`` (C++, same bins bit for bit),
+and for CUDA tensors ``build_microbatch`` gathers and ``scatter_outputs``
+splits rows with one ``lf_copy_rows`` launch (byte-exact copies) instead of
+``torch.cat`` over slices and a per-row Python loop.  CPU tensors keep the
+reference's torch semantics.  ``scatter_outputs`` returns, for CUDA input,
+disjoint contiguous views of one freshly allocated buffer.
 """
 
 from __future__ import annotations
 
+import ctypes
+import functools
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from lorafusion_b200.config import TileRoute, TileRoutingConfig
@@ -147,26 +155,35 @@ def _split_into_chunks(adapter_rows: dict[int, int], cap: int) -> list[tuple[int
 
 def greedy_pack(adapter_rows: dict[int, int], tile_capacity: int) -> PackingResult:
     """First-fit-decreasing packing of per-adapter row counts into bins of
-    ``tile_capacity`` rows (milp_packer.py:36-72).
+    ``tile_capacity`` rows (milp_packer.py:36-72), computed by ``lf_greedy_pack``.
 
     Chunks are ordered by size, largest first, keeping dict order among equal
     sizes (a stable sort); each goes into the first bin with room, else a new
     bin at the end.
     """
+    from lorafusion_b200 import _native as nat
+
     if tile_capacity <= 0:
         raise ValueError("tile_capacity must be positive")
-    order = sorted(_split_into_chunks(adapter_rows, tile_capacity), key=lambda c: -c[1])
-    bins: list[list[tuple[int, int]]] = []
-    room: list[int] = []
-    for aid, n in order:
-        for b, free in enumerate(room):
-            if free >= n:
-                bins[b].append((aid, n))
-                room[b] = free - n
-                break
-        else:
-            bins.append([(aid, n)])
-            room.append(tile_capacity - n)
+    ids = np.fromiter(adapter_rows.keys(), dtype=np.int64, count=len(adapter_rows))
+    rows = np.fromiter(adapter_rows.values(), dtype=np.int64, count=len(adapter_rows))
+    lim = np.iinfo(np.int32)
+    if tile_capacity > lim.max or ids.size and (ids.min() < lim.min or ids.max() > lim.max or rows.max() > lim.max):
+        raise ValueError("adapter ids and row counts must fit in 32 bits")
+    ids32, rows32 = ids.astype(np.int32), rows.astype(np.int32)
+    n_chunks = int(np.sum((rows32[rows32 > 0].astype(np.int64) + tile_capacity - 1) // tile_capacity))
+    bin_start = np.zeros(n_chunks + 1, dtype=np.int32)
+    ent_a = np.zeros(max(n_chunks, 1), dtype=np.int32)
+    ent_r = np.zeros(max(n_chunks, 1), dtype=np.int32)
+    n_ent, n_bins = ctypes.c_int32(0), ctypes.c_int32(0)
+    P = ctypes.POINTER(ctypes.c_int32)
+    rc = nat.lib().lf_greedy_pack(ids32.ctypes.data_as(P), rows32.ctypes.data_as(P), ids32.size, tile_capacity,
+                                  n_chunks, bin_start.ctypes.data_as(P), ent_a.ctypes.data_as(P),
+                                  ent_r.ctypes.data_as(P), ctypes.byref(n_ent), ctypes.byref(n_bins))
+    nat.check(rc, "lf_greedy_pack")
+    a_list, r_list, starts = ent_a.tolist(), ent_r.tolist(), bin_start.tolist()
+    bins = [list(zip(a_list[starts[b]:starts[b + 1]], r_list[starts[b]:starts[b + 1]]))
+            for b in range(n_bins.value)]
     return PackingResult(bins=bins, tile_capacity=tile_capacity, method="greedy")
 
 
@@ -218,6 +235,25 @@ def milp_pack(
 # --------------------------------------------------------------------------
 
 
+def _copy_runs(runs: list[tuple[int, int, int, int, int]], row_bytes: int, device: torch.device) -> None:
+    """One ``lf_copy_rows`` launch over ``(src, dst, src_stride, dst_stride, rows)`` runs."""
+    from lorafusion_b200 import _native as nat
+
+    if not runs or row_bytes == 0:
+        return
+    table = np.zeros(len(runs), dtype=[("src", "<u8"), ("dst", "<u8"), ("src_stride", "<i8"),
+                                       ("dst_stride", "<i8"), ("rows", "<i8"), ("row0", "<i8")])
+    cols = np.array(runs, dtype=np.int64).reshape(len(runs), 5)
+    table["src"], table["dst"] = cols[:, 0].astype(np.uint64), cols[:, 1].astype(np.uint64)
+    table["src_stride"], table["dst_stride"], table["rows"] = cols[:, 2], cols[:, 3], cols[:, 4]
+    table["row0"] = np.concatenate(([0], np.cumsum(cols[:, 4])[:-1]))
+    total = int(cols[:, 4].sum())
+    host = torch.from_numpy(table.view(np.uint8)).pin_memory()
+    dev = host.to(device, non_blocking=True)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    nat.check(nat.lib().lf_copy_rows(dev.data_ptr(), len(runs), row_bytes, total, stream), "lf_copy_rows")
+
+
 def build_microbatch(
     requests: list[Request],
     request_tensors: dict[int, torch.Tensor],
@@ -230,14 +266,16 @@ def build_microbatch(
     each remembering how many of its rows earlier entries already took; the
     entry's route always spans ``n`` rows from the running cursor.
     Returns ``(fused_x, routing, row_order)`` where ``row_order[i]`` is the
-    request id of fused row ``i``.
+    request id of fused row ``i``.  With CUDA request tensors the rows are
+    gathered by one ``lf_copy_rows`` launch; ``fused_x`` equals the
+    reference's ``torch.cat`` of the same slices byte for byte.
     """
     in_features = next(iter(request_tensors.values())).shape[1]
     queue: dict[int, list[Request]] = {}
     for req in requests:
         queue.setdefault(req.adapter_id, []).append(req)
     taken: dict[int, int] = {}
-    pieces: list[torch.Tensor] = []
+    pieces: list[tuple[int, int, int]] = []  # (request id, first row, rows)
     routes: list[TileRoute] = []
     row_order: list[int] = []
     cursor = 0
@@ -253,27 +291,92 @@ def build_microbatch(
                 if avail <= 0:
                     continue
                 k = want if want < avail else avail
-                pieces.append(src[start : start + k])
+                pieces.append((req.request_id, start, k))
                 row_order.extend([req.request_id] * k)
                 taken[req.request_id] = start + k
                 want -= k
             routes.append(TileRoute(row_start=cursor, row_end=cursor + n, adapter_id=aid))
             cursor += n
-    fused_x = torch.cat(pieces, dim=0) if pieces else torch.empty((0, in_features))
-    return fused_x, TileRoutingConfig(tile_size=packing.tile_capacity, routes=routes), row_order
+    routing = TileRoutingConfig(tile_size=packing.tile_capacity, routes=routes)
+    if not pieces:
+        return torch.empty((0, in_features)), routing, row_order
+    srcs = [request_tensors[rid] for rid, _, _ in pieces]
+    if not all(t.is_cuda for t in srcs):
+        fused_x = torch.cat([request_tensors[rid][a:a + k] for rid, a, k in pieces], dim=0)
+        return fused_x, routing, row_order
+    device = srcs[0].device
+    if any(t.device != device or t.dim() != 2 for t in srcs):
+        raise ValueError("request tensors must be 2-D and on one device")
+    dtype = functools.reduce(torch.promote_types, {t.dtype for t in srcs})
+    ready: dict[int, torch.Tensor] = {}
+    for rid, _, _ in pieces:  # rows as contiguous lines of the result dtype
+        if rid not in ready:
+            t = request_tensors[rid]
+            if t.dtype != dtype:
+                t = t.to(dtype)
+            if t.shape[1] > 0 and t.stride(1) != 1:
+                t = t.contiguous()
+            ready[rid] = t
+    fused_x = torch.empty((len(row_order), in_features), dtype=dtype, device=device)
+    es = fused_x.element_size()
+    runs, at = [], 0
+    for rid, a, k in pieces:
+        t = ready[rid]
+        runs.append((t.data_ptr() + a * t.stride(0) * es, fused_x.data_ptr() + at * in_features * es,
+                     t.stride(0) * es, in_features * es, k))
+        at += k
+    _copy_runs(runs, in_features * es, device)
+    return fused_x, routing, row_order
 
 
 def scatter_outputs(fused_out: torch.Tensor, row_order: list[int]) -> dict[int, torch.Tensor]:
     """Split fused output rows back per request (data_batcher.py:90-103).
 
     Requests appear in order of their first fused row; each request's rows
-    keep their fused order.
+    keep their fused order.  CUDA input: one ``lf_copy_rows`` launch over the
+    runs of equal ids in ``row_order``; the values are views of one new
+    buffer, request after request.
     """
-    rows_of: dict[int, list[int]] = {}
-    for i, rid in enumerate(row_order):
-        rows_of.setdefault(rid, []).append(i)
-    out: dict[int, torch.Tensor] = {}
-    for rid, idx in rows_of.items():
-        index = torch.tensor(idx, dtype=torch.long, device=fused_out.device)
-        out[rid] = fused_out.index_select(0, index)
-    return out
+    if len(row_order) > fused_out.shape[0]:
+        raise IndexError(f"row_order has {len(row_order)} rows, fused output only {fused_out.shape[0]}")
+    if not row_order:
+        return {}
+    if not fused_out.is_cuda:
+        rows_of: dict[int, list[int]] = {}
+        for i, rid in enumerate(row_order):
+            rows_of.setdefault(rid, []).append(i)
+        out: dict[int, torch.Tensor] = {}
+        for rid, idx in rows_of.items():
+            index = torch.tensor(idx, dtype=torch.long, device=fused_out.device)
+            out[rid] = fused_out.index_select(0, index)
+        return out
+    src = fused_out.contiguous()
+    ids = np.asarray(row_order, dtype=np.int64)
+    cut = np.flatnonzero(ids[1:] != ids[:-1]) + 1
+    run_start = np.concatenate(([0], cut))
+    run_len = np.diff(np.concatenate((run_start, [ids.size])))
+    run_id = ids[run_start]
+    first = {}
+    count: dict[int, int] = {}
+    for rid, n in zip(run_id.tolist(), run_len.tolist()):
+        if rid not in first:
+            first[rid] = len(first)
+        count[rid] = count.get(rid, 0) + n
+    order = list(first.keys())
+    row_shape = tuple(src.shape[1:])
+    row_elems = int(np.prod(row_shape)) if row_shape else 1
+    buf = torch.empty((ids.size,) + row_shape, dtype=src.dtype, device=src.device)
+    base, off = {}, 0
+    for rid in order:
+        base[rid] = off
+        off += count[rid]
+    es = src.element_size()
+    row_bytes = row_elems * es
+    runs, filled = [], dict.fromkeys(order, 0)
+    for rid, a, n in zip(run_id.tolist(), run_start.tolist(), run_len.tolist()):
+        runs.append((src.data_ptr() + a * row_bytes, buf.data_ptr() + (base[rid] + filled[rid]) * row_bytes,
+                     row_bytes, row_bytes, n))
+        filled[rid] += n
+    _copy_runs(runs, row_bytes, src.device)
+    parts = torch.split(buf, [count[rid] for rid in order], dim=0)
+    return dict(zip(order, parts))

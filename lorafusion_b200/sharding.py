@@ -6,7 +6,7 @@ the op needs to run one process per GPU:
 * The global layout is untouched: every rank runs the same scheduler
   (``bucket_by_adapter -> greedy_pack -> build_microbatch``) and gets the same
   bins and routes, bit for bit.
-* :func:`assign_bins` gives each rank whole bins.  Runs of consecutive
+* :func:`assign_bins` gives each rank whole bins (``lf_assign_bins``, C++).  Runs of consecutive
   single-adapter bins form bundles so an adapter's rows stay on one rank where
   possible; bundles larger than a rank's share are cut.  Every rank gets a
   capacity of its even share rounded up to whole 256-row tile pairs; bundles,
@@ -24,8 +24,10 @@ the op needs to run one process per GPU:
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from lorafusion_b200.config import TileRoute, TileRoutingConfig
@@ -47,31 +49,11 @@ class ShardPlan:
         return sum(e - s for (s, e), r in zip(self.bin_rows, self.bin_rank) if r == rank)
 
 
-def _bundles(bins: list[list[tuple[int, int]]], cap_rows: int) -> list[list[int]]:
-    out: list[list[int]] = []
-    cur: list[int] = []
-    cur_adapter = None
-    cur_rows = 0
-    for b, entries in enumerate(bins):
-        adapters = {a for a, _ in entries}
-        rows = sum(n for _, n in entries)
-        solo = next(iter(adapters)) if len(adapters) == 1 else None
-        if cur and (solo is None or solo != cur_adapter or cur_rows + rows > cap_rows):
-            out.append(cur)
-            cur, cur_rows, cur_adapter = [], 0, None
-        cur.append(b)
-        cur_rows += rows
-        cur_adapter = solo
-        if solo is None:
-            out.append(cur)
-            cur, cur_rows, cur_adapter = [], 0, None
-    if cur:
-        out.append(cur)
-    return out
-
-
 def assign_bins(bins: list[list[tuple[int, int]]], world_size: int) -> ShardPlan:
-    """Deterministic bin -> rank assignment (see module docstring)."""
+    """Deterministic bin -> rank assignment (see module docstring), computed by
+    ``lf_assign_bins`` in the native library."""
+    from lorafusion_b200 import _native as nat
+
     if world_size <= 0:
         raise ValueError("world_size must be positive")
     rows = [sum(n for _, n in entries) for entries in bins]
@@ -79,40 +61,23 @@ def assign_bins(bins: list[list[tuple[int, int]]], world_size: int) -> ShardPlan
     for r in rows:
         starts.append((cur, cur + r))
         cur += r
-    share = max(1, -(-cur // world_size))
-    # Each rank's capacity is its share rounded up to whole 256-row tile pairs (the fused GEMM's
-    # row granularity), so an even split costs no extra, mostly empty, row of tiles.
-    cap = -(-share // TILE_PAIR_ROWS) * TILE_PAIR_ROWS
-    bundles = _bundles(bins, share)
-    order = sorted(range(len(bundles)), key=lambda i: -sum(rows[b] for b in bundles[i]))
-    load = [0] * world_size
-    bin_rank = [0] * len(bins)
-
-    def place(members: list[int]) -> bool:
-        n = sum(rows[b] for b in members)
-        fits = [k for k in range(world_size) if load[k] + n <= cap]
-        if not fits:
-            return False
-        r = min(fits, key=lambda k: (cap - load[k] - n, k))  # best fit
-        for b in members:
-            bin_rank[b] = r
-        load[r] += n
-        return True
-
-    for i in order:
-        if place(bundles[i]):
-            continue
-        for b in sorted(bundles[i], key=lambda b: (-rows[b], b)):  # split the bundle into its bins
-            if not place([b]):
-                r = min(range(world_size), key=lambda k: (load[k], k))
-                bin_rank[b] = r
-                load[r] += rows[b]
+    counts = np.fromiter((len(e) for e in bins), dtype=np.int64, count=len(bins))
+    bin_start = np.concatenate(([0], np.cumsum(counts))).astype(np.int32)
+    flat = [x for entries in bins for x in entries]
+    ent_a = np.array([a for a, _ in flat] or [0], dtype=np.int32)
+    ent_r = np.array([n for _, n in flat] or [0], dtype=np.int32)
+    bin_rank = np.zeros(max(len(bins), 1), dtype=np.int32)
+    P = ctypes.POINTER(ctypes.c_int32)
+    rc = nat.lib().lf_assign_bins(bin_start.ctypes.data_as(P), ent_a.ctypes.data_as(P), ent_r.ctypes.data_as(P),
+                                  len(bins), world_size, TILE_PAIR_ROWS, bin_rank.ctypes.data_as(P))
+    nat.check(rc, "lf_assign_bins")
+    ranks = bin_rank[:len(bins)].tolist()
     owners: dict[int, set[int]] = {}
     for b, entries in enumerate(bins):
-        for a, n in entries:
-            owners.setdefault(a, set()).add(bin_rank[b])
+        for a, _ in entries:
+            owners.setdefault(a, set()).add(ranks[b])
     spanning = sorted(a for a, rk in owners.items() if len(rk) > 1)
-    return ShardPlan(world_size=world_size, bin_rank=bin_rank, bin_rows=starts, spanning=spanning)
+    return ShardPlan(world_size=world_size, bin_rank=ranks, bin_rows=starts, spanning=spanning)
 
 
 def local_layout(plan: ShardPlan, bins: list[list[tuple[int, int]]], rank: int, tile_size: int):

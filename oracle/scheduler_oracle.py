@@ -10,6 +10,9 @@ tables bit-exactly.
 * :func:`microbatch_layout` — ``lorafusion/scheduler/data_batcher.py:18-87``,
   returning routes, ``row_order`` and, per fused row, the source
   ``(request_id, row_in_request)``.
+* :func:`assign_bins` — the bin -> rank assignment of the multi-GPU layer (no
+  counterpart in the reference, which runs on one device), restated in plain
+  Python to check ``lf_assign_bins``.
 """
 
 from __future__ import annotations
@@ -76,3 +79,55 @@ def microbatch_layout(requests, bins):
             routes.append((cursor, cursor + n, aid))
             cursor += n
     return routes, row_order, source
+
+
+def assign_bins(bins, world_size: int, granule_rows: int = 256):
+    """Rank of every bin: bundles of consecutive single-adapter bins (at most the
+    even share of rows), capacity = share rounded up to ``granule_rows``,
+    largest bundle first into the best-fitting rank; bundles that fit nowhere
+    are placed bin by bin, and bins that fit nowhere go to the least-loaded rank."""
+    if world_size <= 0:
+        raise ValueError("world_size must be positive")
+    rows = [sum(n for _, n in entries) for entries in bins]
+    total = sum(rows)
+    share = max(1, -(-total // world_size))
+    cap = -(-share // granule_rows) * granule_rows
+    bundles, cur, cur_adapter, cur_rows = [], [], None, 0
+    for b, entries in enumerate(bins):
+        adapters = {a for a, _ in entries}
+        solo = next(iter(adapters)) if len(adapters) == 1 else None
+        if cur and (solo is None or solo != cur_adapter or cur_rows + rows[b] > share):
+            bundles.append(cur)
+            cur, cur_rows, cur_adapter = [], 0, None
+        cur.append(b)
+        cur_rows += rows[b]
+        cur_adapter = solo
+        if solo is None:
+            bundles.append(cur)
+            cur, cur_rows, cur_adapter = [], 0, None
+    if cur:
+        bundles.append(cur)
+    order = sorted(range(len(bundles)), key=lambda i: -sum(rows[b] for b in bundles[i]))
+    load = [0] * world_size
+    rank = [0] * len(bins)
+
+    def place(members):
+        n = sum(rows[b] for b in members)
+        fits = [k for k in range(world_size) if load[k] + n <= cap]
+        if not fits:
+            return False
+        r = min(fits, key=lambda k: (cap - load[k] - n, k))
+        for b in members:
+            rank[b] = r
+        load[r] += n
+        return True
+
+    for i in order:
+        if place(bundles[i]):
+            continue
+        for b in sorted(bundles[i], key=lambda b: (-rows[b], b)):
+            if not place([b]):
+                r = min(range(world_size), key=lambda k: (load[k], k))
+                rank[b] = r
+                load[r] += rows[b]
+    return rank

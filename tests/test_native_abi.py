@@ -57,6 +57,10 @@ def test_plan_info_struct_matches_header():
         for part in decl.split(","):
             fields.append(part.strip().split()[-1].lstrip("*"))
     assert fields == [f[0] for f in nat.Problem._fields_]
+    body = text.split("typedef struct lf_row_run {")[1].split("} lf_row_run;")[0]
+    names = [ln.split("/*")[0].strip().rstrip(";").split()[-1] for ln in body.splitlines() if ln.split("/*")[0].strip()]
+    assert names == [f[0] for f in nat.RowRun._fields_]
+    assert ctypes.sizeof(nat.RowRun) == 48
 
 
 def _reconstruct(info, table):

@@ -88,3 +88,47 @@ def test_routing_validate_errors():
     with pytest.raises(ValueError, match="covers 10 rows"):
         TileRoutingConfig(64, [TileRoute(0, 10, 0)]).validate(20)
     TileRoutingConfig(64, []).validate(0)
+
+
+def _random_rows(rng, n, cap):
+    rows = {}
+    for _ in range(n):
+        aid = int(rng.integers(-50, 10_000))
+        rows[aid] = int(rng.choice([0, -3, 1, cap - 1, cap, cap + 1, 3 * cap + 7, int(rng.integers(1, 4 * cap))]))
+    return rows
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_native_greedy_pack_equals_oracle_first_fit(seed):
+    """lf_greedy_pack (segment-tree first fit) gives the reference's bins exactly, ties included."""
+    from oracle.scheduler_oracle import greedy_bins
+    rng = np.random.default_rng(seed)
+    cap = int(rng.choice([1, 16, 64, 128, 1000]))
+    rows = _random_rows(rng, int(rng.integers(0, 300)), cap)
+    assert greedy_pack(rows, cap).bins == greedy_bins(rows, cap)
+
+
+def test_native_greedy_pack_at_config_sizes():
+    from oracle.scheduler_oracle import greedy_bins
+    from lorafusion_b200.workloads import WORKLOADS, row_counts
+    for wl in WORKLOADS.values():
+        rows = dict(enumerate(row_counts(wl, wl.total_rows)))
+        assert greedy_pack(rows, wl.tile_capacity).bins == greedy_bins(rows, wl.tile_capacity), wl.name
+
+
+def test_native_greedy_pack_argument_errors():
+    import ctypes
+    from lorafusion_b200 import _native as nat
+    with pytest.raises(ValueError):
+        greedy_pack({0: 3}, -1)
+    with pytest.raises(ValueError):
+        greedy_pack({1 << 40: 3}, 8)
+    assert greedy_pack({}, 8).bins == []
+    assert greedy_pack({3: 0, 4: -2}, 8).bins == []
+    P = ctypes.POINTER(ctypes.c_int32)
+    ids = (ctypes.c_int32 * 1)(7)
+    rows = (ctypes.c_int32 * 1)(100)
+    n_ent, n_bins = ctypes.c_int32(0), ctypes.c_int32(0)
+    out = (ctypes.c_int32 * 8)()
+    rc = nat.lib().lf_greedy_pack(ids, rows, 1, 16, 2, out, out, out, ctypes.byref(n_ent), ctypes.byref(n_bins))
+    assert rc == nat.LF_ERR_CAPACITY and n_ent.value == 7  # ceil(100 / 16) chunks needed

@@ -128,3 +128,20 @@ def test_spanning_gradients_allreduce_gloo():
         assert p.exitcode == 0
     assert all(ok for _, ok, _ in results), results
     assert results[0][2] and results[0][2] == results[1][2]
+
+
+@pytest.mark.parametrize("seed", range(10))
+def test_native_assignment_equals_oracle(seed):
+    """lf_assign_bins matches the plain-Python restatement on random packings and world sizes."""
+    from oracle.scheduler_oracle import assign_bins as oracle_assign
+    rng = np.random.default_rng(100 + seed)
+    cap = int(rng.choice([16, 64, 128]))
+    counts = [int(v) for v in rng.integers(1, 6 * cap, size=int(rng.integers(1, 80)))]
+    _, packing = _packing(counts, cap)
+    for world in (1, 2, 3, 5, 8):
+        assert assign_bins(packing.bins, world).bin_rank == oracle_assign(packing.bins, world), (seed, world)
+    bins = [[], [(3, 5), (4, 2)], [(3, 7)], [(3, 9)], []]  # empty and mixed bins
+    for world in (1, 2, 4):
+        assert assign_bins(bins, world).bin_rank == oracle_assign(bins, world)
+    with pytest.raises(ValueError):
+        assign_bins(packing.bins, 0)
