@@ -417,8 +417,19 @@ def run_ours(args):
         tfb = timed(fb, max(5, args.steps // 2), 2, 2)
         fb_ms = rank_max(statistics.mean(s[0] for s in tfb))
         bwd_launches = b200_ops.last_launch_count()
+
+        def bwd_only(ev):
+            if ev:
+                ev[0].record()
+            b200_ops.fused_lora_backward(pr["grad"], pr["x"], pr["w"], pr["lora_a"], pr["lora_b"], pr["adapters"],
+                                         pr["routing"])
+            if ev:
+                ev[1].record()
+
+        tbo = timed(bwd_only, max(5, args.steps // 2), 2, 2)
+        bwd_ms = rank_max(statistics.mean(s[0] for s in tbo))
         fwd_bwd = {"value": pr["global_T"] / (fb_ms / 1e3), "unit": "tokens/s", "ms_per_step": fb_ms,
-                   "launches_per_step": n_launch + bwd_launches,
+                   "launches_per_step": n_launch + bwd_launches, "backward_ms": bwd_ms,
                    "tflops": counts["fwdbwd_flops"] * world / (fb_ms / 1e3) / 1e12,
                    "spanning_adapters": len(pr["plan"].spanning)}
 

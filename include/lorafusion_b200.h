@@ -178,10 +178,10 @@ LF_API int lf_forward_stages(const lf_problem* prob, const lf_plan_info* info, c
 LF_API int lf_forward_launch_count(const lf_problem* prob, const lf_plan_info* info);
 
 /*
- * Kernel launches lf_backward makes for this problem on the current device: 3 when both routed
- * shrinks run on CTA pairs the grad_x GEMM leaves idle (GEMM + two grams), 5 when they run as
- * launches of their own, 1 with no routed rows.  Negative lf_status on bad arguments.
- * No counterpart in the reference.
+ * Kernel launches lf_backward makes for this problem on the current device: 2 when both routed
+ * shrinks run on CTA pairs the grad_x GEMM leaves idle (that GEMM, then one launch for both
+ * grams dA and dB), 4 when the shrinks run as launches of their own, 1 with no routed rows
+ * (5 on the float32 path).  Negative lf_status on bad arguments.  No counterpart in the reference.
  */
 LF_API int lf_backward_launch_count(const lf_problem* prob, const lf_plan_info* info);
 

@@ -47,9 +47,9 @@ def use_cooperative_launch(enabled: bool) -> None:
     """Allow (default) or forbid the co-scheduled cooperative launches (process-wide).
 
     When allowed, the routed shrinks run inside the GEMM's launch on CTA pairs the GEMM
-    leaves idle (forward: 1 launch; backward: 3).  Profilers and SM-partitioned GPUs refuse
+    leaves idle (forward: 1 launch; backward: 2).  Profilers and SM-partitioned GPUs refuse
     cooperative launches; forbid them there and every shrink runs as a launch of its own
-    (forward: 2 launches; backward: 5).
+    (forward: 2 launches; backward: 4).
     """
     nat.check(nat.lib().lf_set_co_scheduling(1 if enabled else 0), "lf_set_co_scheduling")
 

@@ -172,7 +172,7 @@ extern "C" size_t lf_forward_workspace_bytes(const lf_plan_info* info, int32_t d
 
 extern "C" size_t lf_backward_workspace_bytes(const lf_plan_info* info, int32_t dtype) {
   (void)dtype;
-  return info ? 2 * sext_bytes(info) + flag_bytes(info, 2) : 0;
+  return info ? 2 * sext_bytes(info) + flag_bytes(info, 2) + gram_scratch_bytes(info->r_pad > 0 ? info->r_pad : 16) : 0;
 }
 
 extern "C" int lf_pack_adapters(int32_t src_dtype, int32_t dst_dtype, const uint64_t* src_ptrs_dev,
@@ -287,7 +287,7 @@ extern "C" int lf_backward_launch_count(const lf_problem* prob, const lf_plan_in
   const bool lora = info->n_segtiles > 0 && info->n_slots > 0;
   if (!tc) return 5;
   if (!lora) return 1;
-  return (cosched_allowed(ds) && pair_spare_pairs(prob->T, prob->K, ds->num_sms, info->n_shrink_units) > 0) ? 3 : 5;
+  return (cosched_allowed(ds) && pair_spare_pairs(prob->T, prob->K, ds->num_sms, info->n_shrink_units) > 0) ? 2 : 4;
 }
 
 extern "C" int lf_set_co_scheduling(int32_t enable) {
@@ -392,10 +392,19 @@ extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, con
       e = tc_gemm_pair(dt, true, dx, T, K, N, lora, tb, grad_x_dev, K, ds->num_sms, st);
       if (e != cudaSuccess) return LF_ERR_CUDA;
     }
-    if (lora) {
-      e = tc_gram(dt, p_g, sf_map, N, tb, grad_b_dev, 0, ds->num_sms, st, planes);
-      if (e != cudaSuccess) return LF_ERR_CUDA;
-      e = tc_gram(dt, p_x, sb_map, K, tb, grad_a_dev, 1, ds->num_sms, st, planes);
+    if (lora) {  // dB and dA in one launch
+      GramJobDesc jobs[2];
+      jobs[0].d_map = p_g;
+      jobs[0].s_map = sf_map;
+      jobs[0].C = N;
+      jobs[0].out = grad_b_dev;
+      jobs[0].transpose_out = 0;
+      jobs[1].d_map = p_x;
+      jobs[1].s_map = sb_map;
+      jobs[1].C = K;
+      jobs[1].out = grad_a_dev;
+      jobs[1].transpose_out = 1;
+      e = tc_gram(dt, jobs, 2, tb, ds->num_sms, st, planes, ws + 2 * sb + flag_bytes(info, 2), next_generation());
       if (e != cudaSuccess) return LF_ERR_CUDA;
     }
     return LF_OK;

@@ -89,10 +89,31 @@ int pair_spare_pairs(int T, int Nout, int num_sms, int n_units);
 cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, int Nout, int Kred, bool lora,
                          const Tables& tb, void* out, int64_t ldo, int num_sms, cudaStream_t st,
                          const PairShrink* shrink = nullptr);
+// Gram load balance: slots (slot_order positions) the kernel can split into parts, and the
+// capacity of the fp32 partial blocks ([128][r_pad] each) and arrival counters (x4) it may use.
+constexpr int kGramMaxSlots = 512;
+constexpr int kGramMaxPartials = 640;
+constexpr int kGramMaxCounters = 1280;
+inline size_t gram_scratch_bytes(int r_pad) {
+  return (static_cast<size_t>(kGramMaxPartials) * 128 * r_pad * 4 + static_cast<size_t>(kGramMaxCounters) * 4 * 8 +
+          255) & ~size_t(255);
+}
 // planes: S_ext planes to sum (1, or 2 when the K-half partial products of the co-scheduled
 // shrink are read); s_map must then cover both planes.
-cudaError_t tc_gram(int dtype, const CUtensorMap& d_map, const CUtensorMap& s_map, int C, const Tables& tb,
-                    void* out, int transpose_out, int num_sms, cudaStream_t st, int planes = 1);
+// Gram jobs (dB: D = g, C = N, S = s.x.A^T, grad [N, r] blocks; dA: D = x, C = K, S = s.g.B,
+// transposed [r, K] blocks), up to two in one launch.  `scratch` (gram_scratch_bytes(r_pad), any
+// contents) holds the partial sums of split slots; nullptr disables splitting.  `gen` must differ
+// from every earlier launch's on that scratch.  planes: S_ext planes to sum (1, or 2 when the
+// K-half partial products of the co-scheduled shrink are read); s maps must then cover both.
+struct GramJobDesc {
+  CUtensorMap d_map;  // D [T, C] box (64, 128)
+  CUtensorMap s_map;  // S_ext planes [planes * (n_st+1) * 128, r_pad] box (r_pad, 128)
+  int C;
+  void* out;
+  int transpose_out;
+};
+cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables& tb, int num_sms, cudaStream_t st,
+                    int planes = 1, void* scratch = nullptr, uint64_t gen = 0);
 
 // --------------------------------------------------------------- packing
 cudaError_t pack_adapters(int src_dtype, int dst_dtype, const uint64_t* src_ptrs, const int32_t* ranks,

@@ -1140,67 +1140,161 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ========================================================================== gram (dA / dB)
-struct GramParams {
+// grad[slot] = sum over the slot's segment tiles of D_tile^T . S_ext[seg] for up to two jobs in one
+// launch (the backward's dB: D = g, C = N, S = s.x.A^T; and dA: D = x, C = K, S = s.g.B).
+struct GramJob {
   void* out;
-  int C;
-  int n_cblk;
-  int transpose_out;
+  int C, n_cblk, transpose_out;
+};
+struct GramParams {
+  GramJob job[2];
+  int n_jobs;
   int planes, s_plane_rows;  // S_ext planes summed (2: K-half partial products)
   int r_pad;
+  int n_stages, stage_bytes;  // ring of stages: 128x128 D tile, then `planes` S tiles
   uint32_t idesc;
   uint32_t s_layout, s_sbo, s_kstep;
+  // Load balance: a slot with more than `cap` segment tiles is split into parts of about equal
+  // size (0: never split).  Parts of a split slot write fp32 partial sums; per (job, slot, column
+  // block, epilogue warp) the last part to arrive adds them up in part order.
+  int cap;
+  float* partial;      // [kGramMaxPartials][128][r_pad]
+  uint64_t* counters;  // [kGramMaxCounters][4] arrival words, generation in the high half
+  uint32_t gen32;
   Tables tb;
 };
 
 constexpr int kGramDBytes = kBM * 128 * 2;  // 128 rows x 128 columns
-constexpr int kGramSBytes = 2 * kBM * 64 * 2;  // up to two planes of 128 rows x r_pad (<= 64)
-constexpr int kGramSmem = 1024 + kGramStages * (kGramDBytes + kGramSBytes) + 24 * 128 + 256;
+constexpr int kGramMaxStages = 8;
+constexpr int kGramRingBytes = 3 * (kGramDBytes + 2 * kBM * 64 * 2);  // 3 stages at r_pad 64 with 2 planes
 
-// Work units of one CTA (slot, column block), staged in shared memory once so no role
-// waits on a dependent table load per unit.  Units past kGramMaxUnits read the table directly.
+// Work units of one CTA (job, slot part, column block), staged in shared memory once with the
+// segment tiles each one streams, so no role waits on a dependent table load per unit.
 constexpr int kGramMaxUnits = 128;
+constexpr int kGramMaxSteps = 512;
 struct GramUnit {
-  int slot, b, e, rank, rank_prefix, cb;
+  int job, slot, b, e, rank, rank_prefix, cb;
+  int parts;  // parts of this slot (1: written straight from TMEM)
+  int pid;    // partial block of this part
+  int pbase;  // partial block of part 0; part p is pbase + p * n_cblk
+  int cid;    // counter row (x4 warps)
+  int s0;     // first staged step, or -1 (steps read from the table)
 };
+// Per slot position (slot_order index), read from the table once per CTA: the slot's metadata and,
+// per job, prefix sums of parts, split parts and split slots.  Only when n_slots <= kGramMaxSlots
+// (`cached`); otherwise units are decoded from the table and never split.
+struct GramSlotPrefix {
+  int slot[kGramMaxSlots], b0[kGramMaxSlots], nst[kGramMaxSlots], rank[kGramMaxSlots], rprefix[kGramMaxSlots];
+  int part[2][kGramMaxSlots + 1];
+  int split_part[2][kGramMaxSlots + 1];
+  int split_slot[2][kGramMaxSlots + 1];
+  int units[2];           // units of each job
+  int pid_off, cid_off;   // job 1's partial blocks and counter rows follow job 0's
+  int use_split, cached;
+};
+struct GramStep {
+  int st, row0;
+};
+constexpr int kGramSmem = 1024 + kGramRingBytes + kGramMaxUnits * static_cast<int>(sizeof(GramUnit)) +
+                          static_cast<int>(sizeof(GramSlotPrefix)) + kGramMaxSteps * static_cast<int>(sizeof(GramStep)) +
+                          256;
+static_assert(kGramSmem <= 227 * 1024, "gram kernel shared memory");
 
-__device__ __forceinline__ GramUnit gram_unit_from_table(const Tables& tb, int u, int n_cblk) {
+// Unit k of the combined list (job 0's units, then job 1's): part k / n_cblk of the job's parts,
+// listed slot after slot in slot_order, column block k % n_cblk.
+__device__ __forceinline__ GramUnit gram_unit(const GramParams& prm, const GramSlotPrefix& sp, int k) {
+  const Tables& tb = prm.tb;
   GramUnit g;
-  g.slot = tb.slot_order(u / n_cblk);
-  g.cb = u % n_cblk;
-  g.b = tb.slot_st(g.slot);
-  g.e = tb.slot_st(g.slot + 1);
-  g.rank = tb.slot_rank(g.slot);
-  g.rank_prefix = tb.rank_prefix(g.slot);
+  g.job = k < sp.units[0] ? 0 : 1;
+  const int kl = k - (g.job ? sp.units[0] : 0);
+  const int n_cblk = prm.job[g.job].n_cblk;
+  const int pg = kl / n_cblk;
+  g.cb = kl - pg * n_cblk;
+  g.parts = 1;
+  g.pid = g.pbase = g.cid = 0;
+  g.s0 = -1;
+  if (!sp.cached) {
+    g.slot = tb.slot_order(pg);
+    g.b = tb.slot_st(g.slot);
+    g.e = tb.slot_st(g.slot + 1);
+    g.rank = tb.slot_rank(g.slot);
+    g.rank_prefix = tb.rank_prefix(g.slot);
+    return g;
+  }
+  int pos = pg, p = 0;
+  if (sp.use_split) {  // last slot position whose first part is <= pg
+    const int* part = sp.part[g.job];
+    int lo = 0, hi = tb.n_slots - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (part[mid] <= pg) lo = mid;
+      else hi = mid - 1;
+    }
+    pos = lo;
+    p = pg - part[pos];
+    g.parts = part[pos + 1] - part[pos];
+  }
+  g.slot = sp.slot[pos];
+  const int b0 = sp.b0[pos], nst = sp.nst[pos];
+  g.b = b0 + static_cast<int>(static_cast<int64_t>(p) * nst / g.parts);
+  g.e = b0 + static_cast<int>(static_cast<int64_t>(p + 1) * nst / g.parts);
+  g.rank = sp.rank[pos];
+  g.rank_prefix = sp.rprefix[pos];
+  if (g.parts > 1) {
+    g.pbase = (g.job ? sp.pid_off : 0) + sp.split_part[g.job][pos] * n_cblk + g.cb;
+    g.pid = g.pbase + p * n_cblk;
+    g.cid = (g.job ? sp.cid_off : 0) + sp.split_slot[g.job][pos] * n_cblk + g.cb;
+  }
   return g;
+}
+
+// k-th unit of CTA `me` among `G`: units are dealt zig-zag (0..G-1, then G-1..0, ...) so that,
+// listed largest first, every CTA gets a similar share.
+__device__ __forceinline__ int gram_zigzag(int r, int me, int G) { return r * G + ((r & 1) ? G - 1 - me : me); }
+
+// Arrival on a per-launch counter word (generation in the high 32 bits); returns the count after
+// this arrival, or 0 after a bounded number of failed tries (error recorded).
+__device__ __forceinline__ uint32_t gen_arrive(uint64_t* ctr, uint32_t gen32, int* err) {
+  unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(ctr);
+  for (int i = 0; i < (1 << 20); ++i) {
+    const bool same = static_cast<uint32_t>(cur >> 32) == gen32;
+    const unsigned long long next = same ? cur + 1ull : ((static_cast<unsigned long long>(gen32) << 32) | 1ull);
+    const unsigned long long seen = atomicCAS(reinterpret_cast<unsigned long long*>(ctr), cur, next);
+    if (seen == cur) return static_cast<uint32_t>(next);
+    cur = seen;
+  }
+  record_error(err, kErrTimeoutFlag);
+  return 0;
 }
 
 template <typename OutT>
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_gram_kernel(const __grid_constant__ CUtensorMap map_d, const __grid_constant__ CUtensorMap map_s,
+    tc_gram_kernel(const __grid_constant__ CUtensorMap map_d0, const __grid_constant__ CUtensorMap map_s0,
+                   const __grid_constant__ CUtensorMap map_d1, const __grid_constant__ CUtensorMap map_s1,
                    const GramParams prm) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sD = smem;
-  uint8_t* sS = smem + kGramStages * kGramDBytes;
-  GramUnit* units = reinterpret_cast<GramUnit*>(sS + kGramStages * kGramSBytes);
-  uint64_t* full = reinterpret_cast<uint64_t*>(units + kGramMaxUnits);
-  uint64_t* empty = full + kGramStages;
-  uint64_t* tfull = empty + kGramStages;
+  uint8_t* ring = smem;
+  GramUnit* units = reinterpret_cast<GramUnit*>(ring + kGramRingBytes);
+  GramSlotPrefix& sp = *reinterpret_cast<GramSlotPrefix*>(units + kGramMaxUnits);
+  GramStep* steps = reinterpret_cast<GramStep*>(&sp + 1);
+  uint64_t* full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(steps + kGramMaxSteps) + 7) & ~uintptr_t(7));
+  uint64_t* empty = full + kGramMaxStages;
+  uint64_t* tfull = empty + kGramMaxStages;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* n_staged_steps = const_cast<int*>(abort_flag) + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Tables& tb = prm.tb;
-  const int total = tb.n_slots * prm.n_cblk;
-  const int n_mine = total > static_cast<int>(blockIdx.x)
-                         ? (total - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) / gridDim.x
-                         : 0;
+  const int me = static_cast<int>(blockIdx.x), G = static_cast<int>(gridDim.x);
   const int r_pad = prm.r_pad;
+  const int n_stages = prm.n_stages;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kGramStages; ++s) {
+    for (int s = 0; s < n_stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -1211,88 +1305,196 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
-    tma_prefetch_desc(&map_d);
-    tma_prefetch_desc(&map_s);
-  }
-  if (warp >= 2) {  // stage this CTA's unit schedule
-    for (int k = threadIdx.x - 64; k < n_mine && k < kGramMaxUnits; k += kThreads - 64)
-      units[k] = gram_unit_from_table(tb, static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x), prm.n_cblk);
+    tma_prefetch_desc(&map_d0);
+    tma_prefetch_desc(&map_s0);
+    if (prm.n_jobs > 1) {
+      tma_prefetch_desc(&map_d1);
+      tma_prefetch_desc(&map_s1);
+    }
   }
   if (warp == 1) {
     __syncwarp();
     tmem_alloc(tmem_slot, 128);
     tmem_relinquish();
   }
+
+  // Slot metadata and parts per slot position (warp 2): slots with more than `cap` segment tiles
+  // are split, unless the partial blocks or counters that needs would not fit; every CTA decides
+  // the same way.
+  if (warp == 2) {
+    int tp[2] = {0, 0}, ts[2] = {0, 0}, tss[2] = {0, 0};
+    const bool cached = tb.n_slots <= kGramMaxSlots;
+    const bool try_split = cached && prm.cap > 0 && prm.partial != nullptr;
+    if (cached) {
+      for (int i0 = 0; i0 < tb.n_slots; i0 += 32) {
+        const int i = i0 + lane;
+        int nst = 0;
+        if (i < tb.n_slots) {
+          const int sl = tb.slot_order(i);
+          const int b0 = tb.slot_st(sl);
+          nst = tb.slot_st(sl + 1) - b0;
+          sp.slot[i] = sl;
+          sp.b0[i] = b0;
+          sp.nst[i] = nst;
+          sp.rank[i] = tb.slot_rank(sl);
+          sp.rprefix[i] = tb.rank_prefix(sl);
+        }
+        // parts are the same for both jobs (one cap); lanes past the end count nothing
+        const int P = i >= tb.n_slots ? 0 : (try_split && nst > prm.cap) ? (nst + prm.cap - 1) / prm.cap : 1;
+        int a = P, b = P > 1 ? P : 0, c = P > 1 ? 1 : 0;  // inclusive warp scans
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+          const int ua = __shfl_up_sync(0xffffffffu, a, d), ub = __shfl_up_sync(0xffffffffu, b, d),
+                    uc = __shfl_up_sync(0xffffffffu, c, d);
+          if (lane >= d) {
+            a += ua;
+            b += ub;
+            c += uc;
+          }
+        }
+        if (i < tb.n_slots)
+          for (int j = 0; j < 2; ++j) {
+            sp.part[j][i] = tp[j] + a - P;
+            sp.split_part[j][i] = ts[j] + b - (P > 1 ? P : 0);
+            sp.split_slot[j][i] = tss[j] + c - (P > 1 ? 1 : 0);
+          }
+        const int ta = __shfl_sync(0xffffffffu, a, 31), tb2 = __shfl_sync(0xffffffffu, b, 31),
+                  tc = __shfl_sync(0xffffffffu, c, 31);
+        for (int j = 0; j < 2; ++j) {
+          tp[j] += ta;
+          ts[j] += tb2;
+          tss[j] += tc;
+        }
+      }
+    }
+    int64_t need_p = 0, need_c = 0;
+    for (int j = 0; j < prm.n_jobs; ++j) {
+      need_p += static_cast<int64_t>(ts[j]) * prm.job[j].n_cblk;
+      need_c += static_cast<int64_t>(tss[j]) * prm.job[j].n_cblk;
+    }
+    const bool fits = try_split && ts[0] > 0 && need_p <= kGramMaxPartials && need_c <= kGramMaxCounters;
+    if (!fits && cached) {  // one part per slot
+      for (int i = lane; i < tb.n_slots; i += 32) sp.part[0][i] = sp.part[1][i] = i;
+      tp[0] = tp[1] = tb.n_slots;
+    }
+    if (lane == 0) {
+      sp.cached = cached ? 1 : 0;
+      sp.use_split = fits ? 1 : 0;
+      if (cached) sp.part[0][tb.n_slots] = sp.part[1][tb.n_slots] = tp[0];
+      const int slots_or_parts = cached ? tp[0] : tb.n_slots;
+      sp.units[0] = slots_or_parts * prm.job[0].n_cblk;
+      sp.units[1] = prm.n_jobs > 1 ? slots_or_parts * prm.job[1].n_cblk : 0;
+      sp.pid_off = ts[0] * prm.job[0].n_cblk;
+      sp.cid_off = tss[0] * prm.job[0].n_cblk;
+    }
+  }
+  __syncthreads();
+  const int total = sp.units[0] + sp.units[1];
+  int n_mine = 0;
+  for (int r = 0; r * G < total; ++r) n_mine += gram_zigzag(r, me, G) < total ? 1 : 0;
+  const int n_staged = n_mine < kGramMaxUnits ? n_mine : kGramMaxUnits;
+  if (warp >= 2) {  // stage this CTA's units
+    for (int k = threadIdx.x - 64; k < n_staged; k += kThreads - 64) units[k] = gram_unit(prm, sp, gram_zigzag(k, me, G));
+  }
+  __syncthreads();
+  if (warp == 2) {  // step offsets of the staged units, in order, as long as they fit
+    int base = 0, fitted = 0;
+    for (int k0 = 0; k0 < n_staged; k0 += 32) {
+      const int k = k0 + lane;
+      const int len = k < n_staged ? units[k].e - units[k].b : 0;
+      int incl = len;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += u;
+      }
+      const int s0 = base + incl - len;
+      const bool fit = s0 + len <= kGramMaxSteps;
+      if (k < n_staged) units[k].s0 = fit ? s0 : -1;
+      const int f = fit && k < n_staged ? s0 + len : 0;
+      fitted = max(fitted, __reduce_max_sync(0xffffffffu, f));
+      base += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) *n_staged_steps = fitted;
+  }
+  __syncthreads();
+  if (warp >= 2) {  // each staged step's segment tile and D row
+    const int n_steps = *n_staged_steps;
+    for (int f = threadIdx.x - 64; f < n_steps; f += kThreads - 64) {
+      int lo = 0, hi = n_staged - 1;  // unit holding flat step f: last staged unit with s0 <= f
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (units[mid].s0 >= 0 && units[mid].s0 <= f) lo = mid;
+        else if (units[mid].s0 < 0) hi = mid - 1;
+        else hi = mid - 1;
+      }
+      const int st = tb.slot_list(units[lo].b + f - units[lo].s0);
+      steps[f].st = st;
+      steps[f].row0 = tb.st_tile(st) * kBM;
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  auto unit = [&](int k) -> GramUnit {
-    return k < kGramMaxUnits ? units[k]
-                             : gram_unit_from_table(tb, static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x),
-                                                    prm.n_cblk);
-  };
+  auto unit = [&](int k) -> GramUnit { return k < kGramMaxUnits ? units[k] : gram_unit(prm, sp, gram_zigzag(k, me, G)); };
 
   if (warp == 0) {
-    // The whole warp walks the segment-tile lists 32 entries at a time; lane 0 issues the copies.
-    int stage = 0;
-    uint32_t phase = 0, issued_mask = 0, last_parity = 0;
-    bool ok = true;
-    const uint32_t bytes = static_cast<uint32_t>(kGramDBytes + prm.planes * kBM * r_pad * 2);
-    for (int k = 0; k < n_mine && ok; ++k) {
-      const GramUnit g = unit(k);
-      for (int i0 = g.b; i0 < g.e && ok; i0 += 32) {
-        int st = 0, row0 = 0;
-        if (i0 + lane < g.e) {
-          st = tb.slot_list(i0 + lane);
-          row0 = tb.st_tile(st) * kBM;
-        }
-        const int cnt = min(32, g.e - i0);
-        for (int q = 0; q < cnt; ++q) {
-          const int st_q = __shfl_sync(0xffffffffu, st, q);
-          const int row_q = __shfl_sync(0xffffffffu, row0, q);
-          int go = 1;
-          if (lane == 0) {
-            go = mbar_wait(&empty[stage], phase ^ 1, abort_flag, prm.tb.err, kErrTimeoutEmpty) ? 1 : 0;
-            if (go) {
-              mbar_arrive_expect_tx(&full[stage], bytes);
-              tma_load_2d(sD + stage * kGramDBytes, &map_d, &full[stage], g.cb * 128, row_q);
-              tma_load_2d(sD + stage * kGramDBytes + kGramDBytes / 2, &map_d, &full[stage], g.cb * 128 + 64, row_q);
-              for (int pl = 0; pl < prm.planes; ++pl)
-                tma_load_2d(sS + stage * kGramSBytes + pl * (kGramSBytes / 2), &map_s, &full[stage], 0,
-                            pl * prm.s_plane_rows + st_q * kBM);
-            }
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, issued_mask = 0, last_parity = 0;
+      bool ok = true;
+      const uint32_t s_bytes = static_cast<uint32_t>(kBM * r_pad * 2);
+      const uint32_t bytes = static_cast<uint32_t>(kGramDBytes) + prm.planes * s_bytes;
+      for (int k = 0; k < n_mine && ok; ++k) {
+        const GramUnit g = unit(k);
+        const CUtensorMap* md = g.job ? &map_d1 : &map_d0;
+        const CUtensorMap* ms = g.job ? &map_s1 : &map_s0;
+        for (int i = g.b; i < g.e && ok; ++i) {
+          int st, row0;
+          if (g.s0 >= 0) {
+            st = steps[g.s0 + i - g.b].st;
+            row0 = steps[g.s0 + i - g.b].row0;
+          } else {
+            st = tb.slot_list(i);
+            row0 = tb.st_tile(st) * kBM;
           }
-          go = __shfl_sync(0xffffffffu, go, 0);
-          if (!go) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, tb.err, kErrTimeoutEmpty)) {
             ok = false;
             break;
           }
+          mbar_arrive_expect_tx(&full[stage], bytes);
+          uint8_t* sD = ring + stage * prm.stage_bytes;
+          tma_load_2d(sD, md, &full[stage], g.cb * 128, row0);
+          tma_load_2d(sD + kGramDBytes / 2, md, &full[stage], g.cb * 128 + 64, row0);
+          for (int pl = 0; pl < prm.planes; ++pl)
+            tma_load_2d(sD + kGramDBytes + pl * s_bytes, ms, &full[stage], 0, pl * prm.s_plane_rows + st * kBM);
           issued_mask |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
-          if (++stage == kGramStages) {
+          if (++stage == n_stages) {
             stage = 0;
             phase ^= 1;
           }
         }
       }
+      if (!ok)
+        for (int s = 0; s < n_stages; ++s)
+          if (issued_mask & (1u << s)) drain_wait(&full[s], (last_parity >> s) & 1u, tb.err);
     }
-    if (!ok && lane == 0)
-      for (int s = 0; s < kGramStages; ++s)
-        if (issued_mask & (1u << s)) drain_wait(&full[s], (last_parity >> s) & 1u, prm.tb.err);
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true, issued_any = false;
-      const uint32_t d_base = smem_u32(sD), s_base = smem_u32(sS);
+      const uint32_t ring_base = smem_u32(ring);
+      const uint32_t s_bytes = static_cast<uint32_t>(kBM * r_pad * 2);
       int it = 0;
       for (int k = 0; k < n_mine && ok; ++k) {
         const GramUnit g = unit(k);
         if (g.b == g.e) continue;  // adapter with only empty routes: epilogue writes zeros
         const int buf = it & 1;
-        if (!mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1, abort_flag, prm.tb.err, kErrTimeoutAcc)) {
+        if (!mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1, abort_flag, tb.err, kErrTimeoutAcc)) {
           ok = false;
           break;
         }
@@ -1300,14 +1502,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t dt = tmem_base + static_cast<uint32_t>(buf * 64);
         uint32_t acc = 0;
         for (int i = g.b; i < g.e; ++i) {
-          if (!mbar_wait(&full[stage], phase, abort_flag, prm.tb.err, kErrTimeoutFull)) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, tb.err, kErrTimeoutFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = d_base + stage * kGramDBytes;
+          const uint32_t a0 = ring_base + stage * prm.stage_bytes;
           for (int pl = 0; pl < prm.planes; ++pl) {
-            const uint32_t b0 = s_base + stage * kGramSBytes + pl * (kGramSBytes / 2);
+            const uint32_t b0 = a0 + kGramDBytes + pl * s_bytes;
 #pragma unroll
             for (int kk = 0; kk < kBM / 16; ++kk) {
               const uint64_t adesc = umma_sdesc(a0 + kk * 2048, kGramDBytes / 2, 1024, 2);
@@ -1318,7 +1520,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           issued_any = true;
           umma_commit(&empty[stage]);
-          if (++stage == kGramStages) {
+          if (++stage == n_stages) {
             stage = 0;
             phase ^= 1;
           }
@@ -1329,45 +1531,108 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok && issued_any) {
         umma_commit(drain);
-        drain_wait(drain, 0, prm.tb.err);
+        drain_wait(drain, 0, tb.err);
       }
     }
     __syncwarp();
   } else {
     const int q = warp & 3;
+    const int col = q * 32 + lane;
     int it = 0;
-    OutT* out = reinterpret_cast<OutT*>(prm.out);
     for (int k = 0; k < n_mine; ++k) {
       const GramUnit g = unit(k);
-      const int c = g.cb * 128 + q * 32 + lane;
+      const GramJob& jb = prm.job[g.job];
+      const int c = g.cb * 128 + col;
       const int rank = g.rank;
-      OutT* o = out + static_cast<int64_t>(g.rank_prefix) * prm.C;
+      OutT* o = reinterpret_cast<OutT*>(jb.out) + static_cast<int64_t>(g.rank_prefix) * jb.C;
       if (g.b == g.e) {
-        if (c < prm.C)
+        if (c < jb.C)
           for (int j = 0; j < rank; ++j) {
-            if (prm.transpose_out)
-              o[static_cast<int64_t>(j) * prm.C + c] = cvt_out<OutT>(0.f);
+            if (jb.transpose_out)
+              o[static_cast<int64_t>(j) * jb.C + c] = cvt_out<OutT>(0.f);
             else
               o[static_cast<int64_t>(c) * rank + j] = cvt_out<OutT>(0.f);
           }
         continue;
       }
       const int buf = it & 1;
-      if (!warp_wait(&tfull[buf], (it >> 1) & 1, abort_flag, prm.tb.err, kErrTimeoutAcc)) break;
+      if (!warp_wait(&tfull[buf], (it >> 1) & 1, abort_flag, tb.err, kErrTimeoutAcc)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * 64);
+      if (g.parts > 1) {
+        // part of a split slot: fp32 partial of this warp's 32 columns; the last of the slot's
+        // parts to arrive (per column block and warp) adds the parts in part order
+        float* mine = prm.partial + (static_cast<int64_t>(g.pid) * 128 + col) * r_pad;
+        for (int j0 = 0; j0 < r_pad; j0 += 16) {
+          uint32_t v[16];
+          tmem_ld16(tbase + j0, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int jj = 0; jj < 16; jj += 4)
+            *reinterpret_cast<float4*>(mine + j0 + jj) =
+                make_float4(__uint_as_float(v[jj]), __uint_as_float(v[jj + 1]), __uint_as_float(v[jj + 2]),
+                            __uint_as_float(v[jj + 3]));
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[buf]);
+        ++it;
+        __threadfence();
+        __syncwarp();
+        int last = 0;
+        if (lane == 0)
+          last = gen_arrive(prm.counters + static_cast<int64_t>(g.cid) * 4 + q, prm.gen32, tb.err) ==
+                         static_cast<uint32_t>(g.parts)
+                     ? 1
+                     : 0;
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) continue;
+        __threadfence();
+        for (int j0 = 0; j0 < r_pad; j0 += 16) {  // 16 sums per step, parts added in order
+          float acc[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) acc[jj] = 0.f;
+          for (int pp = 0; pp < g.parts; ++pp) {
+            const float4* src = reinterpret_cast<const float4*>(
+                prm.partial + (static_cast<int64_t>(g.pbase + pp * jb.n_cblk) * 128 + col) * r_pad + j0);
+            float4 v4[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) v4[t] = __ldcg(src + t);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              acc[4 * t] += v4[t].x;
+              acc[4 * t + 1] += v4[t].y;
+              acc[4 * t + 2] += v4[t].z;
+              acc[4 * t + 3] += v4[t].w;
+            }
+          }
+          if (c < jb.C) {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int j = j0 + jj;
+              if (j < rank) {
+                const OutT val = cvt_out<OutT>(acc[jj]);
+                if (jb.transpose_out)
+                  o[static_cast<int64_t>(j) * jb.C + c] = val;
+                else
+                  o[static_cast<int64_t>(c) * rank + j] = val;
+              }
+            }
+          }
+        }
+        continue;
+      }
       for (int j0 = 0; j0 < r_pad; j0 += 16) {
         uint32_t v[16];
         tmem_ld16(tbase + j0, v);
         tmem_wait_ld();
-        if (c < prm.C) {
+        if (c < jb.C) {
 #pragma unroll
           for (int jj = 0; jj < 16; ++jj) {
             const int j = j0 + jj;
             if (j < rank) {
               const OutT val = cvt_out<OutT>(__uint_as_float(v[jj]));
-              if (prm.transpose_out)
-                o[static_cast<int64_t>(j) * prm.C + c] = val;
+              if (jb.transpose_out)
+                o[static_cast<int64_t>(j) * jb.C + c] = val;
               else
                 o[static_cast<int64_t>(c) * rank + j] = val;
             }
@@ -1597,34 +1862,54 @@ cudaError_t tc_shrink(int dtype, const CUtensorMap& p_map, const CUtensorMap& a_
   return cudaGetLastError();
 }
 
-cudaError_t tc_gram(int dtype, const CUtensorMap& d_map, const CUtensorMap& s_map, int C, const Tables& tb, void* out,
-                    int transpose_out, int num_sms, cudaStream_t st, int planes) {
+cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables& tb, int num_sms, cudaStream_t st,
+                    int planes, void* scratch, uint64_t gen) {
+  if (n_jobs < 1 || n_jobs > 2) return cudaErrorInvalidValue;
   GramParams p{};
-  p.out = out;
-  p.C = C;
-  p.n_cblk = (C + 127) / 128;
-  p.transpose_out = transpose_out;
+  p.n_jobs = n_jobs;
+  int64_t steps = 0, most = 0;
+  for (int j = 0; j < n_jobs; ++j) {
+    p.job[j].out = jobs[j].out;
+    p.job[j].C = jobs[j].C;
+    p.job[j].n_cblk = (jobs[j].C + 127) / 128;
+    p.job[j].transpose_out = jobs[j].transpose_out;
+    steps += static_cast<int64_t>(tb.n_segtiles) * p.job[j].n_cblk;
+    most += static_cast<int64_t>(tb.n_segtiles + tb.n_slots) * p.job[j].n_cblk;  // units once split
+  }
   p.planes = planes;
   p.s_plane_rows = (tb.n_segtiles + 1) * kBM;
   p.r_pad = tb.r_pad;
+  p.stage_bytes = kGramDBytes + planes * kBM * tb.r_pad * 2;
+  p.n_stages = kGramRingBytes / p.stage_bytes;
+  if (p.n_stages > kGramMaxStages) p.n_stages = kGramMaxStages;
   const int fmt = dtype == LF_BF16 ? 1 : 0;
   p.idesc = umma_idesc_f16(kBM, tb.r_pad, fmt, 1, 1);
   p.s_layout = umma_layout_for_span(tb.r_pad * 2);
   p.s_sbo = sw_sbo(tb.r_pad);
   p.s_kstep = static_cast<uint32_t>(16 * tb.r_pad * 2);
   p.tb = tb;
-  const int total = tb.n_slots * p.n_cblk;
-  if (total == 0) return cudaSuccess;
-  const int grid = total < num_sms ? total : num_sms;
+  if (tb.n_slots == 0 || most == 0) return cudaSuccess;
+  const int grid = static_cast<int>(most < num_sms ? most : num_sms);
+  if (scratch != nullptr && tb.n_slots <= kGramMaxSlots) {
+    // Parts of at most ~half a CTA's even share of segment-tile steps.
+    const int64_t share = (steps + 2 * grid - 1) / (2 * grid);
+    p.cap = static_cast<int>(share < 2 ? 2 : share);
+    p.partial = static_cast<float*>(scratch);
+    p.counters = reinterpret_cast<uint64_t*>(static_cast<char*>(scratch) +
+                                             static_cast<size_t>(kGramMaxPartials) * 128 * tb.r_pad * 4);
+    p.gen32 = static_cast<uint32_t>(gen);
+  }
+  const CUtensorMap& d1 = jobs[n_jobs - 1].d_map;
+  const CUtensorMap& s1 = jobs[n_jobs - 1].s_map;
   cudaError_t e;
   if (dtype == LF_BF16) {
     e = ensure_smem(tc_gram_kernel<__nv_bfloat16>, kGramSmem);
     if (e != cudaSuccess) return e;
-    tc_gram_kernel<__nv_bfloat16><<<grid, kThreads, kGramSmem, st>>>(d_map, s_map, p);
+    tc_gram_kernel<__nv_bfloat16><<<grid, kThreads, kGramSmem, st>>>(jobs[0].d_map, jobs[0].s_map, d1, s1, p);
   } else {
     e = ensure_smem(tc_gram_kernel<__half>, kGramSmem);
     if (e != cudaSuccess) return e;
-    tc_gram_kernel<__half><<<grid, kThreads, kGramSmem, st>>>(d_map, s_map, p);
+    tc_gram_kernel<__half><<<grid, kThreads, kGramSmem, st>>>(jobs[0].d_map, jobs[0].s_map, d1, s1, p);
   }
   return cudaGetLastError();
 }
