@@ -1152,6 +1152,10 @@ struct GramParams {
   int planes, s_plane_rows;  // S_ext planes summed (2: K-half partial products)
   int r_pad;
   int n_stages, stage_bytes;  // ring of stages: 128x128 D tile, then `planes` S tiles
+  // One MMA per 16-row K step covers every plane (N = planes * r_pad: the planes are consecutive
+  // MN chunks of the B operand).  K steps rotate over `chains` accumulators so that consecutive
+  // MMAs do not wait on each other; the epilogue adds chains and planes in fixed order.
+  int chains, acc_cols, tmem_cols;  // acc_cols = chains * planes * r_pad per buffer
   uint32_t idesc;
   uint32_t s_layout, s_sbo, s_kstep;
   // Load balance: a slot with more than `cap` segment tiles is split into parts of about equal
@@ -1314,7 +1318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 1) {
     __syncwarp();
-    tmem_alloc(tmem_slot, 128);
+    tmem_alloc(tmem_slot, static_cast<uint32_t>(prm.tmem_cols));
     tmem_relinquish();
   }
 
@@ -1499,8 +1503,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t dt = tmem_base + static_cast<uint32_t>(buf * 64);
-        uint32_t acc = 0;
+        const uint32_t dt = tmem_base + static_cast<uint32_t>(buf * prm.acc_cols);
+        const uint32_t chain_cols = static_cast<uint32_t>(prm.acc_cols / prm.chains);
+        uint32_t started = 0;  // chains that hold a partial sum already
         for (int i = g.b; i < g.e; ++i) {
           if (!mbar_wait(&full[stage], phase, abort_flag, tb.err, kErrTimeoutFull)) {
             ok = false;
@@ -1508,15 +1513,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t a0 = ring_base + stage * prm.stage_bytes;
-          for (int pl = 0; pl < prm.planes; ++pl) {
-            const uint32_t b0 = a0 + kGramDBytes + pl * s_bytes;
+          const uint32_t b0 = a0 + kGramDBytes;
 #pragma unroll
-            for (int kk = 0; kk < kBM / 16; ++kk) {
-              const uint64_t adesc = umma_sdesc(a0 + kk * 2048, kGramDBytes / 2, 1024, 2);
-              const uint64_t bdesc = umma_sdesc(b0 + kk * prm.s_kstep, kBM * r_pad * 2, prm.s_sbo, prm.s_layout);
-              umma_f16(dt, adesc, bdesc, prm.idesc, acc);
-              acc = 1;
-            }
+          for (int kk = 0; kk < kBM / 16; ++kk) {
+            const int ch = kk % prm.chains;
+            const uint64_t adesc = umma_sdesc(a0 + kk * 2048, kGramDBytes / 2, 1024, 2);
+            const uint64_t bdesc = umma_sdesc(b0 + kk * prm.s_kstep, s_bytes, prm.s_sbo, prm.s_layout);
+            umma_f16(dt + ch * chain_cols, adesc, bdesc, prm.idesc, (started >> ch) & 1u);
+            started |= 1u << ch;
           }
           issued_any = true;
           umma_commit(&empty[stage]);
@@ -1558,20 +1562,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int buf = it & 1;
       if (!warp_wait(&tfull[buf], (it >> 1) & 1, abort_flag, tb.err, kErrTimeoutAcc)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * 64);
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * prm.acc_cols);
+      const int chain_cols = prm.acc_cols / prm.chains;
+      // 16 columns j0.. of this thread's row: chains and planes added in fixed order
+      auto load_sum16 = [&](int j0, float* out16) {
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) out16[jj] = 0.f;
+        for (int ch = 0; ch < prm.chains; ++ch)
+          for (int pl = 0; pl < prm.planes; ++pl) {
+            uint32_t v[16];
+            tmem_ld16(tbase + ch * chain_cols + pl * r_pad + j0, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) out16[jj] += __uint_as_float(v[jj]);
+          }
+      };
       if (g.parts > 1) {
         // part of a split slot: fp32 partial of this warp's 32 columns; the last of the slot's
         // parts to arrive (per column block and warp) adds the parts in part order
         float* mine = prm.partial + (static_cast<int64_t>(g.pid) * 128 + col) * r_pad;
         for (int j0 = 0; j0 < r_pad; j0 += 16) {
-          uint32_t v[16];
-          tmem_ld16(tbase + j0, v);
-          tmem_wait_ld();
+          float v[16];
+          load_sum16(j0, v);
 #pragma unroll
           for (int jj = 0; jj < 16; jj += 4)
-            *reinterpret_cast<float4*>(mine + j0 + jj) =
-                make_float4(__uint_as_float(v[jj]), __uint_as_float(v[jj + 1]), __uint_as_float(v[jj + 2]),
-                            __uint_as_float(v[jj + 3]));
+            *reinterpret_cast<float4*>(mine + j0 + jj) = make_float4(v[jj], v[jj + 1], v[jj + 2], v[jj + 3]);
         }
         tc_fence_before();
         mbar_arrive(&tempty[buf]);
@@ -1622,15 +1637,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
       for (int j0 = 0; j0 < r_pad; j0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(tbase + j0, v);
-        tmem_wait_ld();
+        float v[16];
+        load_sum16(j0, v);
         if (c < jb.C) {
 #pragma unroll
           for (int jj = 0; jj < 16; ++jj) {
             const int j = j0 + jj;
             if (j < rank) {
-              const OutT val = cvt_out<OutT>(__uint_as_float(v[jj]));
+              const OutT val = cvt_out<OutT>(v[jj]);
               if (jb.transpose_out)
                 o[static_cast<int64_t>(j) * jb.C + c] = val;
               else
@@ -1649,7 +1663,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 128);
+    tmem_dealloc(tmem_base, static_cast<uint32_t>(prm.tmem_cols));
   }
 }
 
@@ -1883,7 +1897,13 @@ cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables
   p.n_stages = kGramRingBytes / p.stage_bytes;
   if (p.n_stages > kGramMaxStages) p.n_stages = kGramMaxStages;
   const int fmt = dtype == LF_BF16 ? 1 : 0;
-  p.idesc = umma_idesc_f16(kBM, tb.r_pad, fmt, 1, 1);
+  const int width = planes * tb.r_pad;  // MMA N
+  p.chains = 4;
+  while (p.chains > 1 && 2 * p.chains * width > 512) p.chains >>= 1;
+  p.acc_cols = p.chains * width;
+  p.tmem_cols = 32;
+  while (p.tmem_cols < 2 * p.acc_cols) p.tmem_cols <<= 1;
+  p.idesc = umma_idesc_f16(kBM, width, fmt, 1, 1);
   p.s_layout = umma_layout_for_span(tb.r_pad * 2);
   p.s_sbo = sw_sbo(tb.r_pad);
   p.s_kstep = static_cast<uint32_t>(16 * tb.r_pad * 2);
