@@ -360,14 +360,12 @@ def run_ours(args):
     # e2e through the plugin call with pinned host buffers
     x_host = pr["x"].cpu().pin_memory()
     y_host = torch.empty((T, N), dtype=torch.bfloat16).pin_memory()
-    x_dev = torch.empty_like(pr["x"])
 
     def e2e(ev):
         if ev:
             ev[0].record()
-        x_dev.copy_(x_host, non_blocking=True)
-        out = b200_ops.fused_lora_forward(x_dev, pr["w"], pr["lora_a"], pr["lora_b"], pr["adapters"], pr["routing"])
-        y_host.copy_(out, non_blocking=True)
+        b200_ops.fused_lora_forward_host(x_host, pr["w"], pr["lora_a"], pr["lora_b"], pr["adapters"], pr["routing"],
+                                         out=y_host)
         if ev:
             ev[1].record()
 
@@ -481,7 +479,8 @@ def run_ours(args):
                              "cublas_tflops": 2.0 * T * K * N / (cublas_ms / 1e3) / 1e12},
             "e2e": {"value": pr["global_T"] / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": T * K * 2, "d2h_bytes_per_step": T * N * 2,
-                    "path": "b200_ops.fused_lora_forward with pinned host x/y"},
+                    "path": "b200_ops.fused_lora_forward_host: pinned host x/y, 1024-row chunks, copies in "
+                            "both directions overlapped with the fused forward"},
             "fwd_bwd": fwd_bwd,
             "coordinator": coordinator,
             "cpu_baseline": cpu,

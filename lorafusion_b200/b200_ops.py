@@ -30,8 +30,8 @@ from lorafusion_b200 import _native as nat
 
 _DTYPE_CODE = {torch.float32: nat.LF_F32, torch.bfloat16: nat.LF_BF16, torch.float16: nat.LF_F16}
 
-__all__ = ["fused_lora_forward", "fused_lora_backward", "prepare_forward", "PreparedForward", "clear_weight_cache",
-           "last_launch_count", "use_cooperative_launch"]
+__all__ = ["fused_lora_forward", "fused_lora_backward", "fused_lora_forward_host", "prepare_forward",
+           "PreparedForward", "clear_weight_cache", "last_launch_count", "use_cooperative_launch"]
 
 
 # --------------------------------------------------------------------------- caches
@@ -382,3 +382,78 @@ def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, rout
         grad_b[aid] = gb_flat[off * N:(off + r) * N].view(N, r)
         off += r
     return grad_x, grad_a, grad_b
+
+
+# ----------------------------------------------------------------------------- host-resident batches
+_CHUNK_CACHE: dict[tuple, tuple] = {}
+_SIDE_STREAMS: dict[int, tuple] = {}
+
+
+def _chunk_routings(routing, total_rows: int, chunk_rows: int):
+    """Routes of each row chunk [c0, c1), rebased to the chunk (cached per routing object so the
+    chunks' routing tables are built once)."""
+    key = (id(routing), total_rows, chunk_rows)
+    hit = _CHUNK_CACHE.get(key)
+    if hit is not None and hit[0]() is routing:
+        return hit[1]
+    from lorafusion_b200.config import TileRoute, TileRoutingConfig
+    chunks = []
+    for c0 in range(0, total_rows, chunk_rows):
+        c1 = min(total_rows, c0 + chunk_rows)
+        routes = [TileRoute(max(r.row_start, c0) - c0, min(r.row_end, c1) - c0, r.adapter_id)
+                  for r in routing.routes if r.row_start < c1 and r.row_end > c0]
+        chunks.append((c0, c1, TileRoutingConfig(tile_size=routing.tile_size, routes=routes)))
+    if len(_CHUNK_CACHE) >= _CACHE_MAX:
+        _CHUNK_CACHE.clear()
+    _CHUNK_CACHE[key] = (weakref.ref(routing), chunks)
+    return chunks
+
+
+def fused_lora_forward_host(x_host, base_weight, lora_a, lora_b, adapters, routing, out=None,
+                            chunk_rows: int = 1024):
+    """``fused_lora_forward`` of a batch that lives in host memory; the result lands in host memory.
+
+    The rows travel in chunks of ``chunk_rows`` (a multiple of 256): chunk i is copied to the GPU
+    on one stream while chunk i-1 is computed on the caller's current stream and chunk i-2 is
+    copied back on a third, so both PCIe directions and the GPU work overlap.  Each output row
+    depends only on its own input row, and chunks start on the 128-row tile grid, so the result
+    equals one ``fused_lora_forward`` over the whole batch (bit for bit whenever the chunks and the
+    whole batch run the routed shrink the same way: both co-scheduled, or both as separate
+    launches).  ``x_host`` should be pinned (``pin_memory()``); ``out`` (pinned,
+    ``[T, N]``, x's dtype) is allocated when omitted.  The copies back are enqueued, not waited
+    for: synchronize the current stream before reading the result.  No counterpart in the
+    reference (its ops take device tensors).
+    """
+    routing.validate(x_host.shape[0])
+    if x_host.is_cuda or not base_weight.is_cuda:
+        raise ValueError("x_host must be a host tensor and base_weight a CUDA tensor")
+    if chunk_rows <= 0 or chunk_rows % 256:
+        raise ValueError("chunk_rows must be a positive multiple of 256")
+    device = base_weight.device
+    T, K = x_host.shape
+    N = base_weight.shape[0]
+    y_host = out if out is not None else torch.empty((T, N), dtype=x_host.dtype, pin_memory=True)
+    if y_host.shape != (T, N) or y_host.dtype != x_host.dtype or y_host.is_cuda:
+        raise ValueError("out must be a host tensor [T, N] of x's dtype")
+    if T == 0:
+        return y_host
+    compute = torch.cuda.current_stream(device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SIDE_STREAMS:
+        _SIDE_STREAMS[idx] = (torch.cuda.Stream(device), torch.cuda.Stream(device))
+    s_in, s_out = _SIDE_STREAMS[idx]
+    x_dev = torch.empty((T, K), dtype=x_host.dtype, device=device)
+    s_in.wait_stream(compute)
+    s_out.wait_stream(compute)
+    for c0, c1, rt in _chunk_routings(routing, T, chunk_rows):
+        with torch.cuda.stream(s_in):
+            x_dev[c0:c1].copy_(x_host[c0:c1], non_blocking=True)
+        compute.wait_stream(s_in)
+        y_c = fused_lora_forward(x_dev[c0:c1], base_weight, lora_a, lora_b, adapters, rt)
+        s_out.wait_stream(compute)
+        with torch.cuda.stream(s_out):
+            y_host[c0:c1].copy_(y_c, non_blocking=True)
+        y_c.record_stream(s_out)
+    x_dev.record_stream(s_in)
+    compute.wait_stream(s_out)
+    return y_host

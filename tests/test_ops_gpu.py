@@ -295,3 +295,27 @@ def test_co_scheduling_switch_matches_oracle(co_scheduled):
         _check(gb[k], case["gb"][k], BF16_TOL, f"grad_b[{k}]")
     from lorafusion_b200 import _native as nat
     assert nat.device_error() == 0
+
+
+def test_host_forward_streams_chunks_bit_exact():
+    """fused_lora_forward_host (pinned host batch, row chunks, copies overlapped) equals one
+    fused_lora_forward over the whole batch bit for bit; routes cross chunk boundaries."""
+    ops = _ops()
+    routes = _routes_from_sizes([700, 3, 281, 1000, 57, 259], [0, 1, 2, 0, 3, 1])  # 2300 rows
+    case = _random_case(31, 2300, 512, 384, routes, {0: 16, 1: 8, 2: 32, 3: 16}, torch.bfloat16)
+    x, w, a, b, ad, routing, _ = _to_torch(case, torch.bfloat16)
+    ref = ops.fused_lora_forward(x, w, a, b, ad, routing)
+    x_host = x.cpu().pin_memory()
+    for chunk in (256, 1024, 4096):
+        y = ops.fused_lora_forward_host(x_host, w, a, b, ad, routing, chunk_rows=chunk)
+        torch.cuda.current_stream().synchronize()
+        assert not y.is_cuda and torch.equal(y, ref.cpu()), chunk
+    out = torch.empty((2300, 384), dtype=torch.bfloat16).pin_memory()
+    assert ops.fused_lora_forward_host(x_host, w, a, b, ad, routing, out=out) is out
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(out, ref.cpu())
+    with pytest.raises(ValueError):
+        ops.fused_lora_forward_host(x_host, w, a, b, ad, routing, chunk_rows=100)
+    with pytest.raises(ValueError):
+        ops.fused_lora_forward_host(x, w, a, b, ad, routing)
+    _check(ref, case["y"], BF16_TOL, "forward")
