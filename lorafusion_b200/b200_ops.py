@@ -39,6 +39,7 @@ _ROUTE_CACHE: dict[int, tuple] = {}
 _PLAN_CACHE: dict[tuple, "_Plan"] = {}
 _PACK_CACHE: dict[tuple, dict] = {}
 _WEIGHT_CACHE: dict[tuple, tuple] = {}
+_PLAN_BY_CONTENT: dict[tuple, "_Plan"] = {}
 _CACHE_MAX = 256
 _last_launches = 0
 
@@ -58,6 +59,7 @@ def clear_weight_cache() -> None:
     """Drop every cached table, packed adapter slab and converted weight."""
     _ROUTE_CACHE.clear()
     _PLAN_CACHE.clear()
+    _PLAN_BY_CONTENT.clear()
     _PACK_CACHE.clear()
     _WEIGHT_CACHE.clear()
 
@@ -111,6 +113,15 @@ def _plan(routing, total_rows: int, adapters, lora_a, device: torch.device) -> _
     hit = _PLAN_CACHE.get(key)
     if hit is not None and hit[0]() is routing:
         return hit[1]
+    # a new routing object with the same routes (a runtime that re-packs every batch) reuses the plan
+    content = (starts.tobytes(), ends.tobytes(), route_slot.tobytes(), tuple(slots), total_rows, device, ranks, scales)
+    same = _PLAN_BY_CONTENT.get(content)
+    if same is not None:
+        try:
+            _PLAN_CACHE[key] = (weakref.ref(routing), same)
+        except TypeError:  # pragma: no cover
+            pass
+        return same
     L = nat.lib()
     n_routes = len(starts)
     cap = L.lf_plan_table_words(n_routes, total_rows, len(slots))
@@ -130,6 +141,9 @@ def _plan(routing, total_rows: int, adapters, lora_a, device: torch.device) -> _
     plan = _Plan(info, table_dev, slots, ranks)
     if len(_PLAN_CACHE) >= _CACHE_MAX:
         _PLAN_CACHE.clear()
+    if len(_PLAN_BY_CONTENT) >= _CACHE_MAX:
+        _PLAN_BY_CONTENT.clear()
+    _PLAN_BY_CONTENT[content] = plan
     try:
         _PLAN_CACHE[key] = (weakref.ref(routing), plan)
     except TypeError:  # pragma: no cover

@@ -235,23 +235,49 @@ def milp_pack(
 # --------------------------------------------------------------------------
 
 
+_RUN_DTYPE = np.dtype([("src", "<u8"), ("dst", "<u8"), ("src_stride", "<i8"), ("dst_stride", "<i8"),
+                       ("rows", "<i8"), ("row0", "<i8")])
+_RUN_STAGING: dict[int, list] = {}  # device index -> [pinned host table, device table, copy-done event]
+
+
 def _copy_runs(runs: list[tuple[int, int, int, int, int]], row_bytes: int, device: torch.device) -> None:
-    """One ``lf_copy_rows`` launch over ``(src, dst, src_stride, dst_stride, rows)`` runs."""
+    """One ``lf_copy_rows`` launch over ``(src, dst, src_stride, dst_stride, rows)`` runs.
+
+    The run table goes through a per-device pinned staging buffer that is reused once the copy
+    that last read it has finished (else a fresh one is taken)."""
     from lorafusion_b200 import _native as nat
 
     if not runs or row_bytes == 0:
         return
-    table = np.zeros(len(runs), dtype=[("src", "<u8"), ("dst", "<u8"), ("src_stride", "<i8"),
-                                       ("dst_stride", "<i8"), ("rows", "<i8"), ("row0", "<i8")])
-    cols = np.array(runs, dtype=np.int64).reshape(len(runs), 5)
+    n = len(runs)
+    nbytes = n * _RUN_DTYPE.itemsize
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    stage = _RUN_STAGING.get(idx)
+    if stage is None or stage[0].numel() < nbytes or not stage[2].query():
+        cap = max(nbytes, 64 * _RUN_DTYPE.itemsize)
+        stage = [torch.empty(cap, dtype=torch.uint8, pin_memory=True), torch.empty(cap, dtype=torch.uint8, device=device),
+                 torch.cuda.Event()]
+        _RUN_STAGING[idx] = stage
+    host, dev, done = stage
+    table = host.numpy()[:nbytes].view(_RUN_DTYPE)
+    cols = np.array(runs, dtype=np.int64).reshape(n, 5)
     table["src"], table["dst"] = cols[:, 0].astype(np.uint64), cols[:, 1].astype(np.uint64)
     table["src_stride"], table["dst_stride"], table["rows"] = cols[:, 2], cols[:, 3], cols[:, 4]
-    table["row0"] = np.concatenate(([0], np.cumsum(cols[:, 4])[:-1]))
-    total = int(cols[:, 4].sum())
-    host = torch.from_numpy(table.view(np.uint8)).pin_memory()
-    dev = host.to(device, non_blocking=True)
-    stream = torch.cuda.current_stream(device).cuda_stream
-    nat.check(nat.lib().lf_copy_rows(dev.data_ptr(), len(runs), row_bytes, total, stream), "lf_copy_rows")
+    row0 = np.cumsum(cols[:, 4])
+    table["row0"][1:] = row0[:-1]
+    table["row0"][0] = 0
+    stream = torch.cuda.current_stream(device)
+    dev[:nbytes].copy_(host[:nbytes], non_blocking=True)
+    nat.check(nat.lib().lf_copy_rows(dev.data_ptr(), n, row_bytes, int(row0[-1]), stream.cuda_stream), "lf_copy_rows")
+    done.record(stream)  # both tables are free again once the launch that reads them has finished
+
+
+class _RowOrder(list):
+    """``row_order`` as returned by :func:`build_microbatch`: a plain list of request ids that also
+    carries the row runs it was built from, so :func:`scatter_outputs` can skip re-encoding it
+    (used only while the list still equals the copy taken at build time)."""
+
+    __slots__ = ("_lf_pieces", "_lf_copy")
 
 
 def build_microbatch(
@@ -298,6 +324,10 @@ def build_microbatch(
             routes.append(TileRoute(row_start=cursor, row_end=cursor + n, adapter_id=aid))
             cursor += n
     routing = TileRoutingConfig(tile_size=packing.tile_capacity, routes=routes)
+    order = _RowOrder(row_order)
+    order._lf_pieces = pieces
+    order._lf_copy = row_order
+    row_order = order
     if not pieces:
         return torch.empty((0, in_features)), routing, row_order
     srcs = [request_tensors[rid] for rid, _, _ in pieces]
@@ -351,11 +381,19 @@ def scatter_outputs(fused_out: torch.Tensor, row_order: list[int]) -> dict[int, 
             out[rid] = fused_out.index_select(0, index)
         return out
     src = fused_out.contiguous()
-    ids = np.asarray(row_order, dtype=np.int64)
-    cut = np.flatnonzero(ids[1:] != ids[:-1]) + 1
-    run_start = np.concatenate(([0], cut))
-    run_len = np.diff(np.concatenate((run_start, [ids.size])))
-    run_id = ids[run_start]
+    pieces = getattr(row_order, "_lf_pieces", None)
+    if pieces is not None and list.__eq__(row_order, row_order._lf_copy):
+        run_id = np.fromiter((p[0] for p in pieces), dtype=np.int64, count=len(pieces))
+        run_len = np.fromiter((p[2] for p in pieces), dtype=np.int64, count=len(pieces))
+        run_start = np.concatenate(([0], np.cumsum(run_len)[:-1])).astype(np.int64)
+        ids_size = int(run_len.sum())
+    else:  # runs of equal ids
+        ids = np.fromiter(row_order, dtype=np.int64, count=len(row_order))
+        cut = np.flatnonzero(ids[1:] != ids[:-1]) + 1
+        run_start = np.concatenate(([0], cut))
+        run_len = np.diff(np.concatenate((run_start, [ids.size])))
+        run_id = ids[run_start]
+        ids_size = ids.size
     first = {}
     count: dict[int, int] = {}
     for rid, n in zip(run_id.tolist(), run_len.tolist()):
@@ -365,7 +403,7 @@ def scatter_outputs(fused_out: torch.Tensor, row_order: list[int]) -> dict[int, 
     order = list(first.keys())
     row_shape = tuple(src.shape[1:])
     row_elems = int(np.prod(row_shape)) if row_shape else 1
-    buf = torch.empty((ids.size,) + row_shape, dtype=src.dtype, device=src.device)
+    buf = torch.empty((ids_size,) + row_shape, dtype=src.dtype, device=src.device)
     base, off = {}, 0
     for rid in order:
         base[rid] = off
