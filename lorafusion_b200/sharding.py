@@ -14,7 +14,10 @@ the op needs to run one process per GPU:
   placed bin by bin, and a bin that fits nowhere goes to the least-loaded
   rank).  Deterministic, so every rank computes the same assignment without
   communicating.
-* :func:`local_layout` turns a rank's bins into its own fused row ranges and a
+* Whole bins can leave a rank a few rows over its share rounded up to 256-row
+  tile pairs (an extra, mostly empty pair of row tiles); those rows move to
+  ranks below that capacity, cutting a bin, so ranks hold row *ranges*.
+* :func:`local_layout` turns a rank's row ranges into its own fused rows and a
   rebased :class:`TileRoutingConfig`.
 * The forward needs no communication (base weight replicated, adapters
   resident on every rank).  In the backward, :func:`allreduce_spanning_grads`
@@ -38,15 +41,25 @@ TILE_PAIR_ROWS = 256  # rows of one CTA-pair tile of the fused GEMM
 @dataclass(frozen=True)
 class ShardPlan:
     world_size: int
-    bin_rank: list[int]                 # rank of every global bin
+    bin_rank: list[int]                 # rank of every global bin (of its leading rows if it was split)
     bin_rows: list[tuple[int, int]]     # [start, end) of every bin in the global fused rows
     spanning: list[int]                 # adapters whose routes land on more than one rank, ascending
+    rank_ranges: tuple = ()             # per rank: its global row ranges [start, end), ascending
 
     def rank_bins(self, rank: int) -> list[int]:
         return [b for b, r in enumerate(self.bin_rank) if r == rank]
 
     def rank_rows(self, rank: int) -> int:
-        return sum(e - s for (s, e), r in zip(self.bin_rows, self.bin_rank) if r == rank)
+        return sum(e - s for s, e in self.rank_ranges[rank])
+
+
+def _global_routes(bins: list[list[tuple[int, int]]]) -> list[tuple[int, int, int]]:
+    out, cur = [], 0
+    for entries in bins:
+        for a, n in entries:
+            out.append((cur, cur + n, a))
+            cur += n
+    return out
 
 
 def assign_bins(bins: list[list[tuple[int, int]]], world_size: int) -> ShardPlan:
@@ -72,29 +85,60 @@ def assign_bins(bins: list[list[tuple[int, int]]], world_size: int) -> ShardPlan
                                   len(bins), world_size, TILE_PAIR_ROWS, bin_rank.ctypes.data_as(P))
     nat.check(rc, "lf_assign_bins")
     ranks = bin_rank[:len(bins)].tolist()
+    # Whole bins can leave a rank a few rows over its share rounded up to 256-row tile pairs, which
+    # costs it a whole extra pair of row tiles.  Move such excess rows (the tail of the rank's last
+    # bin) to ranks below that capacity; every rank then holds at most the capacity.
+    total = sum(rows)
+    cap = -(-max(1, -(-total // world_size)) // TILE_PAIR_ROWS) * TILE_PAIR_ROWS
+    ranges: list[list[tuple[int, int]]] = [[] for _ in range(world_size)]
+    for b, r in enumerate(ranks):
+        if starts[b][1] > starts[b][0]:
+            ranges[r].append(starts[b])
+    load = [sum(e - s for s, e in rr) for rr in ranges]
+    for r in range(world_size):
+        while load[r] > cap:
+            s0, e0 = ranges[r].pop()  # the rank's last range (highest rows)
+            under = min(range(world_size), key=lambda k: (load[k] - cap, k))
+            room = cap - load[under]
+            if room <= 0:  # nowhere to go (cannot happen while the total fits)
+                ranges[r].append((s0, e0))
+                break
+            move = min(load[r] - cap, room, e0 - s0)
+            if e0 - s0 > move:
+                ranges[r].append((s0, e0 - move))
+            ranges[under].append((e0 - move, e0))
+            load[r] -= move
+            load[under] += move
+    rank_ranges = tuple(tuple(sorted(rr)) for rr in ranges)
     owners: dict[int, set[int]] = {}
-    for b, entries in enumerate(bins):
-        for a, _ in entries:
-            owners.setdefault(a, set()).add(ranks[b])
+    groutes = _global_routes(bins)
+    for r, rr in enumerate(rank_ranges):
+        for s0, e0 in rr:
+            for g0, g1, a in groutes:
+                if g0 < e0 and g1 > s0:
+                    owners.setdefault(a, set()).add(r)
     spanning = sorted(a for a, rk in owners.items() if len(rk) > 1)
-    return ShardPlan(world_size=world_size, bin_rank=ranks, bin_rows=starts, spanning=spanning)
+    return ShardPlan(world_size=world_size, bin_rank=ranks, bin_rows=starts, spanning=spanning,
+                     rank_ranges=rank_ranges)
 
 
 def local_layout(plan: ShardPlan, bins: list[list[tuple[int, int]]], rank: int, tile_size: int):
-    """(global row index of each local row, local routing) for one rank's bins.
+    """(global row index of each local row, local routing) for one rank's rows.
 
-    Local rows are the rank's bins in global order; routes are the global
-    routes of those bins shifted to local row numbers.
+    Local rows are the rank's global row ranges in ascending order; routes are
+    the global routes cut to those ranges and shifted to local row numbers.
     """
+    groutes = _global_routes(bins)
     rows: list[int] = []
     routes: list[TileRoute] = []
     cur = 0
-    for b in plan.rank_bins(rank):
-        g0, g1 = plan.bin_rows[b]
-        rows.extend(range(g0, g1))
-        for a, n in bins[b]:
-            routes.append(TileRoute(cur, cur + n, a))
-            cur += n
+    for s0, e0 in plan.rank_ranges[rank]:
+        rows.extend(range(s0, e0))
+        for g0, g1, a in groutes:
+            lo, hi = max(g0, s0), min(g1, e0)
+            if lo < hi:
+                routes.append(TileRoute(cur + lo - s0, cur + hi - s0, a))
+        cur += e0 - s0
     return rows, TileRoutingConfig(tile_size=tile_size, routes=routes)
 
 
@@ -115,24 +159,26 @@ def allreduce_spanning_grads(plan: ShardPlan, grad_a: dict[int, torch.Tensor], g
     K, N = in_features, out_features
     sizes = [ranks[a] * (K + N) for a in plan.spanning]
     buf = torch.zeros(sum(sizes), dtype=torch.float32, device=device)
-    off = 0
+    dst, src, off = [], [], 0
+    views = []
     for a, sz in zip(plan.spanning, sizes):
         r = ranks[a]
+        va, vb = buf[off:off + r * K].view(r, K), buf[off + r * K:off + sz].view(N, r)
+        views.append((a, va, vb))
         if a in grad_a:
-            buf[off:off + r * K].copy_(grad_a[a].reshape(-1))
-            buf[off + r * K:off + sz].copy_(grad_b[a].reshape(-1))
+            dst += [va, vb]
+            src += [grad_a[a], grad_b[a]]
         off += sz
+    if dst:  # one multi-tensor launch packs (and converts) every held gradient
+        torch._foreach_copy_(dst, src)
     dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
-    off = 0
-    for a, sz in zip(plan.spanning, sizes):
-        r = ranks[a]
-        dtype = grad_a[a].dtype if a in grad_a else torch.float32
-        ga = buf[off:off + r * K].view(r, K).to(dtype)
-        gb = buf[off + r * K:off + sz].view(N, r).to(dtype)
+    back_dst, back_src = [], []
+    for a, va, vb in views:
         if a in grad_a:
-            grad_a[a].copy_(ga)
-            grad_b[a].copy_(gb)
+            back_dst += [grad_a[a], grad_b[a]]
+            back_src += [va, vb]
         else:
-            grad_a[a] = ga.clone()
-            grad_b[a] = gb.clone()
-        off += sz
+            grad_a[a] = va.clone()
+            grad_b[a] = vb.clone()
+    if back_dst:
+        torch._foreach_copy_(back_dst, back_src)
