@@ -259,17 +259,20 @@ LF_API int lf_greedy_pack(const int32_t* adapter_ids, const int32_t* rows, int32
                           int32_t* n_entries, int32_t* n_bins);
 
 /*
- * Bin -> rank assignment for one process per GPU (host only).  No counterpart in the reference
- * (it runs on one device).  Consecutive bins holding one and the same adapter form bundles (at
- * most ceil(total/world) rows; a bin with several adapters is a bundle of its own).  Each rank
- * may hold its even share rounded up to whole `granule_rows` (the fused GEMM's row tile); bundles,
- * largest first (ties in bundle order), go to the rank they fit best (least room left, then
- * lowest rank); a bundle that fits nowhere is placed bin by bin, largest first, and a bin that
- * fits nowhere goes to the least-loaded rank.  Deterministic: every rank computes the same
- * bin_rank[n_bins] without communicating.  Inputs are the CSR packing of lf_greedy_pack.
+ * Row -> rank assignment for one process per GPU (host only).  No counterpart in the reference
+ * (it runs on one device).  Input: the packing (CSR of lf_greedy_pack), whose entries in bin order
+ * are the global fused rows.  Every rank may hold its even share of the rows rounded up to whole
+ * `granule_rows` (the fused GEMM's row tile).  Adapters, most rows first (ties: first appearance),
+ * go whole to the rank they fit best (least room left, then lowest rank); an adapter that fits
+ * nowhere is cut over the ranks with most room (then lowest rank), each taking what it has room
+ * for, so only such adapters span ranks.  An adapter's rows go to its parts in global row order.
+ * Output: global row ranges [range_start, range_end) with their rank, ascending, adjacent ranges
+ * of one rank merged; *n_ranges is set (LF_ERR_CAPACITY when more than max_ranges: call again with
+ * that many).  Deterministic: every rank computes the same ranges without communicating.
  */
-LF_API int lf_assign_bins(const int32_t* bin_start, const int32_t* entry_adapter, const int32_t* entry_rows,
-                          int32_t n_bins, int32_t world_size, int32_t granule_rows, int32_t* bin_rank);
+LF_API int lf_assign_rows(const int32_t* bin_start, const int32_t* entry_adapter, const int32_t* entry_rows,
+                          int32_t n_bins, int32_t world_size, int32_t granule_rows, int32_t max_ranges,
+                          int64_t* range_start, int64_t* range_end, int32_t* range_rank, int32_t* n_ranges);
 
 /*
  * Read and clear the device-side error word (bounded-wait timeouts inside kernels).

@@ -78,8 +78,9 @@ def _declare(L: ctypes.CDLL) -> None:
     L.lf_greedy_pack.argtypes = [P(_c_i32), P(_c_i32), _c_i32, _c_i32, _c_i32, P(_c_i32), P(_c_i32), P(_c_i32),
                                  P(_c_i32), P(_c_i32)]
     L.lf_greedy_pack.restype = ctypes.c_int
-    L.lf_assign_bins.argtypes = [P(_c_i32), P(_c_i32), P(_c_i32), _c_i32, _c_i32, _c_i32, P(_c_i32)]
-    L.lf_assign_bins.restype = ctypes.c_int
+    L.lf_assign_rows.argtypes = [P(_c_i32), P(_c_i32), P(_c_i32), _c_i32, _c_i32, _c_i32, _c_i32,
+                                 P(ctypes.c_int64), P(ctypes.c_int64), P(_c_i32), P(_c_i32)]
+    L.lf_assign_rows.restype = ctypes.c_int
     L.lf_forward.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, ctypes.c_size_t, _c_p]
     L.lf_forward.restype = ctypes.c_int
     L.lf_forward_stages.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, ctypes.c_size_t, _c_i32, _c_p]

@@ -2,8 +2,8 @@
 //
 // lf_greedy_pack restates greedy_pack (lorafusion/scheduler/milp_packer.py:36-72) with the same
 // output bit for bit; the first-fit search is a max segment tree over the bins' free rows
-// (leftmost bin with room in O(log bins)) instead of a linear scan.  lf_assign_bins gives each
-// rank whole bins for one process per GPU.
+// (leftmost bin with room in O(log bins)) instead of a linear scan.  lf_assign_rows gives each
+// rank its rows for one process per GPU, keeping every adapter on one rank where it fits.
 #include <stdint.h>
 
 #include <algorithm>
@@ -91,79 +91,95 @@ extern "C" int lf_greedy_pack(const int32_t* adapter_ids, const int32_t* rows, i
   return LF_OK;
 }
 
-extern "C" int lf_assign_bins(const int32_t* bin_start, const int32_t* entry_adapter, const int32_t* entry_rows,
-                              int32_t n_bins, int32_t world_size, int32_t granule_rows, int32_t* bin_rank) {
-  if (world_size <= 0 || granule_rows <= 0 || n_bins < 0) return LF_ERR_INVALID_ARG;
+extern "C" int lf_assign_rows(const int32_t* bin_start, const int32_t* entry_adapter, const int32_t* entry_rows,
+                              int32_t n_bins, int32_t world_size, int32_t granule_rows, int32_t max_ranges,
+                              int64_t* range_start, int64_t* range_end, int32_t* range_rank, int32_t* n_ranges) {
+  if (world_size <= 0 || granule_rows <= 0 || n_bins < 0 || max_ranges < 0 || !n_ranges) return LF_ERR_INVALID_ARG;
+  *n_ranges = 0;
   if (n_bins == 0) return LF_OK;
-  if (!bin_start || !entry_adapter || !entry_rows || !bin_rank) return LF_ERR_INVALID_ARG;
-  std::vector<int64_t> rows(n_bins, 0);
-  std::vector<int32_t> adapter_of(n_bins, 0);  // the bin's adapter when `single`
-  std::vector<char> single(n_bins, 0);          // every entry of the bin holds one and the same adapter
-  int64_t total = 0;
-  for (int32_t b = 0; b < n_bins; ++b) {
-    single[b] = bin_start[b + 1] > bin_start[b];
-    for (int32_t e = bin_start[b]; e < bin_start[b + 1]; ++e) {
-      rows[b] += entry_rows[e];
-      if (e == bin_start[b]) adapter_of[b] = entry_adapter[e];
-      else if (entry_adapter[e] != adapter_of[b]) single[b] = 0;
-    }
-    total += rows[b];
+  if (!bin_start || !entry_adapter || !entry_rows) return LF_ERR_INVALID_ARG;
+  const int32_t n_entries = bin_start[n_bins];
+  // entries in global row order; adapters in order of first appearance
+  std::vector<int64_t> e_start(n_entries);
+  std::vector<int32_t> adapter_of_entry(n_entries), first_seen;
+  std::vector<int32_t> ids(entry_adapter, entry_adapter + n_entries);
+  std::sort(ids.begin(), ids.end());
+  ids.erase(std::unique(ids.begin(), ids.end()), ids.end());
+  const int n_ad = static_cast<int>(ids.size());
+  std::vector<int64_t> total_of(n_ad, 0);
+  std::vector<int32_t> order_seen(n_ad, -1);
+  int64_t cur = 0, total = 0;
+  for (int32_t e = 0; e < n_entries; ++e) {
+    const int a = static_cast<int>(std::lower_bound(ids.begin(), ids.end(), entry_adapter[e]) - ids.begin());
+    adapter_of_entry[e] = a;
+    e_start[e] = cur;
+    cur += entry_rows[e];
+    total_of[a] += entry_rows[e];
+    if (order_seen[a] < 0) order_seen[a] = static_cast<int32_t>(first_seen.size()), first_seen.push_back(a);
   }
+  total = cur;
   const int64_t share = std::max<int64_t>(1, (total + world_size - 1) / world_size);
   const int64_t cap = (share + granule_rows - 1) / granule_rows * granule_rows;
-
-  // Bundles: runs of consecutive bins of one single adapter, at most `share` rows each; a bin
-  // with several adapters (or none) is a bundle of its own.
-  std::vector<std::vector<int32_t>> bundles;
-  std::vector<int32_t> cur;
-  int32_t cur_adapter = 0;
-  int64_t cur_rows = 0;
-  for (int32_t b = 0; b < n_bins; ++b) {
-    if (!cur.empty() && (!single[b] || adapter_of[b] != cur_adapter || cur_rows + rows[b] > share)) {
-      bundles.push_back(cur);
-      cur.clear();
-      cur_rows = 0;
-    }
-    cur.push_back(b);
-    cur_rows += rows[b];
-    cur_adapter = adapter_of[b];
-    if (!single[b]) {
-      bundles.push_back(cur);
-      cur.clear();
-      cur_rows = 0;
-    }
-  }
-  if (!cur.empty()) bundles.push_back(cur);
-
-  std::vector<int64_t> bundle_rows(bundles.size(), 0);
-  for (size_t i = 0; i < bundles.size(); ++i)
-    for (int32_t b : bundles[i]) bundle_rows[i] += rows[b];
-  std::vector<size_t> order(bundles.size());
-  std::iota(order.begin(), order.end(), 0);
-  std::stable_sort(order.begin(), order.end(),
-                   [&](size_t x, size_t y) { return bundle_rows[x] > bundle_rows[y]; });
+  // adapters, most rows first (ties: first appearance), to ranks: whole into the rank they fit
+  // best (least room left, then lowest rank); an adapter that fits nowhere is cut over the ranks
+  // with most room (then lowest rank), each taking what it has room for
+  std::vector<int> by_size(first_seen.begin(), first_seen.end());
+  std::stable_sort(by_size.begin(), by_size.end(), [&](int x, int y) { return total_of[x] > total_of[y]; });
   std::vector<int64_t> load(world_size, 0);
-  auto place = [&](const std::vector<int32_t>& members, int64_t n) {
+  std::vector<std::vector<std::pair<int, int64_t>>> parts(n_ad);  // (rank, rows) in order
+  for (int a : by_size) {
+    int64_t left = total_of[a];
     int best = -1;
     for (int k = 0; k < world_size; ++k)
-      if (load[k] + n <= cap && (best < 0 || cap - load[k] - n < cap - load[best] - n)) best = k;
-    if (best < 0) return false;
-    for (int32_t b : members) bin_rank[b] = best;
-    load[best] += n;
-    return true;
-  };
-  for (size_t i : order) {
-    if (place(bundles[i], bundle_rows[i])) continue;
-    std::vector<int32_t> members = bundles[i];
-    std::stable_sort(members.begin(), members.end(), [&](int32_t x, int32_t y) { return rows[x] > rows[y]; });
-    for (int32_t b : members) {
-      if (place({b}, rows[b])) continue;
-      int least = 0;
+      if (load[k] + left <= cap && (best < 0 || cap - load[k] - left < cap - load[best] - left)) best = k;
+    if (best >= 0) {
+      parts[a].push_back({best, left});
+      load[best] += left;
+      continue;
+    }
+    while (left > 0) {
+      int most = 0;
       for (int k = 1; k < world_size; ++k)
-        if (load[k] < load[least]) least = k;
-      bin_rank[b] = least;
-      load[least] += rows[b];
+        if (load[k] < load[most]) most = k;
+      const int64_t room = cap - load[most];
+      const int64_t take = room > 0 ? std::min(room, left) : left;  // no room anywhere: the least-loaded rank
+      parts[a].push_back({most, take});
+      load[most] += take;
+      left -= take;
     }
   }
-  return LF_OK;
+  // each adapter's rows, in global order, go to its parts in order: emit row ranges
+  std::vector<size_t> part_i(n_ad, 0);
+  std::vector<int64_t> part_used(n_ad, 0);
+  int32_t n = 0;
+  auto emit = [&](int64_t s0, int64_t e0, int32_t r) {
+    if (n > 0 && n <= max_ranges && range_rank && range_end && range_rank[n - 1] == r && range_end[n - 1] == s0) {
+      range_end[n - 1] = e0;  // extend the previous range
+      return;
+    }
+    if (n < max_ranges && range_start && range_end && range_rank) {
+      range_start[n] = s0;
+      range_end[n] = e0;
+      range_rank[n] = r;
+    }
+    ++n;
+  };
+  for (int32_t e = 0; e < n_entries; ++e) {
+    const int a = adapter_of_entry[e];
+    int64_t s0 = e_start[e], rows_left = entry_rows[e];
+    while (rows_left > 0) {
+      const auto& pr = parts[a][part_i[a]];
+      const int64_t take = std::min(rows_left, pr.second - part_used[a]);
+      emit(s0, s0 + take, pr.first);
+      s0 += take;
+      rows_left -= take;
+      part_used[a] += take;
+      if (part_used[a] == pr.second) {
+        ++part_i[a];
+        part_used[a] = 0;
+      }
+    }
+  }
+  *n_ranges = n;
+  return n <= max_ranges ? LF_OK : LF_ERR_CAPACITY;
 }

@@ -6,17 +6,13 @@ the op needs to run one process per GPU:
 * The global layout is untouched: every rank runs the same scheduler
   (``bucket_by_adapter -> greedy_pack -> build_microbatch``) and gets the same
   bins and routes, bit for bit.
-* :func:`assign_bins` gives each rank whole bins (``lf_assign_bins``, C++).  Runs of consecutive
-  single-adapter bins form bundles so an adapter's rows stay on one rank where
-  possible; bundles larger than a rank's share are cut.  Every rank gets a
-  capacity of its even share rounded up to whole 256-row tile pairs; bundles,
-  largest first, go to the rank they fit best (a bundle that fits nowhere is
-  placed bin by bin, and a bin that fits nowhere goes to the least-loaded
-  rank).  Deterministic, so every rank computes the same assignment without
-  communicating.
-* Whole bins can leave a rank a few rows over its share rounded up to 256-row
-  tile pairs (an extra, mostly empty pair of row tiles); those rows move to
-  ranks below that capacity, cutting a bin, so ranks hold row *ranges*.
+* :func:`assign_bins` (``lf_assign_rows``, C++) gives each rank row ranges of
+  that global layout: adapters, largest first, go whole to the rank they fit
+  best, where every rank's capacity is its even share rounded up to 256-row
+  tile pairs (so no rank needs an extra, mostly empty pair of row tiles); an
+  adapter that fits nowhere is cut over the ranks with most room.  Only the cut
+  adapters span ranks.  Deterministic, so every rank computes the same
+  assignment without communicating.
 * :func:`local_layout` turns a rank's row ranges into its own fused rows and a
   rebased :class:`TileRoutingConfig`.
 * The forward needs no communication (base weight replicated, adapters
@@ -41,7 +37,7 @@ TILE_PAIR_ROWS = 256  # rows of one CTA-pair tile of the fused GEMM
 @dataclass(frozen=True)
 class ShardPlan:
     world_size: int
-    bin_rank: list[int]                 # rank of every global bin (of its leading rows if it was split)
+    bin_rank: list[int]                 # rank holding the first row of every global bin
     bin_rows: list[tuple[int, int]]     # [start, end) of every bin in the global fused rows
     spanning: list[int]                 # adapters whose routes land on more than one rank, ascending
     rank_ranges: tuple = ()             # per rank: its global row ranges [start, end), ascending
@@ -63,8 +59,8 @@ def _global_routes(bins: list[list[tuple[int, int]]]) -> list[tuple[int, int, in
 
 
 def assign_bins(bins: list[list[tuple[int, int]]], world_size: int) -> ShardPlan:
-    """Deterministic bin -> rank assignment (see module docstring), computed by
-    ``lf_assign_bins`` in the native library."""
+    """Deterministic row -> rank assignment of a packing (see module docstring), computed by
+    ``lf_assign_rows`` in the native library."""
     from lorafusion_b200 import _native as nat
 
     if world_size <= 0:
@@ -79,46 +75,42 @@ def assign_bins(bins: list[list[tuple[int, int]]], world_size: int) -> ShardPlan
     flat = [x for entries in bins for x in entries]
     ent_a = np.array([a for a, _ in flat] or [0], dtype=np.int32)
     ent_r = np.array([n for _, n in flat] or [0], dtype=np.int32)
-    bin_rank = np.zeros(max(len(bins), 1), dtype=np.int32)
     P = ctypes.POINTER(ctypes.c_int32)
-    rc = nat.lib().lf_assign_bins(bin_start.ctypes.data_as(P), ent_a.ctypes.data_as(P), ent_r.ctypes.data_as(P),
-                                  len(bins), world_size, TILE_PAIR_ROWS, bin_rank.ctypes.data_as(P))
-    nat.check(rc, "lf_assign_bins")
-    ranks = bin_rank[:len(bins)].tolist()
-    # Whole bins can leave a rank a few rows over its share rounded up to 256-row tile pairs, which
-    # costs it a whole extra pair of row tiles.  Move such excess rows (the tail of the rank's last
-    # bin) to ranks below that capacity; every rank then holds at most the capacity.
-    total = sum(rows)
-    cap = -(-max(1, -(-total // world_size)) // TILE_PAIR_ROWS) * TILE_PAIR_ROWS
+    P64 = ctypes.POINTER(ctypes.c_int64)
+    cap = max(2 * len(flat) + world_size, 16)
+    while True:
+        r_s = np.zeros(cap, dtype=np.int64)
+        r_e = np.zeros(cap, dtype=np.int64)
+        r_k = np.zeros(cap, dtype=np.int32)
+        n_ranges = ctypes.c_int32(0)
+        rc = nat.lib().lf_assign_rows(bin_start.ctypes.data_as(P), ent_a.ctypes.data_as(P), ent_r.ctypes.data_as(P),
+                                      len(bins), world_size, TILE_PAIR_ROWS, cap, r_s.ctypes.data_as(P64),
+                                      r_e.ctypes.data_as(P64), r_k.ctypes.data_as(P), ctypes.byref(n_ranges))
+        if rc == nat.LF_ERR_CAPACITY and n_ranges.value > cap:
+            cap = n_ranges.value
+            continue
+        nat.check(rc, "lf_assign_rows")
+        break
+    n = n_ranges.value
     ranges: list[list[tuple[int, int]]] = [[] for _ in range(world_size)]
-    for b, r in enumerate(ranks):
-        if starts[b][1] > starts[b][0]:
-            ranges[r].append(starts[b])
-    load = [sum(e - s for s, e in rr) for rr in ranges]
-    for r in range(world_size):
-        while load[r] > cap:
-            s0, e0 = ranges[r].pop()  # the rank's last range (highest rows)
-            under = min(range(world_size), key=lambda k: (load[k] - cap, k))
-            room = cap - load[under]
-            if room <= 0:  # nowhere to go (cannot happen while the total fits)
-                ranges[r].append((s0, e0))
-                break
-            move = min(load[r] - cap, room, e0 - s0)
-            if e0 - s0 > move:
-                ranges[r].append((s0, e0 - move))
-            ranges[under].append((e0 - move, e0))
-            load[r] -= move
-            load[under] += move
-    rank_ranges = tuple(tuple(sorted(rr)) for rr in ranges)
+    for s0, e0, k in zip(r_s[:n].tolist(), r_e[:n].tolist(), r_k[:n].tolist()):
+        ranges[k].append((s0, e0))
+    rank_ranges = tuple(tuple(rr) for rr in ranges)
+    owner = []  # rank of each bin's first row
+    bounds = sorted((s0, e0, k) for k, rr in enumerate(ranges) for s0, e0 in rr)
+    j = 0
+    for g0, g1 in starts:
+        while j + 1 < len(bounds) and bounds[j][1] <= g0:
+            j += 1
+        owner.append(bounds[j][2] if bounds and g1 > g0 else 0)
     owners: dict[int, set[int]] = {}
     groutes = _global_routes(bins)
-    for r, rr in enumerate(rank_ranges):
-        for s0, e0 in rr:
-            for g0, g1, a in groutes:
-                if g0 < e0 and g1 > s0:
-                    owners.setdefault(a, set()).add(r)
+    for s0, e0, k in bounds:
+        for g0, g1, a in groutes:
+            if g0 < e0 and g1 > s0:
+                owners.setdefault(a, set()).add(k)
     spanning = sorted(a for a, rk in owners.items() if len(rk) > 1)
-    return ShardPlan(world_size=world_size, bin_rank=ranks, bin_rows=starts, spanning=spanning,
+    return ShardPlan(world_size=world_size, bin_rank=owner, bin_rows=starts, spanning=spanning,
                      rank_ranges=rank_ranges)
 
 

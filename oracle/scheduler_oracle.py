@@ -10,9 +10,9 @@ tables bit-exactly.
 * :func:`microbatch_layout` — ``lorafusion/scheduler/data_batcher.py:18-87``,
   returning routes, ``row_order`` and, per fused row, the source
   ``(request_id, row_in_request)``.
-* :func:`assign_bins` — the bin -> rank assignment of the multi-GPU layer (no
+* :func:`assign_rows` — the row -> rank assignment of the multi-GPU layer (no
   counterpart in the reference, which runs on one device), restated in plain
-  Python to check ``lf_assign_bins``.
+  Python to check ``lf_assign_rows``.
 """
 
 from __future__ import annotations
@@ -81,53 +81,52 @@ def microbatch_layout(requests, bins):
     return routes, row_order, source
 
 
-def assign_bins(bins, world_size: int, granule_rows: int = 256):
-    """Rank of every bin: bundles of consecutive single-adapter bins (at most the
-    even share of rows), capacity = share rounded up to ``granule_rows``,
-    largest bundle first into the best-fitting rank; bundles that fit nowhere
-    are placed bin by bin, and bins that fit nowhere go to the least-loaded rank."""
+def assign_rows(bins, world_size: int, granule_rows: int = 256):
+    """Global row ranges (start, end, rank), ascending, adjacent ranges of one rank merged:
+    adapters, most rows first (ties: first appearance), whole into the best-fitting rank (least
+    room left, then lowest); an adapter that fits nowhere is cut over the ranks with most room
+    (then lowest), each taking what it has room for; its rows go to its parts in row order."""
     if world_size <= 0:
         raise ValueError("world_size must be positive")
-    rows = [sum(n for _, n in entries) for entries in bins]
-    total = sum(rows)
+    entries = [(a, n) for b in bins for a, n in b]
+    total = sum(n for _, n in entries)
     share = max(1, -(-total // world_size))
     cap = -(-share // granule_rows) * granule_rows
-    bundles, cur, cur_adapter, cur_rows = [], [], None, 0
-    for b, entries in enumerate(bins):
-        adapters = {a for a, _ in entries}
-        solo = next(iter(adapters)) if len(adapters) == 1 else None
-        if cur and (solo is None or solo != cur_adapter or cur_rows + rows[b] > share):
-            bundles.append(cur)
-            cur, cur_rows, cur_adapter = [], 0, None
-        cur.append(b)
-        cur_rows += rows[b]
-        cur_adapter = solo
-        if solo is None:
-            bundles.append(cur)
-            cur, cur_rows, cur_adapter = [], 0, None
-    if cur:
-        bundles.append(cur)
-    order = sorted(range(len(bundles)), key=lambda i: -sum(rows[b] for b in bundles[i]))
+    totals: dict[int, int] = {}
+    for a, n in entries:
+        totals[a] = totals.get(a, 0) + n  # dict keeps first appearance
+    order = sorted(totals, key=lambda a: -totals[a])  # stable
     load = [0] * world_size
-    rank = [0] * len(bins)
-
-    def place(members):
-        n = sum(rows[b] for b in members)
-        fits = [k for k in range(world_size) if load[k] + n <= cap]
-        if not fits:
-            return False
-        r = min(fits, key=lambda k: (cap - load[k] - n, k))
-        for b in members:
-            rank[b] = r
-        load[r] += n
-        return True
-
-    for i in order:
-        if place(bundles[i]):
+    parts: dict[int, list[list[int]]] = {}
+    for a in order:
+        left = totals[a]
+        fits = [k for k in range(world_size) if load[k] + left <= cap]
+        if fits:
+            k = min(fits, key=lambda k: (cap - load[k] - left, k))
+            parts[a] = [[k, left]]
+            load[k] += left
             continue
-        for b in sorted(bundles[i], key=lambda b: (-rows[b], b)):
-            if not place([b]):
-                r = min(range(world_size), key=lambda k: (load[k], k))
-                rank[b] = r
-                load[r] += rows[b]
-    return rank
+        parts[a] = []
+        while left > 0:
+            k = min(range(world_size), key=lambda k: (load[k], k))
+            room = cap - load[k]
+            take = min(room, left) if room > 0 else left
+            parts[a].append([k, take])
+            load[k] += take
+            left -= take
+    out, cur = [], 0
+    for a, n in entries:
+        while n > 0:
+            k, rem = parts[a][0]
+            take = min(n, rem)
+            if out and out[-1][2] == k and out[-1][1] == cur:
+                out[-1][1] = cur + take
+            else:
+                out.append([cur, cur + take, k])
+            cur += take
+            n -= take
+            if take == rem:
+                parts[a].pop(0)
+            else:
+                parts[a][0][1] = rem - take
+    return [tuple(x) for x in out]

@@ -142,16 +142,28 @@ def test_spanning_gradients_allreduce_gloo():
 
 @pytest.mark.parametrize("seed", range(10))
 def test_native_assignment_equals_oracle(seed):
-    """lf_assign_bins matches the plain-Python restatement on random packings and world sizes."""
-    from oracle.scheduler_oracle import assign_bins as oracle_assign
+    """lf_assign_rows matches the plain-Python restatement on random packings and world sizes."""
+    from oracle.scheduler_oracle import assign_rows
     rng = np.random.default_rng(100 + seed)
     cap = int(rng.choice([16, 64, 128]))
     counts = [int(v) for v in rng.integers(1, 6 * cap, size=int(rng.integers(1, 80)))]
     _, packing = _packing(counts, cap)
     for world in (1, 2, 3, 5, 8):
-        assert assign_bins(packing.bins, world).bin_rank == oracle_assign(packing.bins, world), (seed, world)
+        plan = assign_bins(packing.bins, world)
+        got = sorted((s0, e0, k) for k, rr in enumerate(plan.rank_ranges) for s0, e0 in rr)
+        assert got == assign_rows(packing.bins, world), (seed, world)
     bins = [[], [(3, 5), (4, 2)], [(3, 7)], [(3, 9)], []]  # empty and mixed bins
     for world in (1, 2, 4):
-        assert assign_bins(bins, world).bin_rank == oracle_assign(bins, world)
+        plan = assign_bins(bins, world)
+        assert sorted((s0, e0, k) for k, rr in enumerate(plan.rank_ranges) for s0, e0 in rr) == assign_rows(bins, world)
     with pytest.raises(ValueError):
         assign_bins(packing.bins, 0)
+
+
+def test_only_adapters_larger_than_a_share_span():
+    """cfg2 at 8 ranks: adapters that fit in a rank's capacity stay whole on one rank."""
+    wl = WORKLOADS["cfg2_h4096_a16_r16"]
+    counts = row_counts(wl, wl.total_rows * 8)
+    _, packing = _packing(counts, wl.tile_capacity)
+    plan = assign_bins(packing.bins, 8)
+    assert len(plan.spanning) <= 8 + sum(c > 4096 for c in counts)
