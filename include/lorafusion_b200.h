@@ -205,6 +205,19 @@ LF_API int lf_backward(const lf_problem* prob, const lf_plan_info* info, const i
                 void* workspace_dev, size_t workspace_bytes, lf_stream_t stream);
 
 /*
+ * lf_backward with S_f = s_i x A_i^T taken from a forward instead of recomputed: `s_f_dev` is the
+ * workspace a lf_forward / lf_forward_stages(SHRINK | EXPAND) call on the same x, adapters and
+ * tables filled, holding `s_f_planes` planes (2 when that forward ran its shrink inside the GEMM
+ * launch, i.e. lf_forward_launch_count returned 1; else 1).  The caller keeps that workspace
+ * unchanged until this call's work is done.  bf16/f16 only: the float32 path recomputes S_f.
+ * Saves the backward's x . A^T shrink (reference: mock_ops.py:79-80 recomputes it per route).
+ */
+LF_API int lf_backward_sf(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
+                          const void* grad_out_dev, const void* s_f_dev, int32_t s_f_planes, void* grad_x_dev,
+                          void* grad_a_dev, void* grad_b_dev, void* workspace_dev, size_t workspace_bytes,
+                          lf_stream_t stream);
+
+/*
  * Forward for callers that cannot allocate device memory: same inputs, output and result as
  * lf_forward, but no workspace argument.  The scratch lives in a fixed array of
  * LF_NOALLOC_SCRATCH_BYTES that the library declares in device memory; every GPU that loads the

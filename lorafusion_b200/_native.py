@@ -93,6 +93,9 @@ def _declare(L: ctypes.CDLL) -> None:
     L.lf_set_co_scheduling.restype = ctypes.c_int
     L.lf_backward.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_size_t, _c_p]
     L.lf_backward.restype = ctypes.c_int
+    L.lf_backward_sf.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_i32, _c_p, _c_p, _c_p, _c_p,
+                                 ctypes.c_size_t, _c_p]
+    L.lf_backward_sf.restype = ctypes.c_int
     L.lf_forward_noalloc.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p]
     L.lf_forward_noalloc.restype = ctypes.c_int
     L.lf_device_error.argtypes = [P(_c_i32)]

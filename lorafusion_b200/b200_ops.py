@@ -42,6 +42,10 @@ _WEIGHT_CACHE: dict[tuple, tuple] = {}
 _PLAN_BY_CONTENT: dict[tuple, "_Plan"] = {}
 _CACHE_MAX = 256
 _last_launches = 0
+# S_f = s x A^T left in recent forwards' workspaces, for a backward on the same inputs:
+# id(x) -> (weakref x, x version, weakref routing, plan, A signatures, workspace, planes)
+_SAVED_SF: dict[int, tuple] = {}
+_SAVED_MAX = 4
 
 
 def use_cooperative_launch(enabled: bool) -> None:
@@ -60,6 +64,7 @@ def clear_weight_cache() -> None:
     _ROUTE_CACHE.clear()
     _PLAN_CACHE.clear()
     _PLAN_BY_CONTENT.clear()
+    _SAVED_SF.clear()
     _PACK_CACHE.clear()
     _WEIGHT_CACHE.clear()
 
@@ -272,6 +277,7 @@ def fused_lora_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> tor
     global _last_launches
     routing.validate(x.shape[0])
     _last_launches = 0
+    x_in = x
     x = _activation(x, "x")
     device = x.device
     T, K = x.shape
@@ -297,7 +303,38 @@ def fused_lora_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> tor
                       ws.data_ptr(), ws.numel(), stream)
     nat.check(rc, "lf_forward")
     _last_launches = int(L.lf_forward_launch_count(ctypes.byref(prob), ctypes.byref(plan.info)))
+    if dtype != torch.float32 and plan.info.n_segtiles > 0:
+        _save_sf(x_in, routing, plan, lora_a, ws, 2 if _last_launches == 1 else 1)
     return y
+
+
+def _a_signature(plan, lora_a):
+    return tuple((lora_a[aid].data_ptr(), lora_a[aid]._version) for aid in plan.slots)
+
+
+def _save_sf(x, routing, plan, lora_a, ws, planes: int) -> None:
+    """Remember this forward's workspace (its S_f) for a backward on the same inputs."""
+    while len(_SAVED_SF) >= _SAVED_MAX:
+        _SAVED_SF.pop(next(iter(_SAVED_SF)))
+    try:
+        _SAVED_SF[id(x)] = (weakref.ref(x), x._version, weakref.ref(routing), plan, _a_signature(plan, lora_a), ws,
+                            planes)
+    except TypeError:  # pragma: no cover - objects without weakref support
+        pass
+
+
+def _saved_sf(x, routing, plan, lora_a):
+    """(workspace, planes) of a forward on this very x (unchanged since), routing, plan and A
+    tensors (unchanged since), or None."""
+    hit = _SAVED_SF.get(id(x))
+    if hit is None:
+        return None
+    xref, ver, rref, p, asig, ws, planes = hit
+    if xref() is not x or x._version != ver or rref() is not routing or p is not plan:
+        return None
+    if _a_signature(plan, lora_a) != asig:
+        return None
+    return ws, planes
 
 
 class PreparedForward:
@@ -356,6 +393,7 @@ def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, rout
     global _last_launches
     routing.validate(x.shape[0])
     _last_launches = 0
+    x_in = x
     x = _activation(x, "x")
     g = _activation(grad_out, "grad_out")
     device = x.device
@@ -384,10 +422,20 @@ def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, rout
     ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=device)
     prob = _problem(code, T, K, N, x, w, packs)
     stream = torch.cuda.current_stream(device).cuda_stream
-    rc = L.lf_backward(ctypes.byref(prob), ctypes.byref(info), plan.table_dev.data_ptr(), g.data_ptr(),
-                       grad_x.data_ptr(), ga_flat.data_ptr(), gb_flat.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+    saved = _saved_sf(x_in, routing, plan, lora_a) if dtype != torch.float32 else None
+    if saved is not None:  # the forward on these inputs left S_f: skip recomputing s x A^T
+        sf_ws, sf_planes = saved
+        rc = L.lf_backward_sf(ctypes.byref(prob), ctypes.byref(info), plan.table_dev.data_ptr(), g.data_ptr(),
+                              sf_ws.data_ptr(), sf_planes, grad_x.data_ptr(), ga_flat.data_ptr(), gb_flat.data_ptr(),
+                              ws.data_ptr(), ws.numel(), stream)
+        sf_ws.record_stream(torch.cuda.current_stream(device))
+    else:
+        rc = L.lf_backward(ctypes.byref(prob), ctypes.byref(info), plan.table_dev.data_ptr(), g.data_ptr(),
+                           grad_x.data_ptr(), ga_flat.data_ptr(), gb_flat.data_ptr(), ws.data_ptr(), ws.numel(),
+                           stream)
     nat.check(rc, "lf_backward")
-    _last_launches = max(0, int(L.lf_backward_launch_count(ctypes.byref(prob), ctypes.byref(info))))
+    n_launch = max(0, int(L.lf_backward_launch_count(ctypes.byref(prob), ctypes.byref(info))))
+    _last_launches = n_launch - 1 if saved is not None and n_launch == 4 else n_launch
     grad_a: dict[int, torch.Tensor] = {}
     grad_b: dict[int, torch.Tensor] = {}
     off = 0

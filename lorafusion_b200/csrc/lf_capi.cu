@@ -301,9 +301,12 @@ extern "C" int lf_forward(const lf_problem* prob, const lf_plan_info* info, cons
                            LF_STAGE_SHRINK | LF_STAGE_EXPAND, stream);
 }
 
-extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
-                           const void* grad_out_dev, void* grad_x_dev, void* grad_a_dev, void* grad_b_dev,
-                           void* workspace_dev, size_t workspace_bytes, lf_stream_t stream) {
+namespace {
+// The backward; `sf_given` (planes `sf_planes`) is S_f = s x A_i^T as a forward left it in its
+// workspace (tensor-core path only), or null to compute it here.
+int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, const void* grad_out_dev,
+                  const void* sf_given, int sf_planes, void* grad_x_dev, void* grad_a_dev, void* grad_b_dev,
+                  void* workspace_dev, size_t workspace_bytes, lf_stream_t stream) {
   int rc = check_problem(prob, info, table_dev);
   if (rc != LF_OK) return rc;
   const int T = prob->T, K = prob->K, N = prob->N;
@@ -331,6 +334,8 @@ extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, con
   char* ws = static_cast<char*>(workspace_dev);
   void* s_f = ws;
   void* s_b = ws + sb;
+  const bool reuse_sf = sf_given != nullptr && prob->dtype != LF_F32 && (sf_planes == 1 || sf_planes == 2);
+  if (reuse_sf) s_f = const_cast<void*>(sf_given);
 
   if (tc_eligible(prob, {prob->x_dev, prob->w_dev, prob->a_pack_dev, prob->bt_pack_dev, prob->at_pack_dev,
                          grad_out_dev, grad_x_dev, workspace_dev})) {
@@ -351,12 +356,13 @@ extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, con
     ok = ok && make_map(&dx.o, dt, grad_x_dev, K, T, K * es, 64, 32);
     if (!ok) return LF_ERR_UNSUPPORTED;
     dx.p = p_g;
-    int planes = 1;  // S_ext planes the grams sum
+    int planes = 1;  // S_b planes (S_f planes: sf_planes when reused, else the same as S_b's)
     bool gemm_done = false;
     if (lora) {
       dx.s = sb_map;
-      // Both shrinks inside the dX GEMM launch, on CTA pairs its round count leaves idle:
-      // job 1 = S_b (g . B_i, needed by the dX tiles), job 2 = S_f (x . A_i^T, read by the dB gram).
+      // The shrinks inside the dX GEMM launch, on CTA pairs its round count leaves idle: job 1 =
+      // S_b (g . B_i, needed by the dX tiles), job 2 = S_f (x . A_i^T, read by the dB gram) unless
+      // the forward's is reused.
       const int spare = cosched_allowed(ds) ? pair_spare_pairs(T, K, ds->num_sms, info->n_shrink_units) : 0;
       if (spare > 0) {
         PairShrink sh{};
@@ -365,7 +371,7 @@ extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, con
         sh.unit_ready = reinterpret_cast<uint64_t*>(ws + 2 * sb);
         sh.gen = next_generation();
         sh.n_pairs = spare;
-        sh.job2 = true;
+        sh.job2 = !reuse_sf;
         sh.p2_map = p_x;
         sh.a2_map = a_map;
         sh.s_ext2 = s_f;
@@ -380,8 +386,10 @@ extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, con
         }
       }
       if (!gemm_done) {
-        e = tc_shrink(dt, p_x, a_map, K, tb, s_f, ds->num_sms, st);
-        if (e != cudaSuccess) return LF_ERR_CUDA;
+        if (!reuse_sf) {
+          e = tc_shrink(dt, p_x, a_map, K, tb, s_f, ds->num_sms, st);
+          if (e != cudaSuccess) return LF_ERR_CUDA;
+        }
         e = tc_shrink(dt, p_g, bt_map, N, tb, s_b, ds->num_sms, st);
         if (e != cudaSuccess) return LF_ERR_CUDA;
       }
@@ -404,13 +412,20 @@ extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, con
       jobs[1].C = K;
       jobs[1].out = grad_a_dev;
       jobs[1].transpose_out = 1;
-      e = tc_gram(dt, jobs, 2, tb, ds->num_sms, st, planes, ws + 2 * sb + flag_bytes(info, 2), next_generation());
+      void* scratch = ws + 2 * sb + flag_bytes(info, 2);
+      const int f_planes = reuse_sf ? sf_planes : planes;
+      if (f_planes == planes) {
+        e = tc_gram(dt, jobs, 2, tb, ds->num_sms, st, planes, scratch, next_generation());
+      } else {  // S_f and S_b hold different plane counts: one launch each
+        e = tc_gram(dt, &jobs[0], 1, tb, ds->num_sms, st, f_planes, scratch, next_generation());
+        if (e == cudaSuccess) e = tc_gram(dt, &jobs[1], 1, tb, ds->num_sms, st, planes, scratch, next_generation());
+      }
       if (e != cudaSuccess) return LF_ERR_CUDA;
     }
     return LF_OK;
   }
 
-  float* sf = static_cast<float*>(s_f);
+  float* sf = reinterpret_cast<float*>(ws);  // the CUDA-core path computes its own float S_f
   float* sbp = static_cast<float*>(s_b);
   e = simt_shrink(dt, prob->x_dev, K, K, prob->a_pack_dev, tb, sf, st);
   if (e != cudaSuccess) return LF_ERR_CUDA;
@@ -423,6 +438,23 @@ extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, con
   if (e != cudaSuccess) return LF_ERR_CUDA;
   e = simt_gram(dt, prob->x_dev, K, K, sbp, tb, grad_a_dev, 1, st);
   return to_status(e);
+}
+}  // namespace
+
+extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
+                           const void* grad_out_dev, void* grad_x_dev, void* grad_a_dev, void* grad_b_dev,
+                           void* workspace_dev, size_t workspace_bytes, lf_stream_t stream) {
+  return backward_impl(prob, info, table_dev, grad_out_dev, nullptr, 0, grad_x_dev, grad_a_dev, grad_b_dev,
+                       workspace_dev, workspace_bytes, stream);
+}
+
+extern "C" int lf_backward_sf(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
+                              const void* grad_out_dev, const void* s_f_dev, int32_t s_f_planes, void* grad_x_dev,
+                              void* grad_a_dev, void* grad_b_dev, void* workspace_dev, size_t workspace_bytes,
+                              lf_stream_t stream) {
+  if (!s_f_dev || (s_f_planes != 1 && s_f_planes != 2)) return LF_ERR_INVALID_ARG;
+  return backward_impl(prob, info, table_dev, grad_out_dev, s_f_dev, s_f_planes, grad_x_dev, grad_a_dev, grad_b_dev,
+                       workspace_dev, workspace_bytes, stream);
 }
 
 extern "C" int lf_device_error(int32_t* code) {

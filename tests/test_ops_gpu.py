@@ -275,7 +275,8 @@ def test_gemm_tilings_match_oracle(single_cta):
 @pytest.mark.parametrize("co_scheduled", [True, False], ids=["one_launch_shrinks", "separate_shrinks"])
 def test_co_scheduling_switch_matches_oracle(co_scheduled):
     """Forward and backward with the routed shrinks inside the GEMM launch (forward 1 launch,
-    backward 2) and as launches of their own (2 and 4); both match the oracle."""
+    backward 2) and as launches of their own (2 and 3, S_f taken from the forward); both match
+    the oracle."""
     ops = _ops()
     routes = _routes_from_sizes([300, 5, 1, 94, 200, 100, 324], [0, 1, 2, 3, 0, 1, 2])  # 1024 rows
     case = _random_case(23, 1024, 512, 768, routes, {0: 16, 1: 8, 2: 32, 3: 64}, torch.bfloat16)
@@ -285,7 +286,8 @@ def test_co_scheduling_switch_matches_oracle(co_scheduled):
         y = ops.fused_lora_forward(x, w, a, b, ad, routing)
         assert ops.last_launch_count() == (1 if co_scheduled else 2)
         gx, ga, gb = ops.fused_lora_backward(g, x, w, a, b, ad, routing)
-        assert ops.last_launch_count() == (2 if co_scheduled else 4)
+        # the backward follows a forward on the same x: S_f comes from it (no x . A^T shrink)
+        assert ops.last_launch_count() == (2 if co_scheduled else 3)
     finally:
         ops.use_cooperative_launch(True)
     _check(y, case["y"], BF16_TOL, "forward")
@@ -319,3 +321,36 @@ def test_host_forward_streams_chunks_bit_exact():
     with pytest.raises(ValueError):
         ops.fused_lora_forward_host(x, w, a, b, ad, routing)
     _check(ref, case["y"], BF16_TOL, "forward")
+
+
+def test_backward_reuses_forward_s_only_for_unchanged_inputs():
+    """The backward takes S_f = s x A^T from a forward on the very same x and A (fewer launches,
+    same gradients as recomputing it) and recomputes it once x has changed in place."""
+    ops = _ops()
+    routes = _routes_from_sizes([300, 5, 1, 94, 200, 100, 324], [0, 1, 2, 3, 0, 1, 2])
+    case = _random_case(41, 1024, 512, 768, routes, {0: 16, 1: 8, 2: 32, 3: 16}, torch.bfloat16)
+    x, w, a, b, ad, routing, g = _to_torch(case, torch.bfloat16)
+    ops.clear_weight_cache()
+    ref = ops.fused_lora_backward(g, x, w, a, b, ad, routing)  # no forward yet: computes S_f itself
+    n_plain = ops.last_launch_count()
+    ops.fused_lora_forward(x, w, a, b, ad, routing)
+    got = ops.fused_lora_backward(g, x, w, a, b, ad, routing)  # reuses the forward's S_f
+    assert ops.last_launch_count() <= n_plain
+    for r_t, g_t in zip((ref[0],), (got[0],)):
+        _check(g_t, r_t.float().cpu().numpy(), BF16_TOL, "grad_x")
+    for k in ref[1]:
+        _check(got[1][k], ref[1][k].float().cpu().numpy(), BF16_TOL, f"grad_a[{k}]")
+        _check(got[2][k], ref[2][k].float().cpu().numpy(), BF16_TOL, f"grad_b[{k}]")
+        _check(got[2][k], case["gb"][k], BF16_TOL, f"grad_b[{k}] vs oracle")
+    # x changes in place after the forward: its saved S_f must not be used
+    ops.fused_lora_forward(x, w, a, b, ad, routing)
+    x.mul_(-1.0)
+    gx2, ga2, gb2 = ops.fused_lora_backward(g, x, w, a, b, ad, routing)
+    neg = dict(case)
+    sc = {i: case["alphas"][i] / case["ranks"][i] for i in case["ranks"]}
+    ngx, nga, ngb = mock_oracle.fused_lora_backward(case["g"], -case["x"], case["w"], case["a"], case["b"], sc, routes)
+    for k in ngb:
+        _check(gb2[k], ngb[k], BF16_TOL, f"grad_b[{k}] after x changed")
+        _check(ga2[k], nga[k], BF16_TOL, f"grad_a[{k}] after x changed")
+    from lorafusion_b200 import _native as nat
+    assert nat.device_error() == 0
