@@ -13,9 +13,12 @@ Per call, on the current CUDA stream:
   backward  2 routed shrinks + 1 fused dX launch + 2 segmented gram launches
 
 Host work is cached the way ``triton_ops._prepare`` caches its weight copies
-(``triton_ops.py:114-145``): routing tables per routing object, packed adapter
-slabs per (tensor identity, storage pointer, version counter) of every adapter
-tensor, converted base weights likewise.
+(``triton_ops.py:114-145``): validated routes and routing tables per routing
+object (re-checked against a snapshot of its route list), packed adapter slabs
+per (tensor identity, storage pointer, version counter) of every adapter
+tensor, converted base weights likewise.  A repeated call with unchanged inputs
+costs a few identity and version comparisons per adapter, so batches of hundreds
+of adapters stay ahead of the GPU.
 """
 
 from __future__ import annotations
@@ -35,17 +38,19 @@ __all__ = ["fused_lora_forward", "fused_lora_backward", "fused_lora_forward_host
 
 
 # --------------------------------------------------------------------------- caches
-_ROUTE_CACHE: dict[int, tuple] = {}
-_PLAN_CACHE: dict[tuple, "_Plan"] = {}
-_PACK_CACHE: dict[tuple, dict] = {}
+_ROUTE_CACHE: dict[int, "_Routes"] = {}
+_ADAPTER_CACHE: dict[tuple, list] = {}
 _WEIGHT_CACHE: dict[tuple, tuple] = {}
 _PLAN_BY_CONTENT: dict[tuple, "_Plan"] = {}
 _CACHE_MAX = 256
+_ADAPTER_SETS_PER_KEY = 4
 _last_launches = 0
 # S_f = s x A^T left in recent forwards' workspaces, for a backward on the same inputs:
-# id(x) -> (weakref x, x version, weakref routing, plan, A signatures, workspace, planes)
+# id(x) -> (weakref x, x version, route record, plan, adapter record, workspace, planes)
 _SAVED_SF: dict[int, tuple] = {}
 _SAVED_MAX = 4
+_VERSION = torch.Tensor._version.__get__
+_DATA_PTR = torch.Tensor.data_ptr
 
 
 def use_cooperative_launch(enabled: bool) -> None:
@@ -62,10 +67,9 @@ def use_cooperative_launch(enabled: bool) -> None:
 def clear_weight_cache() -> None:
     """Drop every cached table, packed adapter slab and converted weight."""
     _ROUTE_CACHE.clear()
-    _PLAN_CACHE.clear()
+    _ADAPTER_CACHE.clear()
     _PLAN_BY_CONTENT.clear()
     _SAVED_SF.clear()
-    _PACK_CACHE.clear()
     _WEIGHT_CACHE.clear()
 
 
@@ -74,30 +78,50 @@ def last_launch_count() -> int:
     return _last_launches
 
 
-def _route_arrays(routing):
-    """(starts, ends, adapter ids, slot of each route, slot adapter ids) for a routing object."""
+class _Routes:
+    """A routing object's routes, validated for ``valid_rows`` rows, as the arrays the table
+    builder takes, plus the routing plans built from them."""
+
+    __slots__ = ("ref", "snapshot", "valid_rows", "starts", "ends", "route_slot", "slots", "plans")
+
+    def __init__(self, routing, routes, total_rows):
+        self.ref = weakref.ref(routing)
+        self.snapshot = list(routes)
+        self.valid_rows = total_rows
+        n = len(routes)
+        self.starts = np.fromiter((r.row_start for r in routes), dtype=np.int32, count=n)
+        self.ends = np.fromiter((r.row_end for r in routes), dtype=np.int32, count=n)
+        slot_of: dict[int, int] = {}
+        self.route_slot = np.fromiter((slot_of.setdefault(r.adapter_id, len(slot_of)) for r in routes),
+                                      dtype=np.int32, count=n)
+        self.slots = tuple(slot_of)
+        self.plans: list = []
+
+
+def _routes(routing, total_rows: int) -> _Routes:
+    """Validate ``routing`` for ``total_rows`` rows (``TileRoutingConfig.validate``,
+    lorafusion/ops/config.py:55-69, raising its ``ValueError``) and return its arrays.
+
+    A routing object already seen is re-validated only when its route list differs from the
+    snapshot taken then (routes are immutable records, so comparing the list is enough) or the
+    row count changed.
+    """
     routes = routing.routes
-    key = id(routing)
-    hit = _ROUTE_CACHE.get(key)
-    if hit is not None:
-        ref, rlist, n, arrays = hit
-        if ref() is routing and rlist is routes and n == len(routes):
-            return arrays
-    starts = np.fromiter((r.row_start for r in routes), dtype=np.int32, count=len(routes))
-    ends = np.fromiter((r.row_end for r in routes), dtype=np.int32, count=len(routes))
-    aids = [r.adapter_id for r in routes]
-    slot_of: dict[int, int] = {}
-    route_slot = np.empty(len(routes), dtype=np.int32)
-    for i, aid in enumerate(aids):
-        route_slot[i] = slot_of.setdefault(aid, len(slot_of))
-    arrays = (starts, ends, route_slot, list(slot_of))
+    hit = _ROUTE_CACHE.get(id(routing))
+    if hit is not None and hit.ref() is routing and routes == hit.snapshot:
+        if hit.valid_rows != total_rows:
+            routing.validate(total_rows)
+            hit.valid_rows = total_rows
+        return hit
+    routing.validate(total_rows)
+    rec = _Routes(routing, routes, total_rows)
     if len(_ROUTE_CACHE) >= _CACHE_MAX:
         _ROUTE_CACHE.clear()
     try:
-        _ROUTE_CACHE[key] = (weakref.ref(routing), routes, len(routes), arrays)
+        _ROUTE_CACHE[id(routing)] = rec
     except TypeError:  # pragma: no cover - routing object without weakref support
         pass
-    return arrays
+    return rec
 
 
 class _Plan:
@@ -110,26 +134,85 @@ class _Plan:
         self.ranks = ranks
 
 
-def _plan(routing, total_rows: int, adapters, lora_a, device: torch.device) -> _Plan:
-    starts, ends, route_slot, slots = _route_arrays(routing)
-    ranks = tuple(int(lora_a[aid].shape[0]) for aid in slots)
-    scales = tuple(float(adapters[aid].scaling) for aid in slots)
-    key = (id(routing), total_rows, device, ranks, scales)
-    hit = _PLAN_CACHE.get(key)
-    if hit is not None and hit[0]() is routing:
-        return hit[1]
+class _AdapterSet:
+    """The A and B tensors of one call's adapter slots (in slot order) with the identity,
+    storage pointer and version counter of each, their ranks and scalings, and the padded
+    slabs packed from them (``packs``, per dtype and shape)."""
+
+    __slots__ = ("a", "b", "a_ids", "b_ids", "a_ver", "b_ver", "a_ptr", "b_ptr", "ranks", "spec_ids", "scales",
+                 "packs")
+
+    def __init__(self, a_list, b_list, a_ids, b_ids, specs):
+        self.a, self.b, self.a_ids, self.b_ids = a_list, b_list, a_ids, b_ids
+        self.a_ver = list(map(_VERSION, a_list))
+        self.b_ver = list(map(_VERSION, b_list))
+        self.a_ptr = list(map(_DATA_PTR, a_list))
+        self.b_ptr = list(map(_DATA_PTR, b_list))
+        self.ranks = tuple(int(t.shape[0]) if t.dim() == 2 else -1 for t in a_list)
+        self.spec_ids = list(map(id, specs))
+        self.scales = tuple(float(sp.scaling) for sp in specs)
+        self.packs: dict = {}
+
+    def unchanged(self, a_list, b_list) -> bool:
+        return (list(map(_VERSION, a_list)) == self.a_ver and list(map(_VERSION, b_list)) == self.b_ver
+                and list(map(_DATA_PTR, a_list)) == self.a_ptr and list(map(_DATA_PTR, b_list)) == self.b_ptr)
+
+
+def _adapters(rts: _Routes, lora_a, lora_b, adapters) -> _AdapterSet:
+    """The adapter record of this call's slots: reused while every A/B tensor is the same object
+    with the same storage and version counter, rebuilt (slabs repacked) otherwise.  A missing
+    adapter raises ``KeyError`` like the reference's dict lookups (mock_ops.py:40-42)."""
+    slots = rts.slots
+    specs = list(map(adapters.__getitem__, slots))
+    a_list = list(map(lora_a.__getitem__, slots))
+    b_list = list(map(lora_b.__getitem__, slots))
+    a_ids = list(map(id, a_list))
+    b_ids = list(map(id, b_list))
+    recs = _ADAPTER_CACHE.get(slots)
+    if recs is None:
+        if len(_ADAPTER_CACHE) >= _CACHE_MAX:
+            _ADAPTER_CACHE.clear()
+        recs = _ADAPTER_CACHE[slots] = []
+    for i, rec in enumerate(recs):
+        if rec.a_ids == a_ids and rec.b_ids == b_ids:
+            if not rec.unchanged(a_list, b_list):
+                rec = recs[i] = _AdapterSet(a_list, b_list, a_ids, b_ids, specs)  # same tensors, updated
+            elif list(map(id, specs)) != rec.spec_ids:
+                rec.spec_ids = list(map(id, specs))
+                rec.scales = tuple(float(sp.scaling) for sp in specs)
+            return rec
+    rec = _AdapterSet(a_list, b_list, a_ids, b_ids, specs)
+    recs.insert(0, rec)
+    del recs[_ADAPTER_SETS_PER_KEY:]
+    return rec
+
+
+def _plan(rts: _Routes, aset: _AdapterSet, total_rows: int, device: torch.device) -> _Plan:
+    ranks, scales = aset.ranks, aset.scales
+    for pr, ps, pd, plan in rts.plans:
+        if pd == device and pr == ranks and ps == scales:
+            return plan
+    if any(r <= 0 for r in ranks):
+        bad = rts.slots[next(i for i, r in enumerate(ranks) if r <= 0)]
+        raise ValueError(f"adapter {bad}: lora_a must be a non-empty [rank, in_features] matrix")
     # a new routing object with the same routes (a runtime that re-packs every batch) reuses the plan
-    content = (starts.tobytes(), ends.tobytes(), route_slot.tobytes(), tuple(slots), total_rows, device, ranks, scales)
-    same = _PLAN_BY_CONTENT.get(content)
-    if same is not None:
-        try:
-            _PLAN_CACHE[key] = (weakref.ref(routing), same)
-        except TypeError:  # pragma: no cover
-            pass
-        return same
+    content = (rts.starts.tobytes(), rts.ends.tobytes(), rts.route_slot.tobytes(), rts.slots, total_rows, device,
+               ranks, scales)
+    plan = _PLAN_BY_CONTENT.get(content)
+    if plan is None:
+        plan = _build_plan(rts, ranks, scales, total_rows, device)
+        if len(_PLAN_BY_CONTENT) >= _CACHE_MAX:
+            _PLAN_BY_CONTENT.clear()
+        _PLAN_BY_CONTENT[content] = plan
+    rts.plans.insert(0, (ranks, scales, device, plan))
+    del rts.plans[4:]
+    return plan
+
+
+def _build_plan(rts: _Routes, ranks, scales, total_rows: int, device) -> _Plan:
     L = nat.lib()
-    n_routes = len(starts)
-    cap = L.lf_plan_table_words(n_routes, total_rows, len(slots))
+    n_routes = len(rts.starts)
+    cap = L.lf_plan_table_words(n_routes, total_rows, len(rts.slots))
     if cap < 0:
         raise ValueError("routing too large for int32 tables")
     table = torch.empty(max(cap, 1), dtype=torch.int32, pin_memory=True)
@@ -138,50 +221,29 @@ def _plan(routing, total_rows: int, adapters, lora_a, device: torch.device) -> _
     sc = np.asarray(scales, dtype=np.float32)
     i32p = ctypes.POINTER(ctypes.c_int32)
     rc = L.lf_plan_tables(
-        starts.ctypes.data_as(i32p), ends.ctypes.data_as(i32p), route_slot.ctypes.data_as(i32p), n_routes,
-        total_rows, rk.ctypes.data_as(i32p), sc.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), len(slots),
-        ctypes.cast(table.data_ptr(), i32p), cap, ctypes.byref(info))
+        rts.starts.ctypes.data_as(i32p), rts.ends.ctypes.data_as(i32p), rts.route_slot.ctypes.data_as(i32p),
+        n_routes, total_rows, rk.ctypes.data_as(i32p), sc.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+        len(rts.slots), ctypes.cast(table.data_ptr(), i32p), cap, ctypes.byref(info))
     nat.check(rc, "lf_plan_tables")
     table_dev = table[: max(info.table_words, 1)].to(device, non_blocking=True)
-    plan = _Plan(info, table_dev, slots, ranks)
-    if len(_PLAN_CACHE) >= _CACHE_MAX:
-        _PLAN_CACHE.clear()
-    if len(_PLAN_BY_CONTENT) >= _CACHE_MAX:
-        _PLAN_BY_CONTENT.clear()
-    _PLAN_BY_CONTENT[content] = plan
-    try:
-        _PLAN_CACHE[key] = (weakref.ref(routing), plan)
-    except TypeError:  # pragma: no cover
-        pass
-    return plan
+    return _Plan(info, table_dev, rts.slots, ranks)
 
 
-def _tensor_sig(t: torch.Tensor):
-    return (id(t), t.data_ptr(), t._version)
-
-
-def _pack(plan: _Plan, lora_a, lora_b, dtype: torch.dtype, K: int, N: int, device, backward: bool) -> dict:
-    """Zero-padded adapter slabs in the layouts the kernels read (cached)."""
-    slots = plan.slots
-    a_list = [lora_a[aid] for aid in slots]
-    b_list = [lora_b[aid] for aid in slots]
-    key = (tuple(slots), tuple(_tensor_sig(t) for t in a_list), tuple(_tensor_sig(t) for t in b_list),
-           dtype, K, N, device, plan.info.r_pad)
-    entry = _PACK_CACHE.get(key)
+def _pack(plan: _Plan, aset: _AdapterSet, dtype: torch.dtype, K: int, N: int, device, backward: bool) -> dict:
+    """Zero-padded adapter slabs in the layouts the kernels read (cached in the adapter record)."""
+    key = (dtype, K, N, device, plan.info.r_pad)
+    entry = aset.packs.get(key)
     if entry is None:
-        for aid, a, b, r in zip(slots, a_list, b_list, plan.ranks):
+        for aid, a, b, r in zip(plan.slots, aset.a, aset.b, plan.ranks):
             if a.dim() != 2 or a.shape[1] != K or b.dim() != 2 or b.shape != (N, r):
                 raise ValueError(
                     f"adapter {aid}: lora_a {tuple(a.shape)} / lora_b {tuple(b.shape)} do not match "
                     f"in_features={K}, out_features={N}")
             if a.device != device or b.device != device:
                 raise ValueError(f"adapter {aid}: LoRA weights must live on {device}")
-        if len(_PACK_CACHE) >= _CACHE_MAX:
-            _PACK_CACHE.clear()
-        a_src = [t if t.is_contiguous() else t.contiguous() for t in a_list]
-        b_src = [t if t.is_contiguous() else t.contiguous() for t in b_list]
-        entry = {"src": (a_src, b_src), "keep": (a_list, b_list)}
-        _PACK_CACHE[key] = entry
+        a_src = [t if t.is_contiguous() else t.contiguous() for t in aset.a]
+        b_src = [t if t.is_contiguous() else t.contiguous() for t in aset.b]
+        entry = aset.packs[key] = {"src": (a_src, b_src)}
     want = ("a", "b", "bt", "at") if backward else ("a", "b")
     missing = [w for w in want if w not in entry]
     if missing:
@@ -275,7 +337,7 @@ def fused_lora_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> tor
     ``[T, out_features]`` tensor in ``x.dtype``.
     """
     global _last_launches
-    routing.validate(x.shape[0])
+    rts = _routes(routing, x.shape[0])
     _last_launches = 0
     x_in = x
     x = _activation(x, "x")
@@ -286,11 +348,10 @@ def fused_lora_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> tor
         raise ValueError(f"base_weight {tuple(base_weight.shape)} does not match x {tuple(x.shape)}")
     dtype = x.dtype
     code = _DTYPE_CODE[dtype]
-    for r in routing.routes:  # KeyError for an unknown adapter, like the reference
-        adapters[r.adapter_id]
+    aset = _adapters(rts, lora_a, lora_b, adapters)
     w = _weight(base_weight, dtype, device)
-    plan = _plan(routing, T, adapters, lora_a, device)
-    packs = _pack(plan, lora_a, lora_b, dtype, K, N, device, backward=False)
+    plan = _plan(rts, aset, T, device)
+    packs = _pack(plan, aset, dtype, K, N, device, backward=False)
     y = torch.empty((T, N), dtype=dtype, device=device)
     if T == 0 or N == 0:
         return y
@@ -304,35 +365,28 @@ def fused_lora_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> tor
     nat.check(rc, "lf_forward")
     _last_launches = int(L.lf_forward_launch_count(ctypes.byref(prob), ctypes.byref(plan.info)))
     if dtype != torch.float32 and plan.info.n_segtiles > 0:
-        _save_sf(x_in, routing, plan, lora_a, ws, 2 if _last_launches == 1 else 1)
+        _save_sf(x_in, rts, plan, aset, ws, 2 if _last_launches == 1 else 1)
     return y
 
 
-def _a_signature(plan, lora_a):
-    return tuple((lora_a[aid].data_ptr(), lora_a[aid]._version) for aid in plan.slots)
-
-
-def _save_sf(x, routing, plan, lora_a, ws, planes: int) -> None:
+def _save_sf(x, rts, plan, aset, ws, planes: int) -> None:
     """Remember this forward's workspace (its S_f) for a backward on the same inputs."""
     while len(_SAVED_SF) >= _SAVED_MAX:
         _SAVED_SF.pop(next(iter(_SAVED_SF)))
     try:
-        _SAVED_SF[id(x)] = (weakref.ref(x), x._version, weakref.ref(routing), plan, _a_signature(plan, lora_a), ws,
-                            planes)
+        _SAVED_SF[id(x)] = (weakref.ref(x), x._version, rts, plan, aset, ws, planes)
     except TypeError:  # pragma: no cover - objects without weakref support
         pass
 
 
-def _saved_sf(x, routing, plan, lora_a):
-    """(workspace, planes) of a forward on this very x (unchanged since), routing, plan and A
-    tensors (unchanged since), or None."""
+def _saved_sf(x, rts, plan, aset):
+    """(workspace, planes) of a forward on this very x (unchanged since), with the same validated
+    routes, plan and adapter record (every A and B tensor unchanged since), or None."""
     hit = _SAVED_SF.get(id(x))
     if hit is None:
         return None
-    xref, ver, rref, p, asig, ws, planes = hit
-    if xref() is not x or x._version != ver or rref() is not routing or p is not plan:
-        return None
-    if _a_signature(plan, lora_a) != asig:
+    xref, ver, r0, p0, a0, ws, planes = hit
+    if xref() is not x or x._version != ver or r0 is not rts or p0 is not plan or a0 is not aset:
         return None
     return ws, planes
 
@@ -347,16 +401,17 @@ class PreparedForward:
     """
 
     def __init__(self, x, base_weight, lora_a, lora_b, adapters, routing):
-        routing.validate(x.shape[0])
+        rts = _routes(routing, x.shape[0])
         self.x = _activation(x, "x")
         self.device = self.x.device
         self.T, self.K = self.x.shape
         self.N = base_weight.shape[0]
         dtype = self.x.dtype
         self.dtype = dtype
+        aset = _adapters(rts, lora_a, lora_b, adapters)
         self.w = _weight(base_weight, dtype, self.device)
-        self.plan = _plan(routing, self.T, adapters, lora_a, self.device)
-        self.packs = _pack(self.plan, lora_a, lora_b, dtype, self.K, self.N, self.device, backward=False)
+        self.plan = _plan(rts, aset, self.T, self.device)
+        self.packs = _pack(self.plan, aset, dtype, self.K, self.N, self.device, backward=False)
         code = _DTYPE_CODE[dtype]
         L = nat.lib()
         ws_bytes = L.lf_forward_workspace_bytes(ctypes.byref(self.plan.info), code)
@@ -391,7 +446,7 @@ def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, rout
     each summed over that adapter's routes; tensors are in ``x.dtype``.
     """
     global _last_launches
-    routing.validate(x.shape[0])
+    rts = _routes(routing, x.shape[0])
     _last_launches = 0
     x_in = x
     x = _activation(x, "x")
@@ -407,11 +462,10 @@ def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, rout
     if g.dtype != dtype:
         g = g.to(dtype)
     code = _DTYPE_CODE[dtype]
-    for r in routing.routes:
-        adapters[r.adapter_id]
+    aset = _adapters(rts, lora_a, lora_b, adapters)
     w = _weight(base_weight, dtype, device)
-    plan = _plan(routing, T, adapters, lora_a, device)
-    packs = _pack(plan, lora_a, lora_b, dtype, K, N, device, backward=True)
+    plan = _plan(rts, aset, T, device)
+    packs = _pack(plan, aset, dtype, K, N, device, backward=True)
     info = plan.info
     rtot = info.rank_total
     grad_x = torch.empty((T, K), dtype=dtype, device=device)
@@ -422,7 +476,7 @@ def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, rout
     ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=device)
     prob = _problem(code, T, K, N, x, w, packs)
     stream = torch.cuda.current_stream(device).cuda_stream
-    saved = _saved_sf(x_in, routing, plan, lora_a) if dtype != torch.float32 else None
+    saved = _saved_sf(x_in, rts, plan, aset) if dtype != torch.float32 else None
     if saved is not None:  # the forward on these inputs left S_f: skip recomputing s x A^T
         sf_ws, sf_planes = saved
         rc = L.lf_backward_sf(ctypes.byref(prob), ctypes.byref(info), plan.table_dev.data_ptr(), g.data_ptr(),
@@ -436,14 +490,29 @@ def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, rout
     nat.check(rc, "lf_backward")
     n_launch = max(0, int(L.lf_backward_launch_count(ctypes.byref(prob), ctypes.byref(info))))
     _last_launches = n_launch - 1 if saved is not None and n_launch == 4 else n_launch
-    grad_a: dict[int, torch.Tensor] = {}
+    return grad_x, *_grad_dicts(plan, ga_flat, gb_flat, K, N)
+
+
+def _grad_dicts(plan: _Plan, ga_flat, gb_flat, K: int, N: int):
+    """Per-adapter views of the packed gradients: dA_i rows [rank_prefix_i, +r_i) of a
+    [rank_total, K] matrix, dB_i the [N, r_i] block at element rank_prefix_i * N.  One split per
+    run of equal ranks keeps the view count per call, not per adapter, in Python."""
+    slots, ranks = plan.slots, plan.ranks
+    rtot = plan.info.rank_total
+    if not slots:
+        return {}, {}
+    grad_a = dict(zip(slots, ga_flat[:rtot * K].view(rtot, K).split(ranks)))
     grad_b: dict[int, torch.Tensor] = {}
-    off = 0
-    for aid, r in zip(plan.slots, plan.ranks):
-        grad_a[aid] = ga_flat[off * K:(off + r) * K].view(r, K)
-        grad_b[aid] = gb_flat[off * N:(off + r) * N].view(N, r)
-        off += r
-    return grad_x, grad_a, grad_b
+    i, off, n = 0, 0, len(slots)
+    while i < n:
+        r = ranks[i]
+        j = i + 1
+        while j < n and ranks[j] == r:
+            j += 1
+        grad_b.update(zip(slots[i:j], gb_flat[off * N:(off + (j - i) * r) * N].view((j - i) * N, r).split(N)))
+        off += (j - i) * r
+        i = j
+    return grad_a, grad_b
 
 
 # ----------------------------------------------------------------------------- host-resident batches
@@ -486,7 +555,7 @@ def fused_lora_forward_host(x_host, base_weight, lora_a, lora_b, adapters, routi
     for: synchronize the current stream before reading the result.  No counterpart in the
     reference (its ops take device tensors).
     """
-    routing.validate(x_host.shape[0])
+    _routes(routing, x_host.shape[0])
     if x_host.is_cuda or not base_weight.is_cuda:
         raise ValueError("x_host must be a host tensor and base_weight a CUDA tensor")
     if chunk_rows <= 0 or chunk_rows % 256:
