@@ -359,7 +359,12 @@ constexpr int kRoleStages = 9;
 constexpr int kPairBars = kRoleStages;  // barrier array length shared by both roles
 static_assert(kRoleStages * kRoleStageBytes <= kPairStages * (kPairABytes + kPairBBytes) + kPairOutBytes,
               "shrink-role stages must fit the pair kernel's shared memory");
-constexpr int kPairSmem = 1024 + kPairStages * (kPairABytes + kPairBBytes) + kPairOutBytes + 384;
+// LoRA table entries of one tile (slot, segment tile) staged by the producer warp; a tile with
+// more entries reads the rest from the table.
+constexpr int kPairEntPerLane = 6;
+constexpr int kPairEntBytes = 32 * kPairEntPerLane * 2 * 4;
+constexpr int kPairSmem = 1024 + kPairStages * (kPairABytes + kPairBBytes) + kPairOutBytes + 384 + kPairEntBytes;
+static_assert(kPairSmem <= 227 * 1024, "pair kernel shared memory");
 
 struct PairParams {
   void* out;
@@ -367,6 +372,7 @@ struct PairParams {
   int T, Nout, Kred;
   int n_mpairs, n_ntiles, group_m;
   int lora, r_pad;
+  int lora_per_stage;  // LoRA items (S tile + B tile, kBM x r_pad each) one pipeline stage holds
   uint32_t idesc_main, idesc_lora;
   uint32_t lora_layout, lora_sbo;
   // co-scheduled shrink: the first 2*n_shrink_pairs CTAs compute S_ext (P . A_slot^T) and publish
@@ -654,6 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* pub = drain + 1;  // shrink role: all epilogue warps finished writing a unit
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pub + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* pair_ent = reinterpret_cast<int*>(sOut + kPairOutBytes + 384);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (static_cast<int>(blockIdx.x) < 2 * prm.n_shrink_pairs) {
@@ -702,37 +709,43 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tempty_lead = map_to_cta(smem_u32(tempty), 0);
 
   if (warp == 0) {
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0, issued_mask = 0, last_parity = 0;
-      bool ok = true;
-      const uint32_t main_bytes = 2u * (kPairABytes + kPairBBytes);
-      const uint32_t lora_bytes = static_cast<uint32_t>(2 * 2 * kBM * prm.r_pad * 2);
-      for (int t = pair; t < total && ok; t += n_pairs) {
-        int mp, n;
-        pair_raster(t, prm, mp, n);
-        const int mtile = 2 * mp + static_cast<int>(crank);
-        int pb = 0, pe = 0, sl[4] = {0, 0, 0, 0}, ss[4] = {0, 0, 0, 0};
-        const int32_t* st_of = tb.base + (crank ? tb.off_pl_b : tb.off_pl_a);
-        // ready flags this tile's LoRA stages need, read early (relaxed) while the k-loop runs
-        int it0 = 0, it1 = 0;
-        uint64_t fl[9];
+    // Lane 0 issues every copy.  Each tile's LoRA table entries (slot, segment tile) are fetched
+    // by the whole warp before the tile's k-loop and staged in shared memory after it, so the
+    // LoRA copies that follow the k-loop wait on no table load.
+    int stage = 0;
+    uint32_t phase = 0, issued_mask = 0, last_parity = 0;
+    bool ok = true;
+    const uint32_t main_bytes = 2u * (kPairABytes + kPairBBytes);
+    const uint32_t lora_bytes = static_cast<uint32_t>(2 * 2 * kBM * prm.r_pad * 2);
+    const int lora_item_bytes = kBM * prm.r_pad * 2;  // one operand of one item, this CTA
+    const int32_t* st_of = tb.base + (crank ? tb.off_pl_b : tb.off_pl_a);
+    const int32_t* pl_slot = tb.base + tb.off_pl_slot;
+    for (int t = pair; t < total; t += n_pairs) {
+      int mp, n;
+      pair_raster(t, prm, mp, n);
+      const int mtile = 2 * mp + static_cast<int>(crank);
+      int pb = 0, pe = 0;
+      int e_slot[kPairEntPerLane], e_st[kPairEntPerLane];
+      if (prm.lora) {  // fetched while the k-loop runs
+        pb = ld_early(tb.base + tb.off_pair_lora + mp);
+        pe = ld_early(tb.base + tb.off_pair_lora + mp + 1);
+#pragma unroll
+        for (int q = 0; q < kPairEntPerLane; ++q) {
+          const int i = pb + lane + 32 * q;
+          e_slot[q] = i < pe ? ld_early(pl_slot + i) : 0;
+          e_st[q] = i < pe ? ld_early(st_of + i) : 0;
+        }
+      }
+      // ready flags this tile's LoRA stages need, read early (relaxed) while the k-loop runs
+      int it0 = 0, it1 = 0;
+      uint64_t fl[9];
+      if (lane == 0) {
         if (prm.lora && prm.n_shrink_pairs > 0) {
           it0 = 2 * ld_early(tb.base + tb.off_tile_unit + 2 * mp);
           it1 = 2 * ld_early(tb.base + tb.off_tile_unit + min(2 * mp + 2, tb.n_tiles));
           fl[0] = ld_relaxed_u64(prm.unit_ready);
 #pragma unroll
           for (int q = 0; q < 8; ++q) fl[q + 1] = it0 + q < it1 ? ld_relaxed_u64(prm.unit_ready + it0 + q) : prm.gen;
-        }
-        if (prm.lora) {  // fetched while the k-loop runs
-          pb = ld_early(tb.base + tb.off_pair_lora + mp);
-          pe = ld_early(tb.base + tb.off_pair_lora + mp + 1);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int i = min(pb + q, max(pe - 1, 0));
-            sl[q] = ld_early(tb.base + tb.off_pl_slot + i);
-            ss[q] = ld_early(st_of + i);
-          }
         }
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, tb.err, kErrTimeoutEmpty)) {
@@ -756,7 +769,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1;
           }
         }
-        if (!ok || !prm.lora) continue;
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+      if (!prm.lora) continue;
+      // lane 0 issued the previous tile's LoRA copies before this k-loop: the entries are free
+#pragma unroll
+      for (int q = 0; q < kPairEntPerLane; ++q) {
+        const int e = lane + 32 * q;
+        if (pb + e < pe) {
+          pair_ent[2 * e] = e_slot[q];
+          pair_ent[2 * e + 1] = e_st[q];
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
         if (prm.n_shrink_pairs > 0 && pe > pb) {  // S_ext of both row tiles (and the zero block) published?
           bool seen = it1 - it0 <= 8;
 #pragma unroll
@@ -766,37 +793,44 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else if (!wait_units_ready(prm.unit_ready, 0, 1, prm.gen, abort_flag, tb.err) ||
                      !wait_units_ready(prm.unit_ready, it0, it1, prm.gen, abort_flag, tb.err)) {
             ok = false;
-            break;
           }
           fence_proxy_async_global();
         }
-        for (int i = pb; i < pe && ok; ++i) {
-          const int q = i - pb;
-          const int slot = q == 0 ? sl[0] : q == 1 ? sl[1] : q == 2 ? sl[2] : q == 3 ? sl[3] : tb.pl_slot(i);
-          const int st = q == 0 ? ss[0] : q == 1 ? ss[1] : q == 2 ? ss[2] : q == 3 ? ss[3] : st_of[i];
-          for (int pl = 0; pl < prm.s_planes; ++pl) {
+        // LoRA items (pair-table entry, S plane), entry-major, packed lora_per_stage to a stage
+        const int n_items = (pe - pb) * prm.s_planes;
+        for (int i0 = 0; i0 < n_items && ok; i0 += prm.lora_per_stage) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, tb.err, kErrTimeoutEmpty)) {
             ok = false;
             break;
           }
-          if (crank == 0) mbar_arrive_expect_tx(&full[stage], lora_bytes);
+          const int cnt = min(prm.lora_per_stage, n_items - i0);
+          if (crank == 0) mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(cnt) * lora_bytes);
           const uint32_t fb = full_lead + static_cast<uint32_t>(stage * 8);
-          tma_load_2d_pair(sA + stage * kPairABytes, &map_s, fb, 0, pl * prm.s_plane_rows + st * kBM);
-          tma_load_2d_pair(sB + stage * kPairBBytes, &map_l, fb, 0,
-                           slot * prm.Nout + n * 256 + static_cast<int>(crank) * 128);
+          for (int c = 0; c < cnt; ++c) {
+            const int item = i0 + c;
+            const int e = item / prm.s_planes, pl = item - e * prm.s_planes;
+            const bool staged = e < 32 * kPairEntPerLane;
+            const int slot = staged ? pair_ent[2 * e] : pl_slot[pb + e];
+            const int st = staged ? pair_ent[2 * e + 1] : st_of[pb + e];
+            tma_load_2d_pair(sA + stage * kPairABytes + c * lora_item_bytes, &map_s, fb, 0,
+                             pl * prm.s_plane_rows + st * kBM);
+            tma_load_2d_pair(sB + stage * kPairBBytes + c * lora_item_bytes, &map_l, fb, 0,
+                             slot * prm.Nout + n * 256 + static_cast<int>(crank) * 128);
+          }
           issued_mask |= 1u << stage;
           last_parity = (last_parity & ~(1u << stage)) | (phase << stage);
           if (++stage == kPairStages) {
             stage = 0;
             phase ^= 1;
           }
-          }
         }
       }
-      if (!ok && crank == 0)  // copies of both CTAs complete on the even CTA's barriers
-        for (int s = 0; s < kPairStages; ++s)
-          if (issued_mask & (1u << s)) drain_wait(&full[s], (last_parity >> s) & 1u, tb.err);
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
     }
+    if (lane == 0 && !ok && crank == 0)  // copies of both CTAs complete on the even CTA's barriers
+      for (int s = 0; s < kPairStages; ++s)
+        if (issued_mask & (1u << s)) drain_wait(&full[s], (last_parity >> s) & 1u, tb.err);
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0 && crank == 0) {
@@ -805,6 +839,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true, issued_any = false;
       const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
       const uint32_t empty_local = smem_u32(empty), tfull_local = smem_u32(tfull);  // same offsets in both CTAs
+      const uint32_t lora_item_bytes = static_cast<uint32_t>(kBM * prm.r_pad * 2);
       int it = 0;
       for (int t = pair; t < total && ok; t += n_pairs, ++it) {
         int mp, n;
@@ -843,18 +878,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             phase ^= 1;
           }
         }
-        for (int j = 0; ok && j < n_lora; ++j) {
+        for (int j = 0; ok && j < n_lora; j += prm.lora_per_stage) {
           if (!mbar_wait(&full[stage], phase, abort_flag, tb.err, kErrTimeoutFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = a_base + stage * kPairABytes, b0 = b_base + stage * kPairBBytes;
-          for (int k = 0; k < prm.r_pad / 16; ++k) {
-            const uint64_t adesc = umma_sdesc(a0 + k * 32, 16, prm.lora_sbo, prm.lora_layout);
-            const uint64_t bdesc = umma_sdesc(b0 + k * 32, 16, prm.lora_sbo, prm.lora_layout);
-            umma_f16_pair(d, adesc, bdesc, prm.idesc_lora, acc);
-            acc = 1;
+          const int cnt = min(prm.lora_per_stage, n_lora - j);
+          for (int c = 0; c < cnt; ++c) {
+            const uint32_t a0 = a_base + stage * kPairABytes + c * lora_item_bytes;
+            const uint32_t b0 = b_base + stage * kPairBBytes + c * lora_item_bytes;
+            for (int k = 0; k < prm.r_pad / 16; ++k) {
+              const uint64_t adesc = umma_sdesc(a0 + k * 32, 16, prm.lora_sbo, prm.lora_layout);
+              const uint64_t bdesc = umma_sdesc(b0 + k * 32, 16, prm.lora_sbo, prm.lora_layout);
+              umma_f16_pair(d, adesc, bdesc, prm.idesc_lora, acc);
+              acc = 1;
+            }
           }
           issued_any = true;
           umma_commit_pair_both(empty_local + stage * 8);
@@ -1156,6 +1195,7 @@ struct GramParams {
   // MN chunks of the B operand).  K steps rotate over `chains` accumulators so that consecutive
   // MMAs do not wait on each other; the epilogue adds chains and planes in fixed order.
   int chains, acc_cols, tmem_cols;  // acc_cols = chains * planes * r_pad per buffer
+  int n_bufs;                       // accumulator buffers (<= kGramMaxBufs, n_bufs * acc_cols <= tmem_cols)
   uint32_t idesc;
   uint32_t s_layout, s_sbo, s_kstep;
   // Load balance: a slot with more than `cap` segment tiles is split into parts of about equal
@@ -1175,14 +1215,14 @@ constexpr int kGramRingBytes = 3 * (kGramDBytes + 2 * kBM * 64 * 2);  // 3 stage
 // Work units of one CTA (job, slot part, column block), staged in shared memory once with the
 // segment tiles each one streams, so no role waits on a dependent table load per unit.
 constexpr int kGramMaxUnits = 128;
-constexpr int kGramMaxSteps = 512;
+constexpr int kGramMaxSt = 1024;   // segment tiles whose list entry and row tile are staged (16-bit)
+constexpr int kGramMaxBufs = 8;    // TMEM accumulators (as many as 512 columns hold)
 struct GramUnit {
   int job, slot, b, e, rank, rank_prefix, cb;
   int parts;  // parts of this slot (1: written straight from TMEM)
   int pid;    // partial block of this part
   int pbase;  // partial block of part 0; part p is pbase + p * n_cblk
   int cid;    // counter row (x4 warps)
-  int s0;     // first staged step, or -1 (steps read from the table)
 };
 // Per slot position (slot_order index), read from the table once per CTA: the slot's metadata and,
 // per job, prefix sums of parts, split parts and split slots.  Only when n_slots <= kGramMaxSlots
@@ -1196,12 +1236,14 @@ struct GramSlotPrefix {
   int pid_off, cid_off;   // job 1's partial blocks and counter rows follow job 0's
   int use_split, cached;
 };
-struct GramStep {
-  int st, row0;
+// The slot lists (segment tile of each entry) and each segment tile's row tile, read once per CTA
+// when the table has at most kGramMaxSt segment tiles (`seg_cached`).
+struct GramSegs {
+  uint16_t st[kGramMaxSt];
+  uint16_t tile[kGramMaxSt];
 };
 constexpr int kGramSmem = 1024 + kGramRingBytes + kGramMaxUnits * static_cast<int>(sizeof(GramUnit)) +
-                          static_cast<int>(sizeof(GramSlotPrefix)) + kGramMaxSteps * static_cast<int>(sizeof(GramStep)) +
-                          256;
+                          static_cast<int>(sizeof(GramSlotPrefix)) + static_cast<int>(sizeof(GramSegs)) + 512;
 static_assert(kGramSmem <= 227 * 1024, "gram kernel shared memory");
 
 // Unit k of the combined list (job 0's units, then job 1's): part k / n_cblk of the job's parts,
@@ -1216,7 +1258,6 @@ __device__ __forceinline__ GramUnit gram_unit(const GramParams& prm, const GramS
   g.cb = kl - pg * n_cblk;
   g.parts = 1;
   g.pid = g.pbase = g.cid = 0;
-  g.s0 = -1;
   if (!sp.cached) {
     g.slot = tb.slot_order(pg);
     g.b = tb.slot_st(g.slot);
@@ -1281,15 +1322,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* ring = smem;
   GramUnit* units = reinterpret_cast<GramUnit*>(ring + kGramRingBytes);
   GramSlotPrefix& sp = *reinterpret_cast<GramSlotPrefix*>(units + kGramMaxUnits);
-  GramStep* steps = reinterpret_cast<GramStep*>(&sp + 1);
-  uint64_t* full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(steps + kGramMaxSteps) + 7) & ~uintptr_t(7));
+  GramSegs& segs = *reinterpret_cast<GramSegs*>(&sp + 1);
+  uint64_t* full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(&segs + 1) + 7) & ~uintptr_t(7));
   uint64_t* empty = full + kGramMaxStages;
   uint64_t* tfull = empty + kGramMaxStages;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
+  uint64_t* tempty = tfull + kGramMaxBufs;
+  uint64_t* drain = tempty + kGramMaxBufs;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* n_staged_steps = const_cast<int*>(abort_flag) + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Tables& tb = prm.tb;
@@ -1302,7 +1342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < prm.n_bufs; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 128);
     }
@@ -1322,6 +1362,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
   }
 
+  const bool seg_cached = tb.n_segtiles <= kGramMaxSt;
+  if (warp >= 3 && seg_cached)  // slot-list entries and row tiles of every segment tile
+    for (int j = threadIdx.x - 96; j < tb.n_segtiles; j += kThreads - 96) {
+      segs.st[j] = static_cast<uint16_t>(tb.slot_list(j));
+      segs.tile[j] = static_cast<uint16_t>(tb.st_tile(j));
+    }
   // Slot metadata and parts per slot position (warp 2): slots with more than `cap` segment tiles
   // are split, unless the partial blocks or counters that needs would not fit; every CTA decides
   // the same way.
@@ -1400,43 +1446,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp >= 2) {  // stage this CTA's units
     for (int k = threadIdx.x - 64; k < n_staged; k += kThreads - 64) units[k] = gram_unit(prm, sp, gram_zigzag(k, me, G));
   }
-  __syncthreads();
-  if (warp == 2) {  // step offsets of the staged units, in order, as long as they fit
-    int base = 0, fitted = 0;
-    for (int k0 = 0; k0 < n_staged; k0 += 32) {
-      const int k = k0 + lane;
-      const int len = k < n_staged ? units[k].e - units[k].b : 0;
-      int incl = len;
-#pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        const int u = __shfl_up_sync(0xffffffffu, incl, d);
-        if (lane >= d) incl += u;
-      }
-      const int s0 = base + incl - len;
-      const bool fit = s0 + len <= kGramMaxSteps;
-      if (k < n_staged) units[k].s0 = fit ? s0 : -1;
-      const int f = fit && k < n_staged ? s0 + len : 0;
-      fitted = max(fitted, __reduce_max_sync(0xffffffffu, f));
-      base += __shfl_sync(0xffffffffu, incl, 31);
-    }
-    if (lane == 0) *n_staged_steps = fitted;
-  }
-  __syncthreads();
-  if (warp >= 2) {  // each staged step's segment tile and D row
-    const int n_steps = *n_staged_steps;
-    for (int f = threadIdx.x - 64; f < n_steps; f += kThreads - 64) {
-      int lo = 0, hi = n_staged - 1;  // unit holding flat step f: last staged unit with s0 <= f
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (units[mid].s0 >= 0 && units[mid].s0 <= f) lo = mid;
-        else if (units[mid].s0 < 0) hi = mid - 1;
-        else hi = mid - 1;
-      }
-      const int st = tb.slot_list(units[lo].b + f - units[lo].s0);
-      steps[f].st = st;
-      steps[f].row0 = tb.st_tile(st) * kBM;
-    }
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -1455,14 +1464,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const CUtensorMap* md = g.job ? &map_d1 : &map_d0;
         const CUtensorMap* ms = g.job ? &map_s1 : &map_s0;
         for (int i = g.b; i < g.e && ok; ++i) {
-          int st, row0;
-          if (g.s0 >= 0) {
-            st = steps[g.s0 + i - g.b].st;
-            row0 = steps[g.s0 + i - g.b].row0;
-          } else {
-            st = tb.slot_list(i);
-            row0 = tb.st_tile(st) * kBM;
-          }
+          const int st = seg_cached ? segs.st[i] : tb.slot_list(i);
+          const int row0 = (seg_cached ? segs.tile[st] : tb.st_tile(st)) * kBM;
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, tb.err, kErrTimeoutEmpty)) {
             ok = false;
             break;
@@ -1497,8 +1500,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = 0; k < n_mine && ok; ++k) {
         const GramUnit g = unit(k);
         if (g.b == g.e) continue;  // adapter with only empty routes: epilogue writes zeros
-        const int buf = it & 1;
-        if (!mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1, abort_flag, tb.err, kErrTimeoutAcc)) {
+        const int buf = it % prm.n_bufs;
+        if (!mbar_wait(&tempty[buf], ((it / prm.n_bufs) & 1) ^ 1, abort_flag, tb.err, kErrTimeoutAcc)) {
           ok = false;
           break;
         }
@@ -1559,8 +1562,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         continue;
       }
-      const int buf = it & 1;
-      if (!warp_wait(&tfull[buf], (it >> 1) & 1, abort_flag, tb.err, kErrTimeoutAcc)) break;
+      const int buf = it % prm.n_bufs;
+      if (!warp_wait(&tfull[buf], (it / prm.n_bufs) & 1, abort_flag, tb.err, kErrTimeoutAcc)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * prm.acc_cols);
       const int chain_cols = prm.acc_cols / prm.chains;
@@ -1770,6 +1773,8 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
   p.idesc_lora = umma_idesc_f16(256, 256, fmt, 0, 0);
   p.lora_layout = umma_layout_for_span(tb.r_pad * 2);
   p.lora_sbo = sw_sbo(tb.r_pad);
+  p.lora_per_stage = tb.r_pad > 0 ? kPairABytes / (kBM * tb.r_pad * 2) : 1;  // 4, 2, 1 for r_pad 16, 32, 64
+  static_assert(kPairABytes / kBM == kPairBBytes / 128, "S and B items split a stage alike");
   p.tb = tb;
   const int total = p.n_mpairs * p.n_ntiles;
   if (total == 0) return cudaSuccess;
@@ -1901,8 +1906,9 @@ cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables
   p.chains = 4;
   while (p.chains > 1 && 2 * p.chains * width > 512) p.chains >>= 1;
   p.acc_cols = p.chains * width;
-  p.tmem_cols = 32;
-  while (p.tmem_cols < 2 * p.acc_cols) p.tmem_cols <<= 1;
+  p.tmem_cols = 512;  // one CTA per SM: the whole TMEM, as many accumulators as fit
+  p.n_bufs = p.tmem_cols / p.acc_cols;
+  if (p.n_bufs > kGramMaxBufs) p.n_bufs = kGramMaxBufs;
   p.idesc = umma_idesc_f16(kBM, width, fmt, 1, 1);
   p.s_layout = umma_layout_for_span(tb.r_pad * 2);
   p.s_sbo = sw_sbo(tb.r_pad);
