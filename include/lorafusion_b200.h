@@ -123,7 +123,12 @@ typedef struct lf_problem {
   const void* at_pack_dev; /* [n_slots, K, r_pad]  A_i^T                     (backward expand) */
 } lf_problem;
 
-/* Workspace bytes the forward / backward need for this table and dtype. */
+/*
+ * Workspace bytes the forward / backward use for this table and dtype.  About 20 MiB of it is
+ * the scratch of the GEMM's K-split tail (fp32 partial tiles of a last round cut along K);
+ * a smaller workspace that still holds the fixed sections is accepted, and the tail then
+ * splits only as far as the partial tiles fit (not at all below one tile).
+ */
 LF_API size_t lf_forward_workspace_bytes(const lf_plan_info* info, int32_t dtype);
 LF_API size_t lf_backward_workspace_bytes(const lf_plan_info* info, int32_t dtype);
 
@@ -223,7 +228,8 @@ LF_API int lf_backward_sf(const lf_problem* prob, const lf_plan_info* info, cons
  * LF_NOALLOC_SCRATCH_BYTES that the library declares in device memory; every GPU that loads the
  * library holds that array until the process exits.  No counterpart in the reference (its ops
  * allocate freely through torch).
- *  - Returns LF_ERR_CAPACITY when lf_forward_workspace_bytes(info, dtype) exceeds the array.
+ *  - Returns LF_ERR_CAPACITY when the workspace's fixed sections exceed the array (the
+ *    K-split tail scratch is optional and uses what is left).
  *  - Allocates nothing: no cudaMalloc/cudaFree and no allocating library call.
  *  - The first call on each device looks up the array's device address (with that device
  *    current); make that first call before any stream capture.

@@ -95,6 +95,8 @@ size_t segtile_elems(const lf_plan_info* info) {
 // K-half partial products of the co-scheduled shrink) for the tensor-core path
 size_t sext_bytes(const lf_plan_info* info) { return (segtile_elems(info) * 4 + 255) & ~size_t(255); }
 
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
 // ready flags of the (job, unit, K half) items when shrinks run inside the GEMM launch
 // (one job in the forward, two in the backward)
 size_t flag_bytes(const lf_plan_info* info, int jobs = 1) {
@@ -165,14 +167,42 @@ Tables make_tables(const lf_plan_info* info, const int32_t* table_dev) {
 
 using namespace lf;
 
+namespace lf {
+size_t forward_min_workspace_bytes(const lf_plan_info* info) {
+  return info ? align256(sext_bytes(info) + flag_bytes(info)) : 0;
+}
+}  // namespace lf
+
+namespace {
+size_t backward_min_workspace_bytes(const lf_plan_info* info) {
+  return info ? align256(2 * sext_bytes(info) + flag_bytes(info, 2) +
+                         gram_scratch_bytes(info->r_pad > 0 ? info->r_pad : 16))
+              : 0;
+}
+
+// The K-split tail's scratch at byte `off` of a workspace of `bytes`: as many partial tiles as
+// fit there (none: no split).
+PairTail tail_scratch(void* ws, size_t bytes, size_t off) {
+  PairTail t{};
+  if (ws == nullptr || bytes < off + kTailFlagBytes + kTailPartialBytes) return t;
+  char* base = static_cast<char*>(ws) + off;
+  t.flags = reinterpret_cast<uint64_t*>(base);
+  t.partial = reinterpret_cast<float*>(base + kTailFlagBytes);
+  const size_t fit = (bytes - off - kTailFlagBytes) / kTailPartialBytes;
+  t.slots = static_cast<int>(fit < static_cast<size_t>(kTailSlots) ? fit : kTailSlots);
+  t.gen = next_generation();
+  return t;
+}
+}  // namespace
+
 extern "C" size_t lf_forward_workspace_bytes(const lf_plan_info* info, int32_t dtype) {
   (void)dtype;
-  return info ? sext_bytes(info) + flag_bytes(info) : 0;
+  return info ? forward_min_workspace_bytes(info) + tail_scratch_bytes() : 0;
 }
 
 extern "C" size_t lf_backward_workspace_bytes(const lf_plan_info* info, int32_t dtype) {
   (void)dtype;
-  return info ? 2 * sext_bytes(info) + flag_bytes(info, 2) + gram_scratch_bytes(info->r_pad > 0 ? info->r_pad : 16) : 0;
+  return info ? backward_min_workspace_bytes(info) + tail_scratch_bytes() : 0;
 }
 
 extern "C" int lf_pack_adapters(int32_t src_dtype, int32_t dst_dtype, const uint64_t* src_ptrs_dev,
@@ -195,7 +225,7 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
   const int T = prob->T, K = prob->K, N = prob->N;
   if (T == 0 || N == 0) return LF_OK;
   if (!prob->x_dev || !prob->w_dev || !prob->a_pack_dev || !prob->b_pack_dev || !y_dev) return LF_ERR_INVALID_ARG;
-  if (workspace_bytes < lf_forward_workspace_bytes(info, prob->dtype) || !workspace_dev) return LF_ERR_CAPACITY;
+  if (workspace_bytes < forward_min_workspace_bytes(info) || !workspace_dev) return LF_ERR_CAPACITY;
   DeviceState* ds = nullptr;
   cudaError_t e = device_state(&ds);
   if (e != cudaSuccess) return LF_ERR_CUDA;
@@ -231,6 +261,8 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
     const int spare = (!single && !separate && do_shrink && lora && cosched_allowed(ds))
                           ? pair_spare_pairs(T, N, ds->num_sms, info->n_shrink_units)
                           : 0;
+    // the K-split tail needs a cooperative launch too
+    const PairTail tail = tail_scratch(workspace_dev, workspace_bytes, forward_min_workspace_bytes(info));
     if (spare > 0) {
       PairShrink sh{};
       sh.a_map = a_map;
@@ -238,7 +270,7 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
       sh.unit_ready = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace_dev) + sext_bytes(info));
       sh.gen = next_generation();
       sh.n_pairs = spare;
-      e = tc_gemm_pair(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st, &sh);
+      e = tc_gemm_pair(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st, &sh, &tail);
       if (e == cudaSuccess) return LF_OK;
       // The cooperative launch was refused (e.g. other work holds SMs, or a profiler
       // serializes launches): nothing ran; use the two-launch path from now on.
@@ -249,9 +281,19 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
       e = tc_shrink(dt, maps.p, a_map, K, tb, workspace_dev, ds->num_sms, st);
       if (e != cudaSuccess) return LF_ERR_CUDA;
     }
-    if (do_gemm)
-      e = single ? tc_gemm(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st)
-                 : tc_gemm_pair(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st);
+    if (do_gemm) {
+      if (single) {
+        e = tc_gemm(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st);
+      } else {
+        e = tc_gemm_pair(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st, nullptr,
+                         cosched_allowed(ds) ? &tail : nullptr);
+        if (e != cudaSuccess && cosched_allowed(ds)) {  // cooperative launch refused: nothing ran
+          (void)cudaGetLastError();
+          ds->no_cosched = true;
+          e = tc_gemm_pair(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st);
+        }
+      }
+    }
     return to_status(e);
   }
 
@@ -311,7 +353,7 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
   if (rc != LF_OK) return rc;
   const int T = prob->T, K = prob->K, N = prob->N;
   const size_t sb = sext_bytes(info);
-  if (workspace_bytes < lf_backward_workspace_bytes(info, prob->dtype) || !workspace_dev) return LF_ERR_CAPACITY;
+  if (workspace_bytes < backward_min_workspace_bytes(info) || !workspace_dev) return LF_ERR_CAPACITY;
   DeviceState* ds = nullptr;
   cudaError_t e = device_state(&ds);
   if (e != cudaSuccess) return LF_ERR_CUDA;
@@ -341,6 +383,7 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
                          grad_out_dev, grad_x_dev, workspace_dev})) {
     CUtensorMap p_x, p_g, a_map, bt_map, sf_map, sb_map;
     TcMaps dx;
+    const PairTail tail = tail_scratch(workspace_dev, workspace_bytes, backward_min_workspace_bytes(info));
     const uint64_t s_rows = 2 * static_cast<uint64_t>(info->n_segtiles + 1) * LF_TILE_ROWS;  // two planes
     bool ok = make_map(&p_x, dt, prob->x_dev, K, T, K * es, 64, 128) &&
               make_map(&p_g, dt, grad_out_dev, N, T, N * es, 64, 128) &&
@@ -376,7 +419,7 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
         sh.a2_map = a_map;
         sh.s_ext2 = s_f;
         sh.K2 = K;
-        e = tc_gemm_pair(dt, true, dx, T, K, N, lora, tb, grad_x_dev, K, ds->num_sms, st, &sh);
+        e = tc_gemm_pair(dt, true, dx, T, K, N, lora, tb, grad_x_dev, K, ds->num_sms, st, &sh, &tail);
         if (e == cudaSuccess) {
           planes = 2;
           gemm_done = true;
@@ -397,7 +440,13 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
       dx.s = dx.l = p_g;
     }
     if (!gemm_done) {
-      e = tc_gemm_pair(dt, true, dx, T, K, N, lora, tb, grad_x_dev, K, ds->num_sms, st);
+      e = tc_gemm_pair(dt, true, dx, T, K, N, lora, tb, grad_x_dev, K, ds->num_sms, st, nullptr,
+                       cosched_allowed(ds) ? &tail : nullptr);
+      if (e != cudaSuccess && cosched_allowed(ds)) {  // cooperative launch refused: nothing ran
+        (void)cudaGetLastError();
+        ds->no_cosched = true;
+        e = tc_gemm_pair(dt, true, dx, T, K, N, lora, tb, grad_x_dev, K, ds->num_sms, st);
+      }
       if (e != cudaSuccess) return LF_ERR_CUDA;
     }
     if (lora) {  // dB and dA in one launch

@@ -85,10 +85,27 @@ struct PairShrink {
   int K2;
 };
 // CTA pairs the pair GEMM can leave to a co-scheduled shrink without adding a round (0: none).
+// K-split tail of the pair GEMM (the last round of 256x256 tiles cut along K when it would
+// leave at least half of the CTA pairs idle): fp32 partial tiles and their release flags, in
+// caller scratch after the fixed workspace sections.  `slots` partial tiles fit there; `gen`
+// must differ from every earlier launch's on the same flags.
+constexpr int kTailSlots = 80;                              // >= the CTA pairs of a B200 (74)
+constexpr size_t kTailPartialBytes = size_t(256) * 256 * 4;  // one fp32 256x256 tile
+constexpr size_t kTailFlagBytes = (size_t(kTailSlots) * 8 * 8 + 255) & ~size_t(255);
+inline size_t tail_scratch_bytes() { return kTailFlagBytes + kTailSlots * kTailPartialBytes; }
+struct PairTail {
+  uint64_t* flags;  // [slot][2 CTAs][4 epilogue warps]
+  float* partial;   // [slot][256 x 256]
+  int slots;
+  uint64_t gen;
+};
 int pair_spare_pairs(int T, int Nout, int num_sms, int n_units);
+// `tail` (optional) enables the K-split tail; the launch is then cooperative.
 cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, int Nout, int Kred, bool lora,
                          const Tables& tb, void* out, int64_t ldo, int num_sms, cudaStream_t st,
-                         const PairShrink* shrink = nullptr);
+                         const PairShrink* shrink = nullptr, const PairTail* tail = nullptr);
+// Forward workspace without the tail scratch (the least lf_forward accepts).
+size_t forward_min_workspace_bytes(const lf_plan_info* info);
 // Gram load balance: slots (slot_order positions) the kernel can split into parts, and the
 // capacity of the fp32 partial blocks ([128][r_pad] each) and arrival counters (x4) it may use.
 constexpr int kGramMaxSlots = 512;

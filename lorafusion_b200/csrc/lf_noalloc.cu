@@ -14,6 +14,7 @@
 #include <mutex>
 
 #include "../../include/lorafusion_b200.h"
+#include "lf_internal.cuh"
 
 namespace {
 
@@ -31,7 +32,8 @@ bool g_scratch_known[64];
 extern "C" int lf_forward_noalloc(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
                                   void* y_dev, lf_stream_t stream) {
   if (!prob || !info) return LF_ERR_INVALID_ARG;
-  if (lf_forward_workspace_bytes(info, prob->dtype) > kScratchBytes) return LF_ERR_CAPACITY;
+  // the fixed sections must fit; the K-split tail of the GEMM uses as much of the rest as it can
+  if (lf::forward_min_workspace_bytes(info) > kScratchBytes) return LF_ERR_CAPACITY;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return LF_ERR_CUDA;
   void* scratch = nullptr;

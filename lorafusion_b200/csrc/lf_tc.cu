@@ -373,6 +373,13 @@ struct PairParams {
   int n_mpairs, n_ntiles, group_m;
   int lora, r_pad;
   int lora_per_stage;  // LoRA items (S tile + B tile, kBM x r_pad each) one pipeline stage holds
+  // K-split tail: when the last round of tiles would leave at least half of the pairs idle, each
+  // of its tiles is computed by tail_parts pairs over consecutive K ranges.  Parts before the last
+  // leave fp32 partial tiles in tail_partial and release their tail_flag words; the last part
+  // (which also runs the tile's LoRA stages) adds them, in part order, before it stores.
+  int tail_parts;         // 1: no split
+  float* tail_partial;    // [slot][2 CTAs][4 epilogue warps][4 chunks][16 float4][32 rows]
+  uint64_t* tail_flag;    // [slot][2 CTAs][4 epilogue warps] = gen once that partial is written
   uint32_t idesc_main, idesc_lora;
   uint32_t lora_layout, lora_sbo;
   // co-scheduled shrink: the first 2*n_shrink_pairs CTAs compute S_ext (P . A_slot^T) and publish
@@ -399,6 +406,52 @@ __device__ __forceinline__ void pair_raster(int t, const PairParams& p, int& mp,
   const int r = t - g * per_group;
   mp = first + r % gsize;
   n = r / gsize;
+}
+
+// Work units of one GEMM pair: the full tiles t = pair + k * n_pairs of the first `rounds`
+// rounds, then at most one tail unit.  Tail unit v (counted from the last pair down) is part
+// v % parts of tail tile v / parts; partial slot = tail tile * (parts - 1) + part.
+struct PairSched {
+  int rounds, tail_base, n_tail, parts;
+};
+__device__ __forceinline__ PairSched pair_sched(const PairParams& p, int n_pairs) {
+  const int total = p.n_mpairs * p.n_ntiles;
+  PairSched s;
+  s.rounds = total / n_pairs;
+  s.tail_base = s.rounds * n_pairs;
+  const int rem = total - s.tail_base;
+  s.parts = rem > 0 && p.tail_parts > 1 ? p.tail_parts : 1;
+  s.n_tail = rem * s.parts;
+  return s;
+}
+struct PairUnit {
+  int mp, n;
+  int kb0, kb1;   // K blocks of this unit
+  int part;       // -1: whole tile; else part of a split tail tile
+  int slot0;      // first partial slot of that tile
+  bool last;      // stores the output (whole tile, or the tile's last part)
+};
+__device__ __forceinline__ PairUnit pair_unit(const PairParams& p, const PairSched& s, int pair, int n_pairs,
+                                              int k, int nkb) {
+  PairUnit u;
+  if (k < s.rounds) {
+    pair_raster(pair + k * n_pairs, p, u.mp, u.n);
+    u.kb0 = 0;
+    u.kb1 = nkb;
+    u.part = -1;
+    u.slot0 = 0;
+    u.last = true;
+    return u;
+  }
+  const int v = n_pairs - 1 - pair;
+  const int j = v / s.parts, q = v - j * s.parts;
+  pair_raster(s.tail_base + j, p, u.mp, u.n);
+  u.kb0 = q * nkb / s.parts;
+  u.kb1 = (q + 1) * nkb / s.parts;
+  u.part = s.parts > 1 ? q : -1;
+  u.slot0 = j * (s.parts - 1);
+  u.last = q == s.parts - 1;
+  return u;
 }
 
 // Bounded wait until ready[u] == gen for every u in [u0, u1) (acquire).
@@ -671,8 +724,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t crank = cluster_ctarank();  // 0: issues the MMAs
   const int pair = static_cast<int>(blockIdx.x >> 1) - prm.n_shrink_pairs;
   const int n_pairs = static_cast<int>(gridDim.x >> 1) - prm.n_shrink_pairs;
-  const int total = prm.n_mpairs * prm.n_ntiles;
   const int nkb = (prm.Kred + kBK - 1) / kBK;
+  const PairSched sched = pair_sched(prm, n_pairs);
+  const int n_units = sched.rounds + (n_pairs - 1 - pair < sched.n_tail ? 1 : 0);
   const Tables& tb = prm.tb;
 
   if (threadIdx.x == 0) {
@@ -720,13 +774,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lora_item_bytes = kBM * prm.r_pad * 2;  // one operand of one item, this CTA
     const int32_t* st_of = tb.base + (crank ? tb.off_pl_b : tb.off_pl_a);
     const int32_t* pl_slot = tb.base + tb.off_pl_slot;
-    for (int t = pair; t < total; t += n_pairs) {
-      int mp, n;
-      pair_raster(t, prm, mp, n);
+    for (int k = 0; k < n_units; ++k) {
+      const PairUnit un = pair_unit(prm, sched, pair, n_pairs, k, nkb);
+      const int mp = un.mp, n = un.n;
+      const bool lora = prm.lora && un.last;  // the LoRA stages belong to the part that stores
       const int mtile = 2 * mp + static_cast<int>(crank);
       int pb = 0, pe = 0;
       int e_slot[kPairEntPerLane], e_st[kPairEntPerLane];
-      if (prm.lora) {  // fetched while the k-loop runs
+      if (lora) {  // fetched while the k-loop runs
         pb = ld_early(tb.base + tb.off_pair_lora + mp);
         pe = ld_early(tb.base + tb.off_pair_lora + mp + 1);
 #pragma unroll
@@ -740,14 +795,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it0 = 0, it1 = 0;
       uint64_t fl[9];
       if (lane == 0) {
-        if (prm.lora && prm.n_shrink_pairs > 0) {
+        if (lora && prm.n_shrink_pairs > 0) {
           it0 = 2 * ld_early(tb.base + tb.off_tile_unit + 2 * mp);
           it1 = 2 * ld_early(tb.base + tb.off_tile_unit + min(2 * mp + 2, tb.n_tiles));
           fl[0] = ld_relaxed_u64(prm.unit_ready);
 #pragma unroll
           for (int q = 0; q < 8; ++q) fl[q + 1] = it0 + q < it1 ? ld_relaxed_u64(prm.unit_ready + it0 + q) : prm.gen;
         }
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, tb.err, kErrTimeoutEmpty)) {
             ok = false;
             break;
@@ -772,7 +827,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
       if (!ok) break;
-      if (!prm.lora) continue;
+      if (!lora) continue;
       // lane 0 issued the previous tile's LoRA copies before this k-loop: the entries are free
 #pragma unroll
       for (int q = 0; q < kPairEntPerLane; ++q) {
@@ -841,12 +896,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t empty_local = smem_u32(empty), tfull_local = smem_u32(tfull);  // same offsets in both CTAs
       const uint32_t lora_item_bytes = static_cast<uint32_t>(kBM * prm.r_pad * 2);
       int it = 0;
-      for (int t = pair; t < total && ok; t += n_pairs, ++it) {
-        int mp, n;
-        pair_raster(t, prm, mp, n);
+      for (int k = 0; k < n_units && ok; ++k, ++it) {
+        const PairUnit un = pair_unit(prm, sched, pair, n_pairs, k, nkb);
+        const int mp = un.mp;
         const int buf = it & 1;
         int n_lora = 0;
-        if (prm.lora)
+        if (prm.lora && un.last)
           n_lora = (ld_early(tb.base + tb.off_pair_lora + mp + 1) - ld_early(tb.base + tb.off_pair_lora + mp)) *
                    prm.s_planes;
         if (!mbar_wait(&tempty[buf], ((it >> 1) & 1) ^ 1, abort_flag, tb.err, kErrTimeoutAcc)) {
@@ -856,7 +911,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(buf * 256);
         uint32_t acc = 0;
-        for (int kb = 0; kb < nkb; ++kb) {
+        for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, tb.err, kErrTimeoutFull)) {
             ok = false;
             break;
@@ -915,12 +970,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;
     int it = 0;
     int n_stores = 0;
-    for (int t = pair; t < total; t += n_pairs, ++it) {
-      int mp, n;
-      pair_raster(t, prm, mp, n);
+    const int wslot = static_cast<int>(crank) * 4 + q;  // this warp's 32 rows of a partial tile
+    for (int k = 0; k < n_units; ++k, ++it) {
+      const PairUnit un = pair_unit(prm, sched, pair, n_pairs, k, nkb);
+      const int mp = un.mp, n = un.n;
       const int buf = it & 1;
       if (!warp_wait(&tfull[buf], (it >> 1) & 1, abort_flag, tb.err, kErrTimeoutAcc)) break;
       tc_fence_after();
+      if (un.part > 0 && un.last) {  // the earlier parts of this tile have published their partials?
+        int ok = 1;
+        if (lane == 0)
+          for (int p = 0; p < un.part && ok; ++p)
+            ok = wait_units_ready(prm.tail_flag, (un.slot0 + p) * 8 + wslot, (un.slot0 + p) * 8 + wslot + 1,
+                                  prm.gen, abort_flag, tb.err) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        __syncwarp();
+      }
       // rows [row0, row0+32) of this CTA's tile: TMEM -> registers -> swizzled staging -> TMA store
       const int row0 = (2 * mp + static_cast<int>(crank)) * kBM + q * 32;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * 256);
@@ -935,6 +1000,34 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(tempty_lead + buf * 8);
+        }
+        if (un.part >= 0) {
+          // partial tiles: slot, warp rows, 64-column chunk c; float4 i of lane (row) l at
+          // i * 32 + l, so each warp-wide access covers 512 contiguous bytes
+          const size_t chunk_off = static_cast<size_t>(c) * 2048;
+          if (!un.last) {
+            float4* dst = reinterpret_cast<float4*>(
+                              prm.tail_partial + (static_cast<size_t>(un.slot0 + un.part) * 8 + wslot) * (4 * 2048) +
+                              chunk_off) + lane;
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              dst[i * 32] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                                        __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+            continue;
+          }
+          for (int p = 0; p < un.part; ++p) {  // add the earlier parts in part order
+            const float4* src = reinterpret_cast<const float4*>(
+                                    prm.tail_partial + (static_cast<size_t>(un.slot0 + p) * 8 + wslot) * (4 * 2048) +
+                                    chunk_off) + lane;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float4 f = __ldcg(src + i * 32);
+              v[4 * i] = __float_as_uint(__uint_as_float(v[4 * i]) + f.x);
+              v[4 * i + 1] = __float_as_uint(__uint_as_float(v[4 * i + 1]) + f.y);
+              v[4 * i + 2] = __float_as_uint(__uint_as_float(v[4 * i + 2]) + f.z);
+              v[4 * i + 3] = __float_as_uint(__uint_as_float(v[4 * i + 3]) + f.w);
+            }
+          }
         }
         const int col0 = n * 256 + c * 64;
         if (row0 >= prm.T || col0 >= prm.Nout) continue;
@@ -958,6 +1051,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           bulk_commit();
         }
         ++n_stores;
+      }
+      if (un.part >= 0 && !un.last) {  // publish this warp's share of the partial tile
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) st_release_u64(prm.tail_flag + (un.slot0 + un.part) * 8 + wslot, prm.gen);
       }
     }
     if (lane == 0) bulk_wait_all();
@@ -1752,7 +1850,7 @@ int pair_spare_pairs(int T, int Nout, int num_sms, int n_units) {
 
 cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, int Nout, int Kred, bool lora,
                          const Tables& tb, void* out, int64_t ldo, int num_sms, cudaStream_t st,
-                         const PairShrink* shrink) {
+                         const PairShrink* shrink, const PairTail* tail) {
   PairParams p{};
   p.out = out;
   p.ldo = ldo;
@@ -1776,9 +1874,11 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
   p.lora_per_stage = tb.r_pad > 0 ? kPairABytes / (kBM * tb.r_pad * 2) : 1;  // 4, 2, 1 for r_pad 16, 32, 64
   static_assert(kPairABytes / kBM == kPairBBytes / 128, "S and B items split a stage alike");
   p.tb = tb;
+  p.tail_parts = 1;
   const int total = p.n_mpairs * p.n_ntiles;
   if (total == 0) return cudaSuccess;
   const int all_pairs = num_sms / 2;
+  const int nkb = (Kred + kBK - 1) / kBK;
   int gemm_pairs = total < all_pairs ? total : all_pairs;
   const CUtensorMap* a_map = &maps.p;  // unused unless a shrink is co-scheduled
   const CUtensorMap* p2_map = &maps.p;
@@ -1800,6 +1900,24 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
     const int rounds = (total + all_pairs - 1) / all_pairs;
     gemm_pairs = (total + rounds - 1) / rounds;
   }
+  if (tail != nullptr && tail->slots > 0) {
+    // Cut the tail tiles along K when the last round is at most half full (or there are fewer
+    // tiles than pairs), into as many parts (<= 4, each >= 2 k-blocks) as the idle pairs and the
+    // partial slots allow.
+    const bool few = total < gemm_pairs || (p.n_shrink_pairs == 0 && total < all_pairs);
+    const int avail = few && p.n_shrink_pairs == 0 ? all_pairs : gemm_pairs;
+    const int rem = few ? total : total - (total / gemm_pairs) * gemm_pairs;
+    int parts = rem > 0 && 2 * rem <= avail ? avail / rem : 1;
+    if (parts > 4) parts = 4;
+    while (parts > 1 && (rem * (parts - 1) > tail->slots || nkb < 2 * parts)) --parts;
+    if (parts > 1) {
+      if (few) gemm_pairs = total * parts;  // every tile is a tail tile, one part per pair
+      p.tail_parts = parts;
+      p.tail_partial = tail->partial;
+      p.tail_flag = tail->flags;
+      if (p.n_shrink_pairs == 0) p.gen = tail->gen;  // else the shrink's generation serves both
+    }
+  }
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * (gemm_pairs + p.n_shrink_pairs));
   cfg.blockDim = dim3(kThreads);
@@ -1810,11 +1928,12 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  // GEMM pairs wait on the shrink CTAs' flags: all CTAs must be resident at once
+  // GEMM pairs wait on the shrink CTAs' flags, last tail parts on the earlier parts' flags: all
+  // CTAs must be resident at once
   attr[1].id = cudaLaunchAttributeCooperative;
   attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = p.n_shrink_pairs > 0 ? 2 : 1;
+  cfg.numAttrs = p.n_shrink_pairs > 0 || p.tail_parts > 1 ? 2 : 1;
   cudaError_t e;
 #define LF_LAUNCH_PAIR(QMN, OT)                                                                  \
   e = ensure_smem(tc_gemm_pair_kernel<QMN, OT>, kPairSmem);                                     \

@@ -299,6 +299,60 @@ def test_co_scheduling_switch_matches_oracle(co_scheduled):
     assert nat.device_error() == 0
 
 
+def test_k_split_tail_matches_whole_tiles():
+    """The GEMM's last round, when at most half full, runs its tiles as K-split parts on the idle
+    CTA pairs (partial fp32 tiles summed in part order by the last part).  2560 x 4096 with the
+    shrink in its own launch: 160 tiles on 74 pairs, 12 tail tiles in 4 K parts each.  The result
+    equals whole tiles up to fp32 summation order, is repeatable bit for bit, and matches the
+    oracle; without cooperative launches the tail is not split."""
+    from lorafusion_b200 import _native as nat
+    ops = _ops()
+    routes = _routes_from_sizes([700, 3, 1100, 257, 500], [0, 1, 2, 0, 3])  # 2560 rows
+    case = _random_case(41, 2560, 512, 4096, routes, {0: 16, 1: 8, 2: 32, 3: 16}, torch.bfloat16)
+    x, w, a, b, ad, routing, g = _to_torch(case, torch.bfloat16)
+    prep = ops.prepare_forward(x, w, a, b, ad, routing)
+
+    def run(stages_list):
+        y = prep.new_output()
+        for st in stages_list:
+            prep.launch(y, st)
+        return y
+
+    two = [nat.LF_STAGE_SHRINK, nat.LF_STAGE_EXPAND]
+    base = [nat.LF_STAGE_BASE]
+    y_split, y_split2, base_split = run(two), run(two), run(base)
+    ops.use_cooperative_launch(False)
+    try:
+        y_whole, base_whole = run(two), run(base)
+    finally:
+        ops.use_cooperative_launch(True)
+    assert torch.equal(y_split, y_split2)
+    torch.testing.assert_close(y_split.float(), y_whole.float(), rtol=1e-2, atol=2e-2)
+    torch.testing.assert_close(base_split.float(), base_whole.float(), rtol=1e-2, atol=2e-2)
+    _check(y_split, case["y"], BF16_TOL, "forward, K-split tail")
+    _check(base_split, case["x"] @ case["w"].T, BF16_TOL, "base GEMM, K-split tail")
+    assert nat.device_error() == 0
+
+
+def test_k_split_small_problem_uses_all_pairs():
+    """Fewer tiles than CTA pairs (T=300, N=768: 6 tiles) and no co-scheduled shrink: each tile is
+    cut into 4 K parts; forward and the base GEMM match the oracle."""
+    from lorafusion_b200 import _native as nat
+    ops = _ops()
+    routes = _routes_from_sizes([100, 77, 123], [0, 1, 0])
+    case = _random_case(43, 300, 1024, 768, routes, {0: 16, 1: 32}, torch.bfloat16)
+    x, w, a, b, ad, routing, g = _to_torch(case, torch.bfloat16)
+    prep = ops.prepare_forward(x, w, a, b, ad, routing)
+    y = prep.new_output()
+    prep.launch(y, nat.LF_STAGE_SHRINK)
+    prep.launch(y, nat.LF_STAGE_EXPAND)
+    _check(y, case["y"], BF16_TOL, "forward, K-split small problem")
+    y0 = prep.new_output()
+    prep.launch(y0, nat.LF_STAGE_BASE)
+    _check(y0, case["x"] @ case["w"].T, BF16_TOL, "base GEMM, K-split small problem")
+    assert nat.device_error() == 0
+
+
 def test_host_forward_streams_chunks_bit_exact():
     """fused_lora_forward_host (pinned host batch, row chunks, copies overlapped) equals one
     fused_lora_forward over the whole batch bit for bit; routes cross chunk boundaries."""
