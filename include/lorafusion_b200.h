@@ -191,11 +191,16 @@ LF_API int lf_forward_launch_count(const lf_problem* prob, const lf_plan_info* i
 LF_API int lf_backward_launch_count(const lf_problem* prob, const lf_plan_info* info);
 
 /*
- * Process-wide switch for the co-scheduled launches (default on): with 0, lf_forward and
- * lf_backward run each routed shrink as an ordinary launch of its own instead of inside the
- * GEMM's cooperative launch.  For profilers and SM-partitioned GPUs, which refuse cooperative
- * launches (a refused launch also turns co-scheduling off for that device by itself).
- * No counterpart in the reference.
+ * Process-wide switch for the co-scheduled (cooperative) launches:
+ *   1 (default) the routed shrinks run inside the GEMM's launch on CTA pairs the GEMM's round
+ *     count leaves idle (when there are at least four), the GEMM on the others; the GEMM's last
+ *     round may be K-split over idle CTA pairs;
+ *   2  the same, but every CTA first computes its share of the shrink items and then its GEMM
+ *     tiles (which wait only for the S tiles they read), so the GEMM has every CTA pair;
+ *   0  no cooperative launches: each routed shrink is an ordinary launch of its own and no tail
+ *     is K-split.  For profilers and SM-partitioned GPUs, which refuse cooperative launches (a
+ *     refused launch also turns co-scheduling off for that device by itself).
+ * Other values return LF_ERR_INVALID_ARG.  No counterpart in the reference.
  */
 LF_API int lf_set_co_scheduling(int32_t enable);
 

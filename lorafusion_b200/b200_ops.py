@@ -53,15 +53,18 @@ _VERSION = torch.Tensor._version.__get__
 _DATA_PTR = torch.Tensor.data_ptr
 
 
-def use_cooperative_launch(enabled: bool) -> None:
+def use_cooperative_launch(enabled: bool, shrink_prologue: bool = False) -> None:
     """Allow (default) or forbid the co-scheduled cooperative launches (process-wide).
 
-    When allowed, the routed shrinks run inside the GEMM's launch on CTA pairs the GEMM
-    leaves idle (forward: 1 launch; backward: 2).  Profilers and SM-partitioned GPUs refuse
-    cooperative launches; forbid them there and every shrink runs as a launch of its own
-    (forward: 2 launches; backward: 4).
+    When allowed, the routed shrinks run inside the GEMM's launch (forward: 1 launch;
+    backward: 2): by default on CTA pairs the GEMM's round count leaves idle (when there are at
+    least four; otherwise forward 2 launches, backward 3-4); with ``shrink_prologue`` every CTA
+    instead computes its share of the shrink items before its GEMM tiles.  Profilers and
+    SM-partitioned GPUs refuse cooperative launches; forbid them there and every shrink runs as
+    a launch of its own (forward: 2 launches; backward: 4).
     """
-    nat.check(nat.lib().lf_set_co_scheduling(1 if enabled else 0), "lf_set_co_scheduling")
+    mode = (2 if shrink_prologue else 1) if enabled else 0
+    nat.check(nat.lib().lf_set_co_scheduling(mode), "lf_set_co_scheduling")
 
 
 def clear_weight_cache() -> None:

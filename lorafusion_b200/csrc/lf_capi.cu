@@ -31,9 +31,12 @@ struct DeviceState {
 
 std::mutex g_mu;
 DeviceState g_dev[64];
-std::atomic<bool> g_cosched_enabled{true};  // process-wide switch (lf_set_co_scheduling)
+std::atomic<int> g_cosched_mode{1};  // process-wide switch (lf_set_co_scheduling): 0 off, 1 dedicated, 2 prologue
 
-bool cosched_allowed(const DeviceState* ds) { return !ds->no_cosched && g_cosched_enabled.load(); }
+bool cosched_allowed(const DeviceState* ds) { return !ds->no_cosched && g_cosched_mode.load() != 0; }
+// Shrink inside the GEMM launch: on CTA pairs the GEMM's round count leaves idle (default, when
+// there are at least four), or as every CTA's prologue (mode 2).
+bool cosched_prologue() { return g_cosched_mode.load() == 2; }
 EncodeTiledFn g_encode = nullptr;
 
 int elem_bytes(int dtype) { return dtype == LF_F32 ? 4 : 2; }
@@ -258,18 +261,18 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
     // Shrink and expand requested together: run the shrink on CTA pairs the GEMM's round count
     // leaves idle, inside the same launch, when there are enough of them.
     const bool separate = (stages & LF_STAGE_SEPARATE) != 0;
-    const int spare = (!single && !separate && do_shrink && lora && cosched_allowed(ds))
-                          ? pair_spare_pairs(T, N, ds->num_sms, info->n_shrink_units)
-                          : 0;
+    const bool fuse = !single && !separate && do_shrink && lora && cosched_allowed(ds);
+    const int spare = fuse && !cosched_prologue() ? pair_spare_pairs(T, N, ds->num_sms, info->n_shrink_units) : 0;
     // the K-split tail needs a cooperative launch too
     const PairTail tail = tail_scratch(workspace_dev, workspace_bytes, forward_min_workspace_bytes(info));
-    if (spare > 0) {
+    if (fuse && (spare > 0 || cosched_prologue())) {
       PairShrink sh{};
       sh.a_map = a_map;
       sh.s_ext = workspace_dev;
       sh.unit_ready = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace_dev) + sext_bytes(info));
       sh.gen = next_generation();
       sh.n_pairs = spare;
+      sh.prologue = cosched_prologue();
       e = tc_gemm_pair(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st, &sh, &tail);
       if (e == cudaSuccess) return LF_OK;
       // The cooperative launch was refused (e.g. other work holds SMs, or a profiler
@@ -315,7 +318,7 @@ extern "C" int lf_forward_launch_count(const lf_problem* prob, const lf_plan_inf
   if (device_state(&ds) != cudaSuccess) return -LF_ERR_CUDA;
   const bool tc = prob->dtype != LF_F32 && prob->K > 0 && prob->K % 8 == 0 && prob->N % 8 == 0;
   if (tc && info->n_segtiles > 0 && cosched_allowed(ds) &&
-      pair_spare_pairs(prob->T, prob->N, ds->num_sms, info->n_shrink_units) > 0)
+      (cosched_prologue() || pair_spare_pairs(prob->T, prob->N, ds->num_sms, info->n_shrink_units) > 0))
     return 1;
   return 2;
 }
@@ -329,11 +332,15 @@ extern "C" int lf_backward_launch_count(const lf_problem* prob, const lf_plan_in
   const bool lora = info->n_segtiles > 0 && info->n_slots > 0;
   if (!tc) return 5;
   if (!lora) return 1;
-  return (cosched_allowed(ds) && pair_spare_pairs(prob->T, prob->K, ds->num_sms, info->n_shrink_units) > 0) ? 2 : 4;
+  return (cosched_allowed(ds) &&
+          (cosched_prologue() || pair_spare_pairs(prob->T, prob->K, ds->num_sms, info->n_shrink_units) > 0))
+             ? 2
+             : 4;
 }
 
 extern "C" int lf_set_co_scheduling(int32_t enable) {
-  g_cosched_enabled.store(enable != 0);
+  if (enable < 0 || enable > 2) return LF_ERR_INVALID_ARG;
+  g_cosched_mode.store(enable);
   return LF_OK;
 }
 
@@ -406,14 +413,16 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
       // The shrinks inside the dX GEMM launch, on CTA pairs its round count leaves idle: job 1 =
       // S_b (g . B_i, needed by the dX tiles), job 2 = S_f (x . A_i^T, read by the dB gram) unless
       // the forward's is reused.
-      const int spare = cosched_allowed(ds) ? pair_spare_pairs(T, K, ds->num_sms, info->n_shrink_units) : 0;
-      if (spare > 0) {
+      const int spare =
+          cosched_allowed(ds) && !cosched_prologue() ? pair_spare_pairs(T, K, ds->num_sms, info->n_shrink_units) : 0;
+      if (cosched_allowed(ds) && (spare > 0 || cosched_prologue())) {
         PairShrink sh{};
         sh.a_map = bt_map;
         sh.s_ext = s_b;
         sh.unit_ready = reinterpret_cast<uint64_t*>(ws + 2 * sb);
         sh.gen = next_generation();
         sh.n_pairs = spare;
+        sh.prologue = cosched_prologue();
         sh.job2 = !reuse_sf;
         sh.p2_map = p_x;
         sh.a2_map = a_map;

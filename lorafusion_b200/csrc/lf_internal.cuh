@@ -77,14 +77,14 @@ struct PairShrink {
   void* s_ext;           // two K-half planes written by the launch, job 1
   uint64_t* unit_ready;  // [2*n_units] ready flags of job 1 (then [2*n_units] of job 2)
   uint64_t gen;          // value the flags take in this launch
-  int n_pairs;           // CTA pairs given to the shrink
+  int n_pairs;           // CTA pairs given to the shrink (dedicated mode)
+  bool prologue;         // instead: every CTA runs its share of the shrink before its GEMM tiles
   bool job2;             // second job present
   CUtensorMap p2_map;    // job 2 activations [T, K2] box (64, 128)
   CUtensorMap a2_map;    // job 2 slab [n_slots*r_pad, K2] box (64, r_pad)
   void* s_ext2;
   int K2;
 };
-// CTA pairs the pair GEMM can leave to a co-scheduled shrink without adding a round (0: none).
 // K-split tail of the pair GEMM (the last round of 256x256 tiles cut along K when it would
 // leave at least half of the CTA pairs idle): fp32 partial tiles and their release flags, in
 // caller scratch after the fixed workspace sections.  `slots` partial tiles fit there; `gen`
@@ -99,6 +99,7 @@ struct PairTail {
   int slots;
   uint64_t gen;
 };
+// CTA pairs the pair GEMM can leave to a co-scheduled shrink without adding a round (0: none).
 int pair_spare_pairs(int T, int Nout, int num_sms, int n_units);
 // `tail` (optional) enables the K-split tail; the launch is then cooperative.
 cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, int Nout, int Kred, bool lora,

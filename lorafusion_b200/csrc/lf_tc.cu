@@ -363,7 +363,11 @@ static_assert(kRoleStages * kRoleStageBytes <= kPairStages * (kPairABytes + kPai
 // more entries reads the rest from the table.
 constexpr int kPairEntPerLane = 6;
 constexpr int kPairEntBytes = 32 * kPairEntPerLane * 2 * 4;
-constexpr int kPairSmem = 1024 + kPairStages * (kPairABytes + kPairBBytes) + kPairOutBytes + 384 + kPairEntBytes;
+// barriers: the GEMM's (and a dedicated shrink role's) at +0, a shrink prologue's at +256
+constexpr int kPairBarBytes = 512;
+static_assert((2 * kPairBars + 4 + 2) * 8 + 8 <= 256 && 256 + (2 * kRoleStages + 6) * 8 <= kPairBarBytes,
+              "barrier area");
+constexpr int kPairSmem = 1024 + kPairStages * (kPairABytes + kPairBBytes) + kPairOutBytes + kPairBarBytes + kPairEntBytes;
 static_assert(kPairSmem <= 227 * 1024, "pair kernel shared memory");
 
 struct PairParams {
@@ -383,8 +387,10 @@ struct PairParams {
   uint32_t idesc_main, idesc_lora;
   uint32_t lora_layout, lora_sbo;
   // co-scheduled shrink: the first 2*n_shrink_pairs CTAs compute S_ext (P . A_slot^T) and publish
-  // one ready flag per shrink unit; 0 = S_ext was produced by an earlier launch
+  // one ready flag per shrink unit; 0 = S_ext was produced by an earlier launch ...
   int n_shrink_pairs;
+  // ... or, with shrink_prologue, every CTA runs its share of the shrink items first
+  int shrink_prologue;
   int ab_fmt;
   void* s_ext;
   uint64_t* unit_ready;  // one flag per (unit, K half) item
@@ -473,11 +479,13 @@ __device__ __forceinline__ bool wait_units_ready(const uint64_t* ready, int u0, 
   return true;
 }
 
-// Shrink role of the co-scheduled pair kernel, run by CTAs [0, 2*n_shrink_pairs): whole shrink
-// units (row tile, <= 64/r_pad segment tiles, full K) on single CTAs, S written straight from TMEM
-// (scaled, masked per segment, bf16/f16), then the unit's ready flag is released.  The epilogue
-// warps of CTA 0 also write the all-zero block before releasing unit 0.
-template <typename OutT>
+// Shrink role of the co-scheduled pair kernel, run by CTAs [0, 2*n_shrink_pairs) for the whole
+// launch, or (kPrologue) by every CTA before its GEMM tiles: items (job, unit = row tile and
+// <= 64/r_pad segment tiles, K half) on single CTAs, S written straight from TMEM (scaled, masked
+// per segment, bf16/f16), then the item's ready flag is released.  The epilogue warps of CTA 0
+// also write the all-zero block before releasing item 0.  In prologue mode the role keeps the
+// TMEM allocation permit (the GEMM allocates after it) and its barriers are its own.
+template <typename OutT, bool kPrologue>
 __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CUtensorMap& map_p,
                                                  const CUtensorMap& map_a, const CUtensorMap& map_p2,
                                                  const CUtensorMap& map_a2, uint8_t* sA, uint8_t* sB, uint64_t* full,
@@ -485,7 +493,7 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
                                                  uint64_t* pub, uint32_t* tmem_slot, volatile int* abort_flag) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Tables& tb = prm.tb;
-  const int me = static_cast<int>(blockIdx.x), n_me = 2 * prm.n_shrink_pairs;
+  const int me = static_cast<int>(blockIdx.x), n_me = kPrologue ? static_cast<int>(gridDim.x) : 2 * prm.n_shrink_pairs;
   const int r_pad = prm.r_pad;
   // item = (job, unit, K half): half h of a job covers its k-blocks [h*half, min(nkb, (h+1)*half))
   const int n_items = (prm.job2 ? 4 : 2) * tb.n_units;
@@ -514,11 +522,11 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
   if (warp == 1) {
     __syncwarp();
     tmem_alloc(tmem_slot, 128);
-    tmem_relinquish();
+    if (!kPrologue) tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
-  cluster_sync_all();
+  if (!kPrologue) cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -686,11 +694,12 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
 
   tc_fence_before();
   __syncthreads();
-  cluster_sync_all();
+  if (!kPrologue) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 128);
   }
+  if (kPrologue) __syncthreads();
 }
 
 template <bool kQMN, typename OutT>
@@ -713,14 +722,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* pub = drain + 1;  // shrink role: all epilogue warps finished writing a unit
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pub + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* pair_ent = reinterpret_cast<int*>(sOut + kPairOutBytes + 384);
+  // a shrink prologue's barriers: never re-initialized while its last arrivals may be in flight
+  uint64_t* rfull = reinterpret_cast<uint64_t*>(sOut + kPairOutBytes + 256);
+  uint64_t* rempty = rfull + kRoleStages;
+  uint64_t* rtfull = rempty + kRoleStages;
+  uint64_t* rtempty = rtfull + 2;
+  uint64_t* rdrain = rtempty + 2;
+  uint64_t* rpub = rdrain + 1;
+  int* pair_ent = reinterpret_cast<int*>(sOut + kPairOutBytes + kPairBarBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (static_cast<int>(blockIdx.x) < 2 * prm.n_shrink_pairs) {
-    pair_shrink_role<OutT>(prm, map_p, map_a, map_p2, map_a2, sA, sB, full, empty, tfull, tempty, drain, pub,
-                           tmem_slot, abort_flag);
+    pair_shrink_role<OutT, false>(prm, map_p, map_a, map_p2, map_a2, sA, sB, full, empty, tfull, tempty, drain, pub,
+                                  tmem_slot, abort_flag);
     return;
   }
+  if (prm.shrink_prologue && static_cast<int>(blockIdx.x) < (prm.job2 ? 4 : 2) * prm.tb.n_units)
+    pair_shrink_role<OutT, true>(prm, map_p, map_a, map_p2, map_a2, sA, sB, rfull, rempty, rtfull, rtempty, rdrain,
+                                 rpub, tmem_slot, abort_flag);
   const uint32_t crank = cluster_ctarank();  // 0: issues the MMAs
   const int pair = static_cast<int>(blockIdx.x >> 1) - prm.n_shrink_pairs;
   const int n_pairs = static_cast<int>(gridDim.x >> 1) - prm.n_shrink_pairs;
@@ -795,7 +814,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int it0 = 0, it1 = 0;
       uint64_t fl[9];
       if (lane == 0) {
-        if (lora && prm.n_shrink_pairs > 0) {
+        if (lora && (prm.n_shrink_pairs > 0 || prm.shrink_prologue)) {
           it0 = 2 * ld_early(tb.base + tb.off_tile_unit + 2 * mp);
           it1 = 2 * ld_early(tb.base + tb.off_tile_unit + min(2 * mp + 2, tb.n_tiles));
           fl[0] = ld_relaxed_u64(prm.unit_ready);
@@ -839,7 +858,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncwarp();
       if (lane == 0) {
-        if (prm.n_shrink_pairs > 0 && pe > pb) {  // S_ext of both row tiles (and the zero block) published?
+        if ((prm.n_shrink_pairs > 0 || prm.shrink_prologue) && pe > pb) {  // S_ext of both row tiles (and the zero block) published?
           bool seen = it1 - it0 <= 8;
 #pragma unroll
           for (int q = 0; q < 9; ++q) seen = seen && fl[q] == prm.gen;
@@ -1883,8 +1902,9 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
   const CUtensorMap* a_map = &maps.p;  // unused unless a shrink is co-scheduled
   const CUtensorMap* p2_map = &maps.p;
   const CUtensorMap* a2_map = &maps.p;
-  if (shrink != nullptr && shrink->n_pairs > 0) {
-    p.n_shrink_pairs = shrink->n_pairs;
+  if (shrink != nullptr && (shrink->n_pairs > 0 || shrink->prologue)) {
+    p.shrink_prologue = shrink->prologue ? 1 : 0;
+    p.n_shrink_pairs = shrink->prologue ? 0 : shrink->n_pairs;
     p.s_planes = 2;
     p.s_ext = shrink->s_ext;
     p.unit_ready = shrink->unit_ready;
@@ -1897,8 +1917,10 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
       p2_map = &shrink->p2_map;
       a2_map = &shrink->a2_map;
     }
-    const int rounds = (total + all_pairs - 1) / all_pairs;
-    gemm_pairs = (total + rounds - 1) / rounds;
+    if (!shrink->prologue) {  // the GEMM keeps its round count on the pairs the shrink leaves
+      const int rounds = (total + all_pairs - 1) / all_pairs;
+      gemm_pairs = (total + rounds - 1) / rounds;
+    }
   }
   if (tail != nullptr && tail->slots > 0) {
     // Cut the tail tiles along K when the last round is at most half full (or there are fewer
@@ -1915,7 +1937,7 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
       p.tail_parts = parts;
       p.tail_partial = tail->partial;
       p.tail_flag = tail->flags;
-      if (p.n_shrink_pairs == 0) p.gen = tail->gen;  // else the shrink's generation serves both
+      if (p.n_shrink_pairs == 0 && !p.shrink_prologue) p.gen = tail->gen;  // else the shrink's serves both
     }
   }
   cudaLaunchConfig_t cfg{};
@@ -1933,7 +1955,7 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
   attr[1].id = cudaLaunchAttributeCooperative;
   attr[1].val.cooperative = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = p.n_shrink_pairs > 0 || p.tail_parts > 1 ? 2 : 1;
+  cfg.numAttrs = p.n_shrink_pairs > 0 || p.shrink_prologue || p.tail_parts > 1 ? 2 : 1;
   cudaError_t e;
 #define LF_LAUNCH_PAIR(QMN, OT)                                                                  \
   e = ensure_smem(tc_gemm_pair_kernel<QMN, OT>, kPairSmem);                                     \

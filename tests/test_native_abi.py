@@ -152,3 +152,11 @@ def test_ops_raise_without_gpu_inputs():
         b200_ops.fused_lora_forward(x, torch.zeros(8, 8), {0: torch.zeros(2, 8)}, {0: torch.zeros(8, 2)}, ad, rt)
     with pytest.raises(ValueError, match="covers"):
         b200_ops.fused_lora_forward(torch.zeros(5, 8), torch.zeros(8, 8), {}, {}, ad, rt)
+
+
+def test_co_scheduling_switch_rejects_unknown_modes():
+    L = nat.lib()
+    assert L.lf_set_co_scheduling(3) == nat.LF_ERR_INVALID_ARG
+    assert L.lf_set_co_scheduling(-1) == nat.LF_ERR_INVALID_ARG
+    for mode in (0, 2, 1):  # ends on the default
+        assert L.lf_set_co_scheduling(mode) == 0

@@ -272,15 +272,17 @@ def test_gemm_tilings_match_oracle(single_cta):
     _check(y0, case["x"] @ case["w"].T, BF16_TOL, "base GEMM only")
 
 
-@pytest.mark.parametrize("co_scheduled", [True, False], ids=["one_launch_shrinks", "separate_shrinks"])
-def test_co_scheduling_switch_matches_oracle(co_scheduled):
+@pytest.mark.parametrize("mode", ["prologue", "dedicated", "separate"],
+                         ids=["shrink_prologue", "shrink_pairs", "separate_shrinks"])
+def test_co_scheduling_switch_matches_oracle(mode):
     """Forward and backward with the routed shrinks inside the GEMM launch (forward 1 launch,
-    backward 2) and as launches of their own (2 and 3, S_f taken from the forward); both match
-    the oracle."""
+    backward 2), either as every CTA's prologue or on dedicated CTA pairs, and as launches of
+    their own (2 and 3, S_f taken from the forward); all match the oracle."""
     ops = _ops()
     routes = _routes_from_sizes([300, 5, 1, 94, 200, 100, 324], [0, 1, 2, 3, 0, 1, 2])  # 1024 rows
     case = _random_case(23, 1024, 512, 768, routes, {0: 16, 1: 8, 2: 32, 3: 64}, torch.bfloat16)
-    ops.use_cooperative_launch(co_scheduled)
+    co_scheduled = mode != "separate"
+    ops.use_cooperative_launch(co_scheduled, shrink_prologue=mode == "prologue")
     try:
         x, w, a, b, ad, routing, g = _to_torch(case, torch.bfloat16)
         y = ops.fused_lora_forward(x, w, a, b, ad, routing)
