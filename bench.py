@@ -479,8 +479,9 @@ def run_ours(args):
                              "cublas_tflops": 2.0 * T * K * N / (cublas_ms / 1e3) / 1e12},
             "e2e": {"value": pr["global_T"] / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": T * K * 2, "d2h_bytes_per_step": T * N * 2,
-                    "path": "b200_ops.fused_lora_forward_host: pinned host x/y, 1024-row chunks, copies in "
-                            "both directions overlapped with the fused forward"},
+                    "path": "b200_ops.fused_lora_forward_host -> lf_forward_host: pinned host x/y, 1024-row "
+                            "chunks enqueued by one native call, copies in both directions overlapped with the "
+                            "fused forward"},
             "fwd_bwd": fwd_bwd,
             "coordinator": coordinator,
             "cpu_baseline": cpu,

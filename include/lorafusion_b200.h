@@ -228,6 +228,34 @@ LF_API int lf_backward_sf(const lf_problem* prob, const lf_plan_info* info, cons
                           lf_stream_t stream);
 
 /*
+ * Forward of a batch that lives in host memory, streamed in row chunks: chunk i is copied to
+ * x_dev on `h2d_stream` while chunk i-1 is computed on `stream` and chunk i-2 is copied back to
+ * y_host on `d2h_stream`, so both PCIe directions and the GPU work overlap.  All copies and
+ * launches are enqueued by this one call (no per-chunk host round trips); `stream` waits for
+ * the last copy back, so synchronizing `stream` makes y_host valid.
+ *  - prob: the whole batch (T rows, K, N, dtype, w_dev and the adapter slabs); prob->x_dev is
+ *    ignored.  x_host [T,K] and y_host [T,N] should be pinned; x_dev [T,K] and y_dev [T,N] are
+ *    device buffers the call fills.
+ *  - chunks: rows [row0, row0 + rows) in order, each with tables of its own routes (rows rebased
+ *    to the chunk) built over the whole batch's slots, so every chunk reads the same slabs.
+ *  - workspace: at least the largest lf_forward_workspace_bytes of the chunks' tables; chunks
+ *    run one after another on `stream` and share it.
+ *  - The copies start after the work already enqueued on `stream` (they wait for it).
+ * Returns the first failing chunk's status (nothing after it is enqueued).  No counterpart in
+ * the reference (its ops take device tensors).
+ */
+typedef struct lf_host_chunk {
+  int32_t row0;
+  int32_t rows;
+  const lf_plan_info* info;
+  const int32_t* table_dev;
+} lf_host_chunk;
+LF_API int lf_forward_host(const lf_problem* prob, const lf_host_chunk* chunks, int32_t n_chunks,
+                           const void* x_host, void* y_host, void* x_dev, void* y_dev, void* workspace_dev,
+                           size_t workspace_bytes, lf_stream_t stream, lf_stream_t h2d_stream,
+                           lf_stream_t d2h_stream);
+
+/*
  * Forward for callers that cannot allocate device memory: same inputs, output and result as
  * lf_forward, but no workspace argument.  The scratch lives in a fixed array of
  * LF_NOALLOC_SCRATCH_BYTES that the library declares in device memory; every GPU that loads the

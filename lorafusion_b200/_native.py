@@ -55,6 +55,11 @@ class RowRun(ctypes.Structure):
                 ("dst_stride", ctypes.c_int64), ("rows", ctypes.c_int64), ("row0", ctypes.c_int64)]
 
 
+class HostChunk(ctypes.Structure):
+    _fields_ = [("row0", ctypes.c_int32), ("rows", ctypes.c_int32), ("info", ctypes.POINTER(PlanInfo)),
+                ("table_dev", ctypes.c_void_p)]
+
+
 _lock = threading.Lock()
 _lib: ctypes.CDLL | None = None
 
@@ -74,6 +79,9 @@ def _declare(L: ctypes.CDLL) -> None:
                                    _c_p, _c_p]
     L.lf_pack_adapters.restype = ctypes.c_int
     L.lf_copy_rows.argtypes = [_c_p, _c_i32, ctypes.c_int64, ctypes.c_int64, _c_p]
+    L.lf_forward_host.argtypes = [P(Problem), P(HostChunk), _c_i32, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_size_t,
+                                  _c_p, _c_p, _c_p]
+    L.lf_forward_host.restype = ctypes.c_int
     L.lf_copy_rows.restype = ctypes.c_int
     L.lf_greedy_pack.argtypes = [P(_c_i32), P(_c_i32), _c_i32, _c_i32, _c_i32, P(_c_i32), P(_c_i32), P(_c_i32),
                                  P(_c_i32), P(_c_i32)]

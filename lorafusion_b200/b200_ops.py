@@ -85,7 +85,7 @@ class _Routes:
     """A routing object's routes, validated for ``valid_rows`` rows, as the arrays the table
     builder takes, plus the routing plans built from them."""
 
-    __slots__ = ("ref", "snapshot", "valid_rows", "starts", "ends", "route_slot", "slots", "plans")
+    __slots__ = ("ref", "snapshot", "valid_rows", "starts", "ends", "route_slot", "slots", "plans", "chunk_plans")
 
     def __init__(self, routing, routes, total_rows):
         self.ref = weakref.ref(routing)
@@ -99,6 +99,7 @@ class _Routes:
                                       dtype=np.int32, count=n)
         self.slots = tuple(slot_of)
         self.plans: list = []
+        self.chunk_plans: list = []
 
 
 def _routes(routing, total_rows: int) -> _Routes:
@@ -519,75 +520,123 @@ def _grad_dicts(plan: _Plan, ga_flat, gb_flat, K: int, N: int):
 
 
 # ----------------------------------------------------------------------------- host-resident batches
-_CHUNK_CACHE: dict[tuple, tuple] = {}
 _SIDE_STREAMS: dict[int, tuple] = {}
 
 
-def _chunk_routings(routing, total_rows: int, chunk_rows: int):
-    """Routes of each row chunk [c0, c1), rebased to the chunk (cached per routing object so the
-    chunks' routing tables are built once)."""
-    key = (id(routing), total_rows, chunk_rows)
-    hit = _CHUNK_CACHE.get(key)
-    if hit is not None and hit[0]() is routing:
-        return hit[1]
-    from lorafusion_b200.config import TileRoute, TileRoutingConfig
-    chunks = []
-    for c0 in range(0, total_rows, chunk_rows):
-        c1 = min(total_rows, c0 + chunk_rows)
-        routes = [TileRoute(max(r.row_start, c0) - c0, min(r.row_end, c1) - c0, r.adapter_id)
-                  for r in routing.routes if r.row_start < c1 and r.row_end > c0]
-        chunks.append((c0, c1, TileRoutingConfig(tile_size=routing.tile_size, routes=routes)))
-    if len(_CHUNK_CACHE) >= _CACHE_MAX:
-        _CHUNK_CACHE.clear()
-    _CHUNK_CACHE[key] = (weakref.ref(routing), chunks)
-    return chunks
+class _ChunkPlans:
+    """Row chunks of one routing for the host-streamed forward: per chunk, tables of its routes
+    (rebased to the chunk) over the whole batch's slots, as the C ABI's chunk array."""
+
+    __slots__ = ("array", "n", "infos", "tables", "ws_bytes", "launches")
+
+    def __init__(self, rts: _Routes, ranks, scales, total_rows: int, chunk_rows: int, device, code: int):
+        L = nat.lib()
+        rk = np.asarray(ranks, dtype=np.int32)
+        sc = np.asarray(scales, dtype=np.float32)
+        n_slots = len(rts.slots)
+        i32p = ctypes.POINTER(ctypes.c_int32)
+        bounds = list(range(0, total_rows, chunk_rows))
+        self.n = len(bounds)
+        self.array = (nat.HostChunk * max(self.n, 1))()
+        self.infos, self.tables, self.ws_bytes, self.launches = [], [], 256, 0
+        for i, c0 in enumerate(bounds):
+            c1 = min(total_rows, c0 + chunk_rows)
+            sel = (rts.starts < c1) & (rts.ends > c0)
+            starts = np.ascontiguousarray(np.maximum(rts.starts[sel], c0) - c0, dtype=np.int32)
+            ends = np.ascontiguousarray(np.minimum(rts.ends[sel], c1) - c0, dtype=np.int32)
+            rslot = np.ascontiguousarray(rts.route_slot[sel], dtype=np.int32)
+            cap = L.lf_plan_table_words(len(starts), c1 - c0, n_slots)
+            if cap < 0:
+                raise ValueError("routing too large for int32 tables")
+            table = torch.empty(max(cap, 1), dtype=torch.int32, pin_memory=True)
+            info = nat.PlanInfo()
+            rc = L.lf_plan_tables(starts.ctypes.data_as(i32p), ends.ctypes.data_as(i32p), rslot.ctypes.data_as(i32p),
+                                  len(starts), c1 - c0, rk.ctypes.data_as(i32p),
+                                  sc.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n_slots,
+                                  ctypes.cast(table.data_ptr(), i32p), cap, ctypes.byref(info))
+            nat.check(rc, "lf_plan_tables")
+            table_dev = table[: max(info.table_words, 1)].to(device, non_blocking=True)
+            self.infos.append(info)
+            self.tables.append(table_dev)
+            self.array[i].row0, self.array[i].rows = c0, c1 - c0
+            self.array[i].info = ctypes.pointer(info)
+            self.array[i].table_dev = table_dev.data_ptr()
+            self.ws_bytes = max(self.ws_bytes, int(L.lf_forward_workspace_bytes(ctypes.byref(info), code)))
+
+
+def _chunk_plans(rts: _Routes, aset: _AdapterSet, total_rows: int, chunk_rows: int, device, code: int) -> _ChunkPlans:
+    key = (chunk_rows, total_rows, aset.ranks, aset.scales, device, code)
+    for k, v in rts.chunk_plans:
+        if k == key:
+            return v
+    plans = _ChunkPlans(rts, aset.ranks, aset.scales, total_rows, chunk_rows, device, code)
+    rts.chunk_plans.insert(0, (key, plans))
+    del rts.chunk_plans[4:]
+    return plans
 
 
 def fused_lora_forward_host(x_host, base_weight, lora_a, lora_b, adapters, routing, out=None,
                             chunk_rows: int = 1024):
     """``fused_lora_forward`` of a batch that lives in host memory; the result lands in host memory.
 
-    The rows travel in chunks of ``chunk_rows`` (a multiple of 256): chunk i is copied to the GPU
-    on one stream while chunk i-1 is computed on the caller's current stream and chunk i-2 is
-    copied back on a third, so both PCIe directions and the GPU work overlap.  Each output row
-    depends only on its own input row, and chunks start on the 128-row tile grid, so the result
-    equals one ``fused_lora_forward`` over the whole batch (bit for bit whenever the chunks and the
-    whole batch run the routed shrink the same way: both co-scheduled, or both as separate
-    launches).  ``x_host`` should be pinned (``pin_memory()``); ``out`` (pinned,
+    One native call (``lf_forward_host``) enqueues everything: the rows travel in chunks of
+    ``chunk_rows`` (a multiple of 256); chunk i is copied to the GPU on one stream while chunk
+    i-1 is computed on the caller's current stream and chunk i-2 is copied back on a third, so
+    both PCIe directions and the GPU work overlap.  Each output row depends only on its own input
+    row, chunks start on the 128-row tile grid and their tables use the whole batch's slots, so
+    the result equals one ``fused_lora_forward`` over the whole batch (bit for bit whenever the
+    chunks and the whole batch run the routed shrink the same way: both co-scheduled, or both as
+    separate launches).  ``x_host`` should be pinned (``pin_memory()``); ``out`` (pinned,
     ``[T, N]``, x's dtype) is allocated when omitted.  The copies back are enqueued, not waited
     for: synchronize the current stream before reading the result.  No counterpart in the
     reference (its ops take device tensors).
     """
-    _routes(routing, x_host.shape[0])
+    global _last_launches
+    rts = _routes(routing, x_host.shape[0])
     if x_host.is_cuda or not base_weight.is_cuda:
         raise ValueError("x_host must be a host tensor and base_weight a CUDA tensor")
     if chunk_rows <= 0 or chunk_rows % 256:
         raise ValueError("chunk_rows must be a positive multiple of 256")
+    if x_host.dim() != 2 or x_host.dtype not in _DTYPE_CODE:
+        raise ValueError(f"x_host must be a 2-D float32/bfloat16/float16 tensor, got {tuple(x_host.shape)} "
+                         f"{x_host.dtype}")
     device = base_weight.device
     T, K = x_host.shape
     N = base_weight.shape[0]
-    y_host = out if out is not None else torch.empty((T, N), dtype=x_host.dtype, pin_memory=True)
-    if y_host.shape != (T, N) or y_host.dtype != x_host.dtype or y_host.is_cuda:
-        raise ValueError("out must be a host tensor [T, N] of x's dtype")
+    if base_weight.dim() != 2 or base_weight.shape[1] != K:
+        raise ValueError(f"base_weight {tuple(base_weight.shape)} does not match x {tuple(x_host.shape)}")
+    dtype = x_host.dtype
+    y_host = out if out is not None else torch.empty((T, N), dtype=dtype, pin_memory=True)
+    if y_host.shape != (T, N) or y_host.dtype != dtype or y_host.is_cuda or not y_host.is_contiguous():
+        raise ValueError("out must be a contiguous host tensor [T, N] of x's dtype")
+    _last_launches = 0
     if T == 0:
         return y_host
+    if not x_host.is_contiguous():
+        x_host = x_host.contiguous()
+    code = _DTYPE_CODE[dtype]
+    aset = _adapters(rts, lora_a, lora_b, adapters)
+    w = _weight(base_weight, dtype, device)
+    plan = _plan(rts, aset, T, device)
+    packs = _pack(plan, aset, dtype, K, N, device, backward=False)
+    chunks = _chunk_plans(rts, aset, T, chunk_rows, device, code)
+    x_dev = torch.empty((T, K), dtype=dtype, device=device)
+    y_dev = torch.empty((T, N), dtype=dtype, device=device)
+    ws = torch.empty(chunks.ws_bytes, dtype=torch.uint8, device=device)
+    prob = _problem(code, T, K, N, x_dev, w, packs)
     compute = torch.cuda.current_stream(device)
     idx = device.index if device.index is not None else torch.cuda.current_device()
     if idx not in _SIDE_STREAMS:
         _SIDE_STREAMS[idx] = (torch.cuda.Stream(device), torch.cuda.Stream(device))
     s_in, s_out = _SIDE_STREAMS[idx]
-    x_dev = torch.empty((T, K), dtype=x_host.dtype, device=device)
-    s_in.wait_stream(compute)
-    s_out.wait_stream(compute)
-    for c0, c1, rt in _chunk_routings(routing, T, chunk_rows):
-        with torch.cuda.stream(s_in):
-            x_dev[c0:c1].copy_(x_host[c0:c1], non_blocking=True)
-        compute.wait_stream(s_in)
-        y_c = fused_lora_forward(x_dev[c0:c1], base_weight, lora_a, lora_b, adapters, rt)
-        s_out.wait_stream(compute)
-        with torch.cuda.stream(s_out):
-            y_host[c0:c1].copy_(y_c, non_blocking=True)
-        y_c.record_stream(s_out)
-    x_dev.record_stream(s_in)
-    compute.wait_stream(s_out)
+    L = nat.lib()
+    rc = L.lf_forward_host(ctypes.byref(prob), chunks.array, chunks.n, x_host.data_ptr(), y_host.data_ptr(),
+                           x_dev.data_ptr(), y_dev.data_ptr(), ws.data_ptr(), ws.numel(), compute.cuda_stream,
+                           s_in.cuda_stream, s_out.cuda_stream)
+    nat.check(rc, "lf_forward_host")
+    # the current stream waits for the last copy back, so the allocator may reuse these after it
+    pc = nat.Problem.from_buffer_copy(prob)
+    for info in chunks.infos:
+        pc.T = info.total_rows
+        _last_launches += int(L.lf_forward_launch_count(ctypes.byref(pc), ctypes.byref(info)))
     return y_host

@@ -6,8 +6,8 @@
 #include <atomic>
 #include <chrono>
 #include <cstring>
-#include <atomic>
 #include <mutex>
+#include <vector>
 
 #include "lf_internal.cuh"
 
@@ -27,6 +27,8 @@ struct DeviceState {
   int num_sms = 0;
   int* status = nullptr;      // address of g_device_status on this device
   bool no_cosched = false;    // the co-scheduled (cooperative) launch was refused here once
+  std::vector<cudaEvent_t> events;  // lf_forward_host's stream-ordering events (grown on demand)
+  std::mutex ev_mu;
 };
 
 std::mutex g_mu;
@@ -341,6 +343,64 @@ extern "C" int lf_backward_launch_count(const lf_problem* prob, const lf_plan_in
 extern "C" int lf_set_co_scheduling(int32_t enable) {
   if (enable < 0 || enable > 2) return LF_ERR_INVALID_ARG;
   g_cosched_mode.store(enable);
+  return LF_OK;
+}
+
+extern "C" int lf_forward_host(const lf_problem* prob, const lf_host_chunk* chunks, int32_t n_chunks,
+                               const void* x_host, void* y_host, void* x_dev, void* y_dev, void* workspace_dev,
+                               size_t workspace_bytes, lf_stream_t stream, lf_stream_t h2d_stream,
+                               lf_stream_t d2h_stream) {
+  if (!prob || n_chunks < 0 || (n_chunks > 0 && (!chunks || !x_host || !y_host || !x_dev || !y_dev)))
+    return LF_ERR_INVALID_ARG;
+  if (prob->dtype != LF_F32 && prob->dtype != LF_BF16 && prob->dtype != LF_F16) return LF_ERR_INVALID_ARG;
+  const size_t es = static_cast<size_t>(elem_bytes(prob->dtype));
+  int end = 0;
+  for (int32_t c = 0; c < n_chunks; ++c) {
+    const lf_host_chunk& ch = chunks[c];
+    if (ch.row0 != end || ch.rows < 0 || !ch.info || ch.info->total_rows != ch.rows) return LF_ERR_INVALID_ARG;
+    end += ch.rows;
+  }
+  if (end != prob->T) return LF_ERR_INVALID_ARG;
+  if (n_chunks == 0) return LF_OK;
+  DeviceState* ds = nullptr;
+  if (device_state(&ds) != cudaSuccess) return LF_ERR_CUDA;
+  const size_t n_ev = 2 * static_cast<size_t>(n_chunks) + 2;
+  std::lock_guard<std::mutex> lk(ds->ev_mu);  // one enqueue at a time per device shares the events
+  while (ds->events.size() < n_ev) {
+    cudaEvent_t ev;
+    if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return LF_ERR_CUDA;
+    ds->events.push_back(ev);
+  }
+  cudaEvent_t* ev = ds->events.data();
+  cudaStream_t cs = static_cast<cudaStream_t>(stream);
+  cudaStream_t si = static_cast<cudaStream_t>(h2d_stream);
+  cudaStream_t so = static_cast<cudaStream_t>(d2h_stream);
+  // the copies come after the work already on `stream` (earlier readers of x_dev / y_dev)
+  if (cudaEventRecord(ev[0], cs) != cudaSuccess || cudaStreamWaitEvent(si, ev[0], 0) != cudaSuccess ||
+      cudaStreamWaitEvent(so, ev[0], 0) != cudaSuccess)
+    return LF_ERR_CUDA;
+  const char* xh = static_cast<const char*>(x_host);
+  char* yh = static_cast<char*>(y_host);
+  char* xd = static_cast<char*>(x_dev);
+  char* yd = static_cast<char*>(y_dev);
+  const size_t row_in = static_cast<size_t>(prob->K) * es, row_out = static_cast<size_t>(prob->N) * es;
+  for (int32_t c = 0; c < n_chunks; ++c) {
+    const lf_host_chunk& ch = chunks[c];
+    const size_t r0 = static_cast<size_t>(ch.row0), nr = static_cast<size_t>(ch.rows);
+    cudaEvent_t ev_in = ev[2 + 2 * c], ev_out = ev[3 + 2 * c];
+    if (cudaMemcpyAsync(xd + r0 * row_in, xh + r0 * row_in, nr * row_in, cudaMemcpyHostToDevice, si) != cudaSuccess ||
+        cudaEventRecord(ev_in, si) != cudaSuccess || cudaStreamWaitEvent(cs, ev_in, 0) != cudaSuccess)
+      return LF_ERR_CUDA;
+    lf_problem pc = *prob;
+    pc.T = ch.rows;
+    pc.x_dev = xd + r0 * row_in;
+    const int rc = lf_forward(&pc, ch.info, ch.table_dev, yd + r0 * row_out, workspace_dev, workspace_bytes, stream);
+    if (rc != LF_OK) return rc;
+    if (cudaEventRecord(ev_out, cs) != cudaSuccess || cudaStreamWaitEvent(so, ev_out, 0) != cudaSuccess ||
+        cudaMemcpyAsync(yh + r0 * row_out, yd + r0 * row_out, nr * row_out, cudaMemcpyDeviceToHost, so) != cudaSuccess)
+      return LF_ERR_CUDA;
+  }
+  if (cudaEventRecord(ev[1], so) != cudaSuccess || cudaStreamWaitEvent(cs, ev[1], 0) != cudaSuccess) return LF_ERR_CUDA;
   return LF_OK;
 }
 
