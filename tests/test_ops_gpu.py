@@ -379,6 +379,21 @@ def test_host_forward_streams_chunks_bit_exact():
     _check(ref, case["y"], BF16_TOL, "forward")
 
 
+@pytest.mark.parametrize("dtype,K", [(torch.float32, 96), (torch.float16, 50)], ids=["f32", "f16_ragged_k"])
+def test_host_forward_other_dtypes_and_cuda_core_path(dtype, K):
+    """The host-streamed forward in float32 and with a K the tensor-core path cannot address
+    (CUDA-core kernels): chunk results equal the whole-batch forward and match the oracle."""
+    ops = _ops()
+    routes = _routes_from_sizes([300, 1, 400, 99], [1, 0, 1, 2])  # 800 rows
+    case = _random_case(37, 800, K, 136, routes, {0: 4, 1: 16, 2: 8}, dtype)
+    x, w, a, b, ad, routing, _ = _to_torch(case, dtype)
+    ref = ops.fused_lora_forward(x, w, a, b, ad, routing)
+    y = ops.fused_lora_forward_host(x.cpu().pin_memory(), w, a, b, ad, routing, chunk_rows=256)
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(y, ref.cpu())
+    _check(y, case["y"], FP32_TOL if dtype == torch.float32 else BF16_TOL, "host forward")
+
+
 def test_backward_reuses_forward_s_only_for_unchanged_inputs():
     """The backward takes S_f = s x A^T from a forward on the very same x and A (fewer launches,
     same gradients as recomputing it) and recomputes it once x has changed in place."""
