@@ -338,6 +338,14 @@ LF_API const char* lf_status_string(int status);
 /* Build identification: "lorafusion_b200 <version> sm_100a". */
 LF_API const char* lf_version(void);
 
+/*
+ * Release what the library itself holds on every device: lf_forward_host's stream-ordering
+ * events.  Work already enqueued is unaffected (a destroyed event that a stream still waits on
+ * is freed when it completes); later calls recreate what they need.  The caller owns every other
+ * buffer.  Returns LF_OK.
+ */
+LF_API int lf_release(void);
+
 #ifdef __cplusplus
 }
 #endif

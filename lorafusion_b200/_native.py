@@ -82,6 +82,8 @@ def _declare(L: ctypes.CDLL) -> None:
     L.lf_forward_host.argtypes = [P(Problem), P(HostChunk), _c_i32, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_size_t,
                                   _c_p, _c_p, _c_p]
     L.lf_forward_host.restype = ctypes.c_int
+    L.lf_release.argtypes = []
+    L.lf_release.restype = ctypes.c_int
     L.lf_copy_rows.restype = ctypes.c_int
     L.lf_greedy_pack.argtypes = [P(_c_i32), P(_c_i32), _c_i32, _c_i32, _c_i32, P(_c_i32), P(_c_i32), P(_c_i32),
                                  P(_c_i32), P(_c_i32)]

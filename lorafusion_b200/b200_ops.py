@@ -34,7 +34,7 @@ from lorafusion_b200 import _native as nat
 _DTYPE_CODE = {torch.float32: nat.LF_F32, torch.bfloat16: nat.LF_BF16, torch.float16: nat.LF_F16}
 
 __all__ = ["fused_lora_forward", "fused_lora_backward", "fused_lora_forward_host", "prepare_forward",
-           "PreparedForward", "clear_weight_cache", "last_launch_count", "use_cooperative_launch"]
+           "PreparedForward", "clear_weight_cache", "release", "last_launch_count", "use_cooperative_launch"]
 
 
 # --------------------------------------------------------------------------- caches
@@ -74,6 +74,14 @@ def clear_weight_cache() -> None:
     _PLAN_BY_CONTENT.clear()
     _SAVED_SF.clear()
     _WEIGHT_CACHE.clear()
+
+
+def release() -> None:
+    """Drop every host cache (``clear_weight_cache``) and what the library holds on the devices
+    (``lf_release``: the host-streamed forward's events); later calls rebuild what they need."""
+    clear_weight_cache()
+    _SIDE_STREAMS.clear()
+    nat.check(nat.lib().lf_release(), "lf_release")
 
 
 def last_launch_count() -> int:

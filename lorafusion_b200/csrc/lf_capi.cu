@@ -346,6 +346,15 @@ extern "C" int lf_set_co_scheduling(int32_t enable) {
   return LF_OK;
 }
 
+extern "C" int lf_release(void) {
+  for (DeviceState& d : g_dev) {
+    std::lock_guard<std::mutex> lk(d.ev_mu);
+    for (cudaEvent_t ev : d.events) (void)cudaEventDestroy(ev);
+    d.events.clear();
+  }
+  return LF_OK;
+}
+
 extern "C" int lf_forward_host(const lf_problem* prob, const lf_host_chunk* chunks, int32_t n_chunks,
                                const void* x_host, void* y_host, void* x_dev, void* y_dev, void* workspace_dev,
                                size_t workspace_bytes, lf_stream_t stream, lf_stream_t h2d_stream,

@@ -160,3 +160,10 @@ def test_co_scheduling_switch_rejects_unknown_modes():
     assert L.lf_set_co_scheduling(-1) == nat.LF_ERR_INVALID_ARG
     for mode in (0, 2, 1):  # ends on the default
         assert L.lf_set_co_scheduling(mode) == 0
+
+
+def test_release_holds_nothing_without_gpu_work():
+    from lorafusion_b200 import b200_ops
+    assert nat.lib().lf_release() == 0
+    b200_ops.release()  # host caches and library state; safe to repeat
+    assert nat.lib().lf_release() == 0
