@@ -167,3 +167,32 @@ def test_release_holds_nothing_without_gpu_work():
     assert nat.lib().lf_release() == 0
     b200_ops.release()  # host caches and library state; safe to repeat
     assert nat.lib().lf_release() == 0
+
+
+def test_host_streamed_forward_rejects_bad_chunk_lists():
+    """lf_forward_host checks its chunk list before touching the GPU: chunks must follow each other
+    from row 0, match their tables' row counts and cover the batch exactly."""
+    L = nat.lib()
+    rc0, info_a, _ = _tables([(0, 256, 0)], 256, [16], [2.0])
+    rc1, info_b, _ = _tables([(0, 44, 0)], 44, [16], [2.0])
+    assert rc0 == 0 and rc1 == 0
+    prob = nat.Problem()
+    prob.dtype, prob.T, prob.K, prob.N = nat.LF_BF16, 300, 64, 64
+    chunks = (nat.HostChunk * 2)()
+    chunks[0].row0, chunks[0].rows, chunks[0].info = 0, 256, ctypes.pointer(info_a)
+    chunks[1].row0, chunks[1].rows, chunks[1].info = 256, 44, ctypes.pointer(info_b)
+    buf = ctypes.create_string_buffer(64)
+    p = ctypes.cast(buf, ctypes.c_void_p)
+
+    def call(n, T=300):
+        prob.T = T
+        return L.lf_forward_host(ctypes.byref(prob), chunks, n, p, p, p, p, p, 64, None, None, None)
+
+    assert call(2, T=301) == nat.LF_ERR_INVALID_ARG  # rows do not add up to T
+    assert call(1) == nat.LF_ERR_INVALID_ARG          # batch not covered
+    chunks[1].row0 = 200
+    assert call(2) == nat.LF_ERR_INVALID_ARG          # overlapping chunks
+    chunks[1].row0, chunks[1].rows = 256, 45
+    assert call(2) == nat.LF_ERR_INVALID_ARG          # chunk rows differ from its tables'
+    assert call(0, T=0) == 0                          # nothing to do
+    assert L.lf_forward_host(None, chunks, 0, p, p, p, p, p, 64, None, None, None) == nat.LF_ERR_INVALID_ARG
