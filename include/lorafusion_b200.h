@@ -124,7 +124,11 @@ typedef struct lf_problem {
 } lf_problem;
 
 /*
- * Workspace bytes the forward / backward use for this table and dtype.  About 20 MiB of it is
+ * Workspace bytes the forward / backward use for this table and dtype.  The workspace starts with
+ * S_ext, the routed shrink's output per segment tile: on the tensor-core path four bf16/f16 planes
+ * of [n_segtiles + 1][128][r_pad] (each value v stored as hi = round(v) and lo = round(v - hi), for
+ * one or two K-half partial products: planes [hi..., lo...]), on the float32 / CUDA-core path one
+ * f64 buffer of the same shape.  About 20 MiB of it is
  * the scratch of the GEMM's K-split tail (fp32 partial tiles of a last round cut along K);
  * a smaller workspace that still holds the fixed sections is accepted, and the tail then
  * splits only as far as the partial tiles fit (not at all below one tile).
@@ -176,6 +180,28 @@ LF_API int lf_forward_stages(const lf_problem* prob, const lf_plan_info* info, c
                              void* workspace_dev, size_t workspace_bytes, int32_t stages, lf_stream_t stream);
 
 /*
+ * The part of lf_forward_workspace_bytes that holds S_ext and the co-scheduling flags; the rest
+ * (lf_forward_workspace_bytes minus this) is the K-split tail's scratch, needed only while a
+ * forward runs.
+ */
+LF_API size_t lf_forward_fixed_workspace_bytes(const lf_plan_info* info, int32_t dtype);
+
+/*
+ * lf_forward with the K-split tail's scratch in a buffer of its own (`tail_dev`, `tail_bytes`:
+ * up to lf_forward_workspace_bytes - lf_forward_fixed_workspace_bytes; null/0 = take it from the
+ * workspace as lf_forward does), so a caller can keep the workspace, which then needs only
+ * lf_forward_fixed_workspace_bytes, for a later lf_backward_sf while the tail buffer is reused.
+ * Also reports, in *s_f_planes, the K-half planes of S_f = s_i x A_i^T the call left in the
+ * workspace: 2 when the shrink ran inside the GEMM launch, 1 when it ran as a launch of its own, 0
+ * when the workspace holds no tensor-core S_f (float32 / CUDA-core path, empty problem).  That
+ * value, taken from the call that filled the workspace, is what lf_backward_sf needs.  No
+ * counterpart in the reference (it recomputes x A_i^T in the backward).
+ */
+LF_API int lf_forward_sf(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, void* y_dev,
+                         void* workspace_dev, size_t workspace_bytes, void* tail_dev, size_t tail_bytes,
+                         int32_t* s_f_planes, lf_stream_t stream);
+
+/*
  * Kernel launches lf_forward makes for this problem on the current device: 1 when the routed
  * shrink runs on CTA pairs the fused GEMM's round count leaves idle (same launch), else 2.
  * Returns a negative lf_status on bad arguments.  No counterpart in the reference.
@@ -200,9 +226,18 @@ LF_API int lf_backward_launch_count(const lf_problem* prob, const lf_plan_info* 
  *   0  no cooperative launches: each routed shrink is an ordinary launch of its own and no tail
  *     is K-split.  For profilers and SM-partitioned GPUs, which refuse cooperative launches (a
  *     refused launch also turns co-scheduling off for that device by itself).
- * Other values return LF_ERR_INVALID_ARG.  No counterpart in the reference.
+ * Other values return LF_ERR_INVALID_ARG.  The default is 1, or 0 when a CUDA tool is injected
+ * into the process (CUDA_INJECTION64_PATH set, as Nsight Compute and compute-sanitizer do).
+ * No counterpart in the reference.
  */
 LF_API int lf_set_co_scheduling(int32_t enable);
+
+/*
+ * The process-wide co-scheduling mode (*mode, as lf_set_co_scheduling takes it) and, for the
+ * current device, the cudaError_t a refused cooperative launch returned (*refused_error; 0 while
+ * no launch was refused there).  No counterpart in the reference.
+ */
+LF_API int lf_get_co_scheduling(int32_t* mode, int32_t* refused_error);
 
 /*
  * Backward: grad_x [T,K]; grad_a = concatenated [r_s, K] blocks and grad_b = concatenated
@@ -216,16 +251,28 @@ LF_API int lf_backward(const lf_problem* prob, const lf_plan_info* info, const i
 
 /*
  * lf_backward with S_f = s_i x A_i^T taken from a forward instead of recomputed: `s_f_dev` is the
- * workspace a lf_forward / lf_forward_stages(SHRINK | EXPAND) call on the same x, adapters and
- * tables filled, holding `s_f_planes` planes (2 when that forward ran its shrink inside the GEMM
- * launch, i.e. lf_forward_launch_count returned 1; else 1).  The caller keeps that workspace
- * unchanged until this call's work is done.  bf16/f16 only: the float32 path recomputes S_f.
+ * workspace a lf_forward_sf call on the same x, adapters and tables filled, and `s_f_planes` the
+ * value that call reported (1 or 2 K-half planes, each stored as hi and lo).  The caller keeps
+ * that workspace unchanged until this call's work is done.  bf16/f16 only: the float32 path
+ * recomputes S_f.
  * Saves the backward's x . A^T shrink (reference: mock_ops.py:79-80 recomputes it per route).
  */
 LF_API int lf_backward_sf(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
                           const void* grad_out_dev, const void* s_f_dev, int32_t s_f_planes, void* grad_x_dev,
                           void* grad_a_dev, void* grad_b_dev, void* workspace_dev, size_t workspace_bytes,
                           lf_stream_t stream);
+
+/*
+ * lf_backward / lf_backward_sf with the dtype of grad_a and grad_b chosen: `grad_ab_dtype` is the
+ * problem's dtype or LF_F32 (float gradient blocks, summed in float before any rounding: what a
+ * multi-GPU caller all-reduces).  `s_f_dev` may be null (S_f recomputed; `s_f_planes` ignored).
+ * Replaces triton_ops.fused_lora_backward (lorafusion/ops/triton_ops.py:412-468), whose grads
+ * come back in the input dtype (:453-455); LF_F32 has no counterpart there.
+ */
+LF_API int lf_backward_ex(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
+                          const void* grad_out_dev, const void* s_f_dev, int32_t s_f_planes, int32_t grad_ab_dtype,
+                          void* grad_x_dev, void* grad_a_dev, void* grad_b_dev, void* workspace_dev,
+                          size_t workspace_bytes, lf_stream_t stream);
 
 /*
  * Forward of a batch that lives in host memory, streamed in row chunks: chunk i is copied to

@@ -101,6 +101,16 @@ def _declare(L: ctypes.CDLL) -> None:
     L.lf_backward_launch_count.restype = ctypes.c_int
     L.lf_set_co_scheduling.argtypes = [_c_i32]
     L.lf_set_co_scheduling.restype = ctypes.c_int
+    L.lf_get_co_scheduling.argtypes = [P(_c_i32), P(_c_i32)]
+    L.lf_get_co_scheduling.restype = ctypes.c_int
+    L.lf_forward_sf.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, ctypes.c_size_t, _c_p, ctypes.c_size_t,
+                                P(_c_i32), _c_p]
+    L.lf_forward_sf.restype = ctypes.c_int
+    L.lf_forward_fixed_workspace_bytes.argtypes = [P(PlanInfo), _c_i32]
+    L.lf_forward_fixed_workspace_bytes.restype = ctypes.c_size_t
+    L.lf_backward_ex.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_p, _c_p,
+                                 ctypes.c_size_t, _c_p]
+    L.lf_backward_ex.restype = ctypes.c_int
     L.lf_backward.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_size_t, _c_p]
     L.lf_backward.restype = ctypes.c_int
     L.lf_backward_sf.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_i32, _c_p, _c_p, _c_p, _c_p,
@@ -151,6 +161,14 @@ def check(code: int, what: str) -> None:
     if code in (LF_ERR_CUDA, LF_ERR_DEVICE):
         raise RuntimeError(msg)
     raise ValueError(msg)
+
+
+def co_scheduling() -> tuple[int, int]:
+    """(process-wide co-scheduling mode, cudaError_t of a refused cooperative launch on the current
+    device or 0)."""
+    mode, refused = _c_i32(0), _c_i32(0)
+    check(lib().lf_get_co_scheduling(ctypes.byref(mode), ctypes.byref(refused)), "lf_get_co_scheduling")
+    return int(mode.value), int(refused.value)
 
 
 def device_error() -> int:

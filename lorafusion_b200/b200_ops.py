@@ -8,9 +8,13 @@ runs it unchanged.  All arithmetic happens in the sm_100a library behind
 ``include/lorafusion_b200.h``; there is no CPU path and no fallback: CPU inputs
 raise ``ValueError`` and a missing library raises ``RuntimeError``.
 
-Per call, on the current CUDA stream:
-  forward   1 routed shrink + 1 fused base-GEMM/LoRA-expand launch
-  backward  2 routed shrinks + 1 fused dX launch + 2 segmented gram launches
+Per call, on the current CUDA stream (co-scheduled launches, the default on a B200):
+  forward   1 launch: routed shrink on spare CTA pairs + fused base GEMM / LoRA expand
+  backward  2 launches: fused dX GEMM (with the routed shrink g.B_i on spare CTA pairs),
+            then one segmented gram launch for dA and dB
+bf16/f16 problems whose K or N is not a multiple of 8, or whose buffers are not 16-byte
+aligned, cannot use the tensor-core (TMA) path and run on CUDA cores with a
+``CudaCorePathWarning``.
 
 Host work is cached the way ``triton_ops._prepare`` caches its weight copies
 (``triton_ops.py:114-145``): validated routes and routing tables per routing
@@ -24,6 +28,7 @@ of adapters stay ahead of the GPU.
 from __future__ import annotations
 
 import ctypes
+import warnings
 import weakref
 
 import numpy as np
@@ -34,7 +39,31 @@ from lorafusion_b200 import _native as nat
 _DTYPE_CODE = {torch.float32: nat.LF_F32, torch.bfloat16: nat.LF_BF16, torch.float16: nat.LF_F16}
 
 __all__ = ["fused_lora_forward", "fused_lora_backward", "fused_lora_forward_host", "prepare_forward",
-           "PreparedForward", "clear_weight_cache", "release", "last_launch_count", "use_cooperative_launch"]
+           "PreparedForward", "clear_weight_cache", "release", "last_launch_count", "use_cooperative_launch",
+           "CudaCorePathWarning"]
+
+
+class CudaCorePathWarning(UserWarning):
+    """A bf16/f16 problem the tensor-core path cannot address runs on the (much slower) CUDA cores."""
+
+
+_WARNED_SHAPES: set = set()
+
+
+def _warn_if_cuda_core(dtype, K: int, N: int, tensors) -> None:
+    """Warn once per (dtype, K, N) when a bf16/f16 call must run on CUDA cores: TMA needs K and N
+    multiples of 8 and every buffer 16-byte aligned (the same test the library makes)."""
+    if dtype == torch.float32:
+        return
+    ok = K > 0 and N > 0 and K % 8 == 0 and N % 8 == 0 and all(t.data_ptr() % 16 == 0 for t in tensors)
+    if ok:
+        return
+    key = (dtype, K, N)
+    if key not in _WARNED_SHAPES:
+        _WARNED_SHAPES.add(key)
+        warnings.warn(f"{dtype} problem with in_features={K}, out_features={N} runs on the CUDA-core path: the "
+                      "tensor-core path needs both to be multiples of 8 and 16-byte aligned buffers",
+                      CudaCorePathWarning, stacklevel=3)
 
 
 # --------------------------------------------------------------------------- caches
@@ -367,22 +396,31 @@ def fused_lora_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> tor
     y = torch.empty((T, N), dtype=dtype, device=device)
     if T == 0 or N == 0:
         return y
+    _warn_if_cuda_core(dtype, K, N, (x, w, y))
     L = nat.lib()
-    ws_bytes = L.lf_forward_workspace_bytes(ctypes.byref(plan.info), code)
-    ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=device)
+    info = ctypes.byref(plan.info)
+    # S_ext and flags in one buffer (kept for the backward), the K-split tail's scratch in another
+    # (back to the allocator's cache once the launch is enqueued)
+    fixed = int(L.lf_forward_fixed_workspace_bytes(info, code))
+    ws = torch.empty(max(fixed, 256), dtype=torch.uint8, device=device)
+    tail = torch.empty(max(int(L.lf_forward_workspace_bytes(info, code)) - fixed, 256), dtype=torch.uint8,
+                       device=device)
     prob = _problem(code, T, K, N, x, w, packs)
     stream = torch.cuda.current_stream(device).cuda_stream
-    rc = L.lf_forward(ctypes.byref(prob), ctypes.byref(plan.info), plan.table_dev.data_ptr(), y.data_ptr(),
-                      ws.data_ptr(), ws.numel(), stream)
-    nat.check(rc, "lf_forward")
-    _last_launches = int(L.lf_forward_launch_count(ctypes.byref(prob), ctypes.byref(plan.info)))
-    if dtype != torch.float32 and plan.info.n_segtiles > 0:
-        _save_sf(x_in, rts, plan, aset, ws, 2 if _last_launches == 1 else 1)
+    planes = ctypes.c_int32(0)
+    rc = L.lf_forward_sf(ctypes.byref(prob), info, plan.table_dev.data_ptr(), y.data_ptr(), ws.data_ptr(), ws.numel(),
+                         tail.data_ptr(), tail.numel(), ctypes.byref(planes), stream)
+    nat.check(rc, "lf_forward_sf")
+    # 2 K-half planes: shrink inside the GEMM launch (1 launch); 1: shrink launched on its own
+    _last_launches = {2: 1, 1: 2}.get(planes.value) or int(L.lf_forward_launch_count(ctypes.byref(prob), info))
+    if planes.value > 0 and plan.info.n_segtiles > 0:
+        _save_sf(x_in, rts, plan, aset, ws, planes.value)
     return y
 
 
 def _save_sf(x, rts, plan, aset, ws, planes: int) -> None:
-    """Remember this forward's workspace (its S_f) for a backward on the same inputs."""
+    """Remember this forward's S_f (the fixed part of its workspace: S_ext planes and flags, not
+    the K-split tail's scratch) for a backward on the same inputs."""
     while len(_SAVED_SF) >= _SAVED_MAX:
         _SAVED_SF.pop(next(iter(_SAVED_SF)))
     try:
@@ -450,12 +488,14 @@ def prepare_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> Prepar
     return PreparedForward(x, base_weight, lora_a, lora_b, adapters, routing)
 
 
-def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, routing):
+def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, routing, *, grad_dtype=None):
     """Return ``(grad_x, grad_lora_a, grad_lora_b)`` as ``mock_ops.fused_lora_backward``.
 
     mock_ops.py:51-95: the base weight is frozen (no gradient); the dicts hold
     one entry per adapter that owns a route, in order of first appearance,
     each summed over that adapter's routes; tensors are in ``x.dtype``.
+    ``grad_dtype=torch.float32`` (keyword only, no counterpart in the reference) returns the
+    adapter gradients in float32, unrounded, for a caller that sums them across GPUs first.
     """
     global _last_launches
     rts = _routes(routing, x.shape[0])
@@ -474,6 +514,9 @@ def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, rout
     if g.dtype != dtype:
         g = g.to(dtype)
     code = _DTYPE_CODE[dtype]
+    gdt = dtype if grad_dtype is None else grad_dtype
+    if gdt not in (dtype, torch.float32):
+        raise ValueError(f"grad_dtype must be None, x.dtype or torch.float32, got {grad_dtype}")
     aset = _adapters(rts, lora_a, lora_b, adapters)
     w = _weight(base_weight, dtype, device)
     plan = _plan(rts, aset, T, device)
@@ -481,25 +524,23 @@ def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, rout
     info = plan.info
     rtot = info.rank_total
     grad_x = torch.empty((T, K), dtype=dtype, device=device)
-    ga_flat = torch.empty(max(rtot * K, 1), dtype=dtype, device=device)
-    gb_flat = torch.empty(max(rtot * N, 1), dtype=dtype, device=device)
+    ga_flat = torch.empty(max(rtot * K, 1), dtype=gdt, device=device)
+    gb_flat = torch.empty(max(rtot * N, 1), dtype=gdt, device=device)
+    _warn_if_cuda_core(dtype, K, N, (x, w, g, grad_x))
     L = nat.lib()
     ws_bytes = L.lf_backward_workspace_bytes(ctypes.byref(info), code)
     ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=device)
     prob = _problem(code, T, K, N, x, w, packs)
     stream = torch.cuda.current_stream(device).cuda_stream
     saved = _saved_sf(x_in, rts, plan, aset) if dtype != torch.float32 else None
-    if saved is not None:  # the forward on these inputs left S_f: skip recomputing s x A^T
-        sf_ws, sf_planes = saved
-        rc = L.lf_backward_sf(ctypes.byref(prob), ctypes.byref(info), plan.table_dev.data_ptr(), g.data_ptr(),
-                              sf_ws.data_ptr(), sf_planes, grad_x.data_ptr(), ga_flat.data_ptr(), gb_flat.data_ptr(),
-                              ws.data_ptr(), ws.numel(), stream)
-        sf_ws.record_stream(torch.cuda.current_stream(device))
-    else:
-        rc = L.lf_backward(ctypes.byref(prob), ctypes.byref(info), plan.table_dev.data_ptr(), g.data_ptr(),
-                           grad_x.data_ptr(), ga_flat.data_ptr(), gb_flat.data_ptr(), ws.data_ptr(), ws.numel(),
-                           stream)
-    nat.check(rc, "lf_backward")
+    sf_ptr, sf_planes = (saved[0].data_ptr(), saved[1]) if saved is not None else (None, 0)
+    # S_f from the forward on these inputs, when there was one: no second s x A^T shrink
+    rc = L.lf_backward_ex(ctypes.byref(prob), ctypes.byref(info), plan.table_dev.data_ptr(), g.data_ptr(), sf_ptr,
+                          sf_planes, _DTYPE_CODE[gdt], grad_x.data_ptr(), ga_flat.data_ptr(), gb_flat.data_ptr(),
+                          ws.data_ptr(), ws.numel(), stream)
+    if saved is not None:
+        saved[0].record_stream(torch.cuda.current_stream(device))
+    nat.check(rc, "lf_backward_ex")
     n_launch = max(0, int(L.lf_backward_launch_count(ctypes.byref(prob), ctypes.byref(info))))
     _last_launches = n_launch - 1 if saved is not None and n_launch == 4 else n_launch
     return grad_x, *_grad_dicts(plan, ga_flat, gb_flat, K, N)

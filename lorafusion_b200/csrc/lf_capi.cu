@@ -5,6 +5,7 @@
 
 #include <atomic>
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -26,16 +27,35 @@ struct DeviceState {
   bool ready = false;
   int num_sms = 0;
   int* status = nullptr;      // address of g_device_status on this device
-  bool no_cosched = false;    // the co-scheduled (cooperative) launch was refused here once
+  std::atomic<bool> no_cosched{false};  // the co-scheduled (cooperative) launch was refused here once
+  std::atomic<int> refusal{0};          // the cudaError_t that refused launch returned
   std::vector<cudaEvent_t> events;  // lf_forward_host's stream-ordering events (grown on demand)
   std::mutex ev_mu;
 };
 
 std::mutex g_mu;
 DeviceState g_dev[64];
-std::atomic<int> g_cosched_mode{1};  // process-wide switch (lf_set_co_scheduling): 0 off, 1 dedicated, 2 prologue
 
-bool cosched_allowed(const DeviceState* ds) { return !ds->no_cosched && g_cosched_mode.load() != 0; }
+// A profiling or checking tool injected into the process (Nsight Compute, compute-sanitizer and
+// the other CUDA tools load through CUDA_INJECTION64_PATH) replays or serializes kernels and
+// refuses cooperative launches, so the default is then "no co-scheduled launches".
+int default_cosched_mode() {
+  const char* inj = std::getenv("CUDA_INJECTION64_PATH");
+  return (inj != nullptr && inj[0] != '\0') ? 0 : 1;
+}
+// process-wide switch (lf_set_co_scheduling): 0 off, 1 dedicated, 2 prologue
+std::atomic<int> g_cosched_mode{default_cosched_mode()};
+
+bool cosched_allowed(const DeviceState* ds) { return !ds->no_cosched.load() && g_cosched_mode.load() != 0; }
+
+// A cooperative launch that returned `e` ran nothing: clear the (non-sticky) launch error, keep
+// the code for lf_get_co_scheduling and use ordinary launches on this device from now on.
+void refuse_cosched(DeviceState* ds, cudaError_t e) {
+  (void)cudaGetLastError();
+  int expect = 0;
+  ds->refusal.compare_exchange_strong(expect, static_cast<int>(e));
+  ds->no_cosched.store(true);
+}
 // Shrink inside the GEMM launch: on CTA pairs the GEMM's round count leaves idle (default, when
 // there are at least four), or as every CTA's prologue (mode 2).
 bool cosched_prologue() { return g_cosched_mode.load() == 2; }
@@ -96,9 +116,15 @@ size_t segtile_elems(const lf_plan_info* info) {
   return static_cast<size_t>(info->n_segtiles + 1) * LF_TILE_ROWS * static_cast<size_t>(info->r_pad);
 }
 
-// one S_ext buffer, 256-byte multiple: f32 for the CUDA-core path, or two bf16/f16 planes (the
-// K-half partial products of the co-scheduled shrink) for the tensor-core path
-size_t sext_bytes(const lf_plan_info* info) { return (segtile_elems(info) * 4 + 255) & ~size_t(255); }
+// One S_ext buffer, 256-byte multiple: f64 for the CUDA-core path, or four bf16/f16 planes for
+// the tensor-core path.  A tensor-core shrink writes each value v as hi = round(v) in plane h and
+// lo = round(v - hi) in plane kh + h, where kh (1 or 2) counts its K-half partial products (two
+// when it runs inside the GEMM launch): planes [hi of each K half..., lo of each K half...].  The
+// LoRA expand reads the hi planes; the dA/dB grams read all 2*kh planes, so S enters the
+// gradient sums with about 16 significant bits instead of 8.
+size_t sext_bytes(const lf_plan_info* info) { return (segtile_elems(info) * 8 + 255) & ~size_t(255); }
+
+constexpr int kSextPlanes = 4;  // planes one tensor-core S_ext buffer holds
 
 size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
 
@@ -221,9 +247,14 @@ extern "C" int lf_pack_adapters(int32_t src_dtype, int32_t dst_dtype, const uint
                                  transpose, d0, d1, dst_dev, static_cast<cudaStream_t>(stream)));
 }
 
-extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
-                                 void* y_dev, void* workspace_dev, size_t workspace_bytes, int32_t stages,
-                                 lf_stream_t stream) {
+namespace {
+// The forward stages; *sf_planes (if given) receives the K-half planes of S_f the shrink left in
+// the workspace (2 when it ran inside the GEMM launch, 1 as a launch of its own, 0 without a
+// tensor-core shrink), the value lf_backward_sf needs.
+int forward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, void* y_dev,
+                 void* workspace_dev, size_t workspace_bytes, void* tail_dev, size_t tail_bytes, int32_t stages,
+                 lf_stream_t stream, int32_t* sf_planes) {
+  if (sf_planes) *sf_planes = 0;
   int rc = check_problem(prob, info, table_dev);
   if (rc != LF_OK) return rc;
   if (stages <= 0 || stages > 31 || ((stages & LF_STAGE_EXPAND) && (stages & LF_STAGE_BASE))) return LF_ERR_INVALID_ARG;
@@ -249,7 +280,7 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
     TcMaps maps;
     CUtensorMap a_map;
     const size_t es = 2;
-    const uint64_t s_rows = 2 * static_cast<uint64_t>(info->n_segtiles + 1) * LF_TILE_ROWS;  // two planes
+    const uint64_t s_rows = kSextPlanes * static_cast<uint64_t>(info->n_segtiles + 1) * LF_TILE_ROWS;
     bool ok = make_map(&maps.p, dt, prob->x_dev, K, T, K * es, 64, 128) &&
               make_map(&maps.q, dt, prob->w_dev, K, N, K * es, 64, nbox) &&
               make_map(&a_map, dt, prob->a_pack_dev, K, static_cast<uint64_t>(info->n_slots) * rp, K * es, 64, rp);
@@ -266,7 +297,8 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
     const bool fuse = !single && !separate && do_shrink && lora && cosched_allowed(ds);
     const int spare = fuse && !cosched_prologue() ? pair_spare_pairs(T, N, ds->num_sms, info->n_shrink_units) : 0;
     // the K-split tail needs a cooperative launch too
-    const PairTail tail = tail_scratch(workspace_dev, workspace_bytes, forward_min_workspace_bytes(info));
+    const PairTail tail = tail_dev ? tail_scratch(tail_dev, tail_bytes, 0)
+                                   : tail_scratch(workspace_dev, workspace_bytes, forward_min_workspace_bytes(info));
     if (fuse && (spare > 0 || cosched_prologue())) {
       PairShrink sh{};
       sh.a_map = a_map;
@@ -276,15 +308,18 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
       sh.n_pairs = spare;
       sh.prologue = cosched_prologue();
       e = tc_gemm_pair(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st, &sh, &tail);
-      if (e == cudaSuccess) return LF_OK;
+      if (e == cudaSuccess) {
+        if (sf_planes) *sf_planes = 2;
+        return LF_OK;
+      }
       // The cooperative launch was refused (e.g. other work holds SMs, or a profiler
       // serializes launches): nothing ran; use the two-launch path from now on.
-      (void)cudaGetLastError();
-      ds->no_cosched = true;
+      refuse_cosched(ds, e);
     }
     if (do_shrink) {
       e = tc_shrink(dt, maps.p, a_map, K, tb, workspace_dev, ds->num_sms, st);
       if (e != cudaSuccess) return LF_ERR_CUDA;
+      if (sf_planes) *sf_planes = 1;
     }
     if (do_gemm) {
       if (single) {
@@ -293,8 +328,7 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
         e = tc_gemm_pair(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st, nullptr,
                          cosched_allowed(ds) ? &tail : nullptr);
         if (e != cudaSuccess && cosched_allowed(ds)) {  // cooperative launch refused: nothing ran
-          (void)cudaGetLastError();
-          ds->no_cosched = true;
+          refuse_cosched(ds, e);
           e = tc_gemm_pair(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st);
         }
       }
@@ -302,7 +336,7 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
     return to_status(e);
   }
 
-  float* s_ext = static_cast<float*>(workspace_dev);
+  double* s_ext = static_cast<double*>(workspace_dev);
   if (do_shrink) {
     e = simt_shrink(dt, prob->x_dev, K, K, prob->a_pack_dev, tb, s_ext, st);
     if (e != cudaSuccess) return LF_ERR_CUDA;
@@ -311,6 +345,27 @@ extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* inf
     e = simt_gemm(dt, prob->x_dev, K, prob->w_dev, K, 1, T, N, K, s_ext, lora ? prob->b_pack_dev : nullptr, tb, y_dev,
                   N, st);
   return to_status(e);
+}
+}  // namespace
+
+extern "C" int lf_forward_stages(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
+                                 void* y_dev, void* workspace_dev, size_t workspace_bytes, int32_t stages,
+                                 lf_stream_t stream) {
+  return forward_impl(prob, info, table_dev, y_dev, workspace_dev, workspace_bytes, nullptr, 0, stages, stream,
+                      nullptr);
+}
+
+extern "C" int lf_forward_sf(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, void* y_dev,
+                             void* workspace_dev, size_t workspace_bytes, void* tail_dev, size_t tail_bytes,
+                             int32_t* s_f_planes, lf_stream_t stream) {
+  if (!s_f_planes) return LF_ERR_INVALID_ARG;
+  return forward_impl(prob, info, table_dev, y_dev, workspace_dev, workspace_bytes, tail_dev, tail_bytes,
+                      LF_STAGE_SHRINK | LF_STAGE_EXPAND, stream, s_f_planes);
+}
+
+extern "C" size_t lf_forward_fixed_workspace_bytes(const lf_plan_info* info, int32_t dtype) {
+  (void)dtype;
+  return forward_min_workspace_bytes(info);
 }
 
 extern "C" int lf_forward_launch_count(const lf_problem* prob, const lf_plan_info* info) {
@@ -346,6 +401,15 @@ extern "C" int lf_set_co_scheduling(int32_t enable) {
   return LF_OK;
 }
 
+extern "C" int lf_get_co_scheduling(int32_t* mode, int32_t* refused_error) {
+  if (!mode || !refused_error) return LF_ERR_INVALID_ARG;
+  DeviceState* ds = nullptr;
+  if (device_state(&ds) != cudaSuccess) return LF_ERR_CUDA;
+  *mode = g_cosched_mode.load();
+  *refused_error = ds->no_cosched.load() ? ds->refusal.load() : 0;
+  return LF_OK;
+}
+
 extern "C" int lf_release(void) {
   for (DeviceState& d : g_dev) {
     std::lock_guard<std::mutex> lk(d.ev_mu);
@@ -363,17 +427,26 @@ extern "C" int lf_forward_host(const lf_problem* prob, const lf_host_chunk* chun
     return LF_ERR_INVALID_ARG;
   if (prob->dtype != LF_F32 && prob->dtype != LF_BF16 && prob->dtype != LF_F16) return LF_ERR_INVALID_ARG;
   const size_t es = static_cast<size_t>(elem_bytes(prob->dtype));
+  // Every chunk is checked before anything is enqueued, with the checks lf_forward makes, so a
+  // bad chunk list fails with nothing in flight.
   int end = 0;
   for (int32_t c = 0; c < n_chunks; ++c) {
     const lf_host_chunk& ch = chunks[c];
     if (ch.row0 != end || ch.rows < 0 || !ch.info || ch.info->total_rows != ch.rows) return LF_ERR_INVALID_ARG;
+    lf_problem pc = *prob;
+    pc.T = ch.rows;
+    const int rc = check_problem(&pc, ch.info, ch.table_dev);
+    if (rc != LF_OK) return rc;
+    if (ch.rows > 0 && prob->N > 0 && (workspace_bytes < forward_min_workspace_bytes(ch.info) || !workspace_dev))
+      return LF_ERR_CAPACITY;
     end += ch.rows;
   }
   if (end != prob->T) return LF_ERR_INVALID_ARG;
   if (n_chunks == 0) return LF_OK;
+  if (prob->N > 0 && (!prob->w_dev || !prob->a_pack_dev || !prob->b_pack_dev)) return LF_ERR_INVALID_ARG;
   DeviceState* ds = nullptr;
   if (device_state(&ds) != cudaSuccess) return LF_ERR_CUDA;
-  const size_t n_ev = 2 * static_cast<size_t>(n_chunks) + 2;
+  const size_t n_ev = 2 * static_cast<size_t>(n_chunks) + 3;
   std::lock_guard<std::mutex> lk(ds->ev_mu);  // one enqueue at a time per device shares the events
   while (ds->events.size() < n_ev) {
     cudaEvent_t ev;
@@ -393,24 +466,31 @@ extern "C" int lf_forward_host(const lf_problem* prob, const lf_host_chunk* chun
   char* xd = static_cast<char*>(x_dev);
   char* yd = static_cast<char*>(y_dev);
   const size_t row_in = static_cast<size_t>(prob->K) * es, row_out = static_cast<size_t>(prob->N) * es;
-  for (int32_t c = 0; c < n_chunks; ++c) {
+  int rc = LF_OK;
+  for (int32_t c = 0; c < n_chunks && rc == LF_OK; ++c) {
     const lf_host_chunk& ch = chunks[c];
     const size_t r0 = static_cast<size_t>(ch.row0), nr = static_cast<size_t>(ch.rows);
-    cudaEvent_t ev_in = ev[2 + 2 * c], ev_out = ev[3 + 2 * c];
+    cudaEvent_t ev_in = ev[3 + 2 * c], ev_out = ev[4 + 2 * c];
     if (cudaMemcpyAsync(xd + r0 * row_in, xh + r0 * row_in, nr * row_in, cudaMemcpyHostToDevice, si) != cudaSuccess ||
-        cudaEventRecord(ev_in, si) != cudaSuccess || cudaStreamWaitEvent(cs, ev_in, 0) != cudaSuccess)
-      return LF_ERR_CUDA;
+        cudaEventRecord(ev_in, si) != cudaSuccess || cudaStreamWaitEvent(cs, ev_in, 0) != cudaSuccess) {
+      rc = LF_ERR_CUDA;
+      break;
+    }
     lf_problem pc = *prob;
     pc.T = ch.rows;
     pc.x_dev = xd + r0 * row_in;
-    const int rc = lf_forward(&pc, ch.info, ch.table_dev, yd + r0 * row_out, workspace_dev, workspace_bytes, stream);
-    if (rc != LF_OK) return rc;
+    rc = lf_forward(&pc, ch.info, ch.table_dev, yd + r0 * row_out, workspace_dev, workspace_bytes, stream);
+    if (rc != LF_OK) break;
     if (cudaEventRecord(ev_out, cs) != cudaSuccess || cudaStreamWaitEvent(so, ev_out, 0) != cudaSuccess ||
         cudaMemcpyAsync(yh + r0 * row_out, yd + r0 * row_out, nr * row_out, cudaMemcpyDeviceToHost, so) != cudaSuccess)
-      return LF_ERR_CUDA;
+      rc = LF_ERR_CUDA;
   }
-  if (cudaEventRecord(ev[1], so) != cudaSuccess || cudaStreamWaitEvent(cs, ev[1], 0) != cudaSuccess) return LF_ERR_CUDA;
-  return LF_OK;
+  // `stream` waits for both copy streams, also after a failure part-way: the caller may release
+  // x_dev / y_dev / the host buffers once `stream` has passed this point.
+  const bool joined = cudaEventRecord(ev[1], so) == cudaSuccess && cudaStreamWaitEvent(cs, ev[1], 0) == cudaSuccess &&
+                      cudaEventRecord(ev[2], si) == cudaSuccess && cudaStreamWaitEvent(cs, ev[2], 0) == cudaSuccess;
+  if (rc == LF_OK && !joined) rc = LF_ERR_CUDA;
+  return rc;
 }
 
 extern "C" int lf_forward(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, void* y_dev,
@@ -423,8 +503,8 @@ namespace {
 // The backward; `sf_given` (planes `sf_planes`) is S_f = s x A_i^T as a forward left it in its
 // workspace (tensor-core path only), or null to compute it here.
 int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, const void* grad_out_dev,
-                  const void* sf_given, int sf_planes, void* grad_x_dev, void* grad_a_dev, void* grad_b_dev,
-                  void* workspace_dev, size_t workspace_bytes, lf_stream_t stream) {
+                  const void* sf_given, int sf_planes, int grad_f32, void* grad_x_dev, void* grad_a_dev,
+                  void* grad_b_dev, void* workspace_dev, size_t workspace_bytes, lf_stream_t stream) {
   int rc = check_problem(prob, info, table_dev);
   if (rc != LF_OK) return rc;
   const int T = prob->T, K = prob->K, N = prob->N;
@@ -439,8 +519,9 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
   if (info->n_slots > 0 && (!grad_a_dev || !grad_b_dev)) return LF_ERR_INVALID_ARG;
   if (T == 0 || info->n_segtiles == 0) {  // adapters whose routes are all empty still get (zero) gradients
     const size_t ra = static_cast<size_t>(info->rank_total);
-    if (ra > 0 && K > 0 && cudaMemsetAsync(grad_a_dev, 0, ra * K * es, st) != cudaSuccess) return LF_ERR_CUDA;
-    if (ra > 0 && N > 0 && cudaMemsetAsync(grad_b_dev, 0, ra * N * es, st) != cudaSuccess) return LF_ERR_CUDA;
+    const size_t gs = grad_f32 ? 4 : es;
+    if (ra > 0 && K > 0 && cudaMemsetAsync(grad_a_dev, 0, ra * K * gs, st) != cudaSuccess) return LF_ERR_CUDA;
+    if (ra > 0 && N > 0 && cudaMemsetAsync(grad_b_dev, 0, ra * N * gs, st) != cudaSuccess) return LF_ERR_CUDA;
     if (T == 0) return LF_OK;
   }
   if (!prob->x_dev || !prob->w_dev || !grad_out_dev || !grad_x_dev) return LF_ERR_INVALID_ARG;
@@ -460,7 +541,7 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
     CUtensorMap p_x, p_g, a_map, bt_map, sf_map, sb_map;
     TcMaps dx;
     const PairTail tail = tail_scratch(workspace_dev, workspace_bytes, backward_min_workspace_bytes(info));
-    const uint64_t s_rows = 2 * static_cast<uint64_t>(info->n_segtiles + 1) * LF_TILE_ROWS;  // two planes
+    const uint64_t s_rows = kSextPlanes * static_cast<uint64_t>(info->n_segtiles + 1) * LF_TILE_ROWS;
     bool ok = make_map(&p_x, dt, prob->x_dev, K, T, K * es, 64, 128) &&
               make_map(&p_g, dt, grad_out_dev, N, T, N * es, 64, 128) &&
               make_map(&dx.q, dt, prob->w_dev, K, N, K * es, 64, 64);
@@ -475,7 +556,7 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
     ok = ok && make_map(&dx.o, dt, grad_x_dev, K, T, K * es, 64, 32);
     if (!ok) return LF_ERR_UNSUPPORTED;
     dx.p = p_g;
-    int planes = 1;  // S_b planes (S_f planes: sf_planes when reused, else the same as S_b's)
+    int planes = 1;  // S_b's K-half planes (S_f's: sf_planes when reused, else the same as S_b's)
     bool gemm_done = false;
     if (lora) {
       dx.s = sb_map;
@@ -502,8 +583,7 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
           planes = 2;
           gemm_done = true;
         } else {
-          (void)cudaGetLastError();  // cooperative launch refused: nothing ran
-          ds->no_cosched = true;
+          refuse_cosched(ds, e);  // cooperative launch refused: nothing ran
         }
       }
       if (!gemm_done) {
@@ -521,8 +601,7 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
       e = tc_gemm_pair(dt, true, dx, T, K, N, lora, tb, grad_x_dev, K, ds->num_sms, st, nullptr,
                        cosched_allowed(ds) ? &tail : nullptr);
       if (e != cudaSuccess && cosched_allowed(ds)) {  // cooperative launch refused: nothing ran
-        (void)cudaGetLastError();
-        ds->no_cosched = true;
+        refuse_cosched(ds, e);
         e = tc_gemm_pair(dt, true, dx, T, K, N, lora, tb, grad_x_dev, K, ds->num_sms, st);
       }
       if (e != cudaSuccess) return LF_ERR_CUDA;
@@ -534,26 +613,30 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
       jobs[0].C = N;
       jobs[0].out = grad_b_dev;
       jobs[0].transpose_out = 0;
+      jobs[0].out_f32 = grad_f32;
       jobs[1].d_map = p_x;
       jobs[1].s_map = sb_map;
       jobs[1].C = K;
       jobs[1].out = grad_a_dev;
       jobs[1].transpose_out = 1;
+      jobs[1].out_f32 = grad_f32;
       void* scratch = ws + 2 * sb + flag_bytes(info, 2);
+      // the grams read hi and lo planes: 2 per K half
       const int f_planes = reuse_sf ? sf_planes : planes;
       if (f_planes == planes) {
-        e = tc_gram(dt, jobs, 2, tb, ds->num_sms, st, planes, scratch, next_generation());
+        e = tc_gram(dt, jobs, 2, tb, ds->num_sms, st, 2 * planes, scratch, next_generation());
       } else {  // S_f and S_b hold different plane counts: one launch each
-        e = tc_gram(dt, &jobs[0], 1, tb, ds->num_sms, st, f_planes, scratch, next_generation());
-        if (e == cudaSuccess) e = tc_gram(dt, &jobs[1], 1, tb, ds->num_sms, st, planes, scratch, next_generation());
+        e = tc_gram(dt, &jobs[0], 1, tb, ds->num_sms, st, 2 * f_planes, scratch, next_generation());
+        if (e == cudaSuccess)
+          e = tc_gram(dt, &jobs[1], 1, tb, ds->num_sms, st, 2 * planes, scratch, next_generation());
       }
       if (e != cudaSuccess) return LF_ERR_CUDA;
     }
     return LF_OK;
   }
 
-  float* sf = reinterpret_cast<float*>(ws);  // the CUDA-core path computes its own float S_f
-  float* sbp = static_cast<float*>(s_b);
+  double* sf = reinterpret_cast<double*>(ws);  // the CUDA-core path computes its own f64 S_f
+  double* sbp = static_cast<double*>(s_b);
   e = simt_shrink(dt, prob->x_dev, K, K, prob->a_pack_dev, tb, sf, st);
   if (e != cudaSuccess) return LF_ERR_CUDA;
   e = simt_shrink(dt, grad_out_dev, N, N, prob->bt_pack_dev, tb, sbp, st);
@@ -561,9 +644,9 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
   // grad_x = g W + S_b . A   (Q(c, m) = W[m][c])
   e = simt_gemm(dt, grad_out_dev, N, prob->w_dev, 1, K, T, K, N, sbp, prob->at_pack_dev, tb, grad_x_dev, K, st);
   if (e != cudaSuccess) return LF_ERR_CUDA;
-  e = simt_gram(dt, grad_out_dev, N, N, sf, tb, grad_b_dev, 0, st);
+  e = simt_gram(dt, grad_out_dev, N, N, sf, tb, grad_b_dev, 0, grad_f32, st);
   if (e != cudaSuccess) return LF_ERR_CUDA;
-  e = simt_gram(dt, prob->x_dev, K, K, sbp, tb, grad_a_dev, 1, st);
+  e = simt_gram(dt, prob->x_dev, K, K, sbp, tb, grad_a_dev, 1, grad_f32, st);
   return to_status(e);
 }
 }  // namespace
@@ -571,7 +654,7 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
 extern "C" int lf_backward(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
                            const void* grad_out_dev, void* grad_x_dev, void* grad_a_dev, void* grad_b_dev,
                            void* workspace_dev, size_t workspace_bytes, lf_stream_t stream) {
-  return backward_impl(prob, info, table_dev, grad_out_dev, nullptr, 0, grad_x_dev, grad_a_dev, grad_b_dev,
+  return backward_impl(prob, info, table_dev, grad_out_dev, nullptr, 0, 0, grad_x_dev, grad_a_dev, grad_b_dev,
                        workspace_dev, workspace_bytes, stream);
 }
 
@@ -580,8 +663,20 @@ extern "C" int lf_backward_sf(const lf_problem* prob, const lf_plan_info* info, 
                               void* grad_a_dev, void* grad_b_dev, void* workspace_dev, size_t workspace_bytes,
                               lf_stream_t stream) {
   if (!s_f_dev || (s_f_planes != 1 && s_f_planes != 2)) return LF_ERR_INVALID_ARG;
-  return backward_impl(prob, info, table_dev, grad_out_dev, s_f_dev, s_f_planes, grad_x_dev, grad_a_dev, grad_b_dev,
-                       workspace_dev, workspace_bytes, stream);
+  return backward_impl(prob, info, table_dev, grad_out_dev, s_f_dev, s_f_planes, 0, grad_x_dev, grad_a_dev,
+                       grad_b_dev, workspace_dev, workspace_bytes, stream);
+}
+
+extern "C" int lf_backward_ex(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
+                              const void* grad_out_dev, const void* s_f_dev, int32_t s_f_planes, int32_t grad_ab_dtype,
+                              void* grad_x_dev, void* grad_a_dev, void* grad_b_dev, void* workspace_dev,
+                              size_t workspace_bytes, lf_stream_t stream) {
+  if (!prob) return LF_ERR_INVALID_ARG;
+  if (s_f_dev && s_f_planes != 1 && s_f_planes != 2) return LF_ERR_INVALID_ARG;
+  if (grad_ab_dtype != prob->dtype && grad_ab_dtype != LF_F32) return LF_ERR_INVALID_ARG;
+  return backward_impl(prob, info, table_dev, grad_out_dev, s_f_dev, s_f_dev ? s_f_planes : 0,
+                       grad_ab_dtype == LF_F32 ? 1 : 0, grad_x_dev, grad_a_dev, grad_b_dev, workspace_dev,
+                       workspace_bytes, stream);
 }
 
 extern "C" int lf_device_error(int32_t* code) {

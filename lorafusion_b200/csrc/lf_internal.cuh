@@ -42,17 +42,18 @@ struct Tables {
 
 Tables make_tables(const lf_plan_info* info, const int32_t* table_dev);
 
-// --------------------------------------------------------------- SIMT (any dtype, f32 math)
+// --------------------------------------------------------------- SIMT (any dtype, f64 sums)
 // S_ext[st][row][j] = (row in segment) ? scale * sum_k P[tile*128+row][k] * Apk[slot][j][k] : 0
 cudaError_t simt_shrink(int dtype, const void* P, int64_t ldp, int Kred, const void* apk, const Tables& tb,
-                        float* s_ext, cudaStream_t st);
+                        double* s_ext, cudaStream_t st);
 // out[t][n] = sum_k P[t][k] Q(n,k) + sum_j S_ext[st(t)][row][j] * L[slot][n][j],  Q(n,k) = Q[n*qsn + k*qsk]
 cudaError_t simt_gemm(int dtype, const void* P, int64_t ldp, const void* Q, int64_t qsn, int64_t qsk, int T, int Nout,
-                      int Kred, const float* s_ext, const void* lpk, const Tables& tb, void* out, int64_t ldo,
+                      int Kred, const double* s_ext, const void* lpk, const Tables& tb, void* out, int64_t ldo,
                       cudaStream_t st);
-// grad[slot] = sum_{rows of slot} D[row][c] * S_ext[..][row][j]; layout [C][rank] or [rank][C] (transpose_out)
-cudaError_t simt_gram(int dtype, const void* D, int64_t ldd, int C, const float* s_ext, const Tables& tb,
-                      void* out, int transpose_out, cudaStream_t st);
+// grad[slot] = sum_{rows of slot} D[row][c] * S_ext[..][row][j]; layout [C][rank] or [rank][C] (transpose_out),
+// in the input type or (out_f32) in float
+cudaError_t simt_gram(int dtype, const void* D, int64_t ldd, int C, const double* s_ext, const Tables& tb,
+                      void* out, int transpose_out, int out_f32, cudaStream_t st);
 
 // --------------------------------------------------------------- tcgen05 (bf16 / f16)
 struct TcMaps {
@@ -129,6 +130,7 @@ struct GramJobDesc {
   int C;
   void* out;
   int transpose_out;
+  int out_f32;  // write the gradient blocks as float instead of the input type
 };
 cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables& tb, int num_sms, cudaStream_t st,
                     int planes = 1, void* scratch = nullptr, uint64_t gen = 0);

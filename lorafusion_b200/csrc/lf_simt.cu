@@ -1,8 +1,9 @@
-// CUDA-core kernels of the fused LoRA op, f32 arithmetic for any input dtype.
-// They carry the float32 problems (where tensor cores cannot meet a 1e-5 bound)
-// and any shape the TMA path cannot address (rows not 16-byte aligned).
-// Same decomposition as the tensor-core path: routed shrink -> S_ext,
-// base GEMM with the LoRA expand in its epilogue, segmented gram for dA/dB.
+// CUDA-core kernels of the fused LoRA op: products of the input values summed in f64, one
+// rounding to the output type at the end.  They carry the float32 problems (where tensor cores
+// cannot meet a 1e-5 bound: a float32 result within a few float32 ulps of the exact value) and
+// any shape the TMA path cannot address (rows not 16-byte aligned).  Same decomposition as the
+// tensor-core path: routed shrink -> S_ext (f64), base GEMM with the LoRA expand in its
+// epilogue, segmented gram for dA/dB.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -33,15 +34,15 @@ __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_
 template <typename T>
 __global__ void __launch_bounds__(256) simt_shrink_kernel(const T* __restrict__ P, int64_t ldp, int Kred,
                                                           const T* __restrict__ apk, Tables tb,
-                                                          float* __restrict__ s_ext) {
+                                                          double* __restrict__ s_ext) {
   const int st = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.y * 8 + warp;  // row inside the 128-row tile
   const int r_pad = tb.r_pad;
-  float* out = s_ext + (static_cast<int64_t>(st) * LF_TILE_ROWS + row) * r_pad;
+  double* out = s_ext + (static_cast<int64_t>(st) * LF_TILE_ROWS + row) * r_pad;
   const int lo = tb.st_lo(st), hi = tb.st_hi(st);
   if (row < lo || row >= hi) {
-    for (int j = lane; j < r_pad; j += 32) out[j] = 0.f;
+    for (int j = lane; j < r_pad; j += 32) out[j] = 0.0;
     return;
   }
   const int slot = tb.st_slot(st);
@@ -50,13 +51,14 @@ __global__ void __launch_bounds__(256) simt_shrink_kernel(const T* __restrict__ 
   const T* xr = P + grow * ldp;
   const T* a = apk + static_cast<int64_t>(slot) * r_pad * Kred;
   for (int j0 = 0; j0 < r_pad; j0 += 16) {
-    float acc[16];
+    double acc[16];
 #pragma unroll
-    for (int jj = 0; jj < 16; ++jj) acc[jj] = 0.f;
+    for (int jj = 0; jj < 16; ++jj) acc[jj] = 0.0;
     for (int k = lane; k < Kred; k += 32) {
-      const float xv = to_f(xr[k]);
+      const double xv = to_f(xr[k]);
 #pragma unroll
-      for (int jj = 0; jj < 16; ++jj) acc[jj] = fmaf(xv, to_f(a[static_cast<int64_t>(j0 + jj) * Kred + k]), acc[jj]);
+      for (int jj = 0; jj < 16; ++jj)
+        acc[jj] = fma(xv, static_cast<double>(to_f(a[static_cast<int64_t>(j0 + jj) * Kred + k])), acc[jj]);
     }
 #pragma unroll
     for (int jj = 0; jj < 16; ++jj) {
@@ -64,11 +66,11 @@ __global__ void __launch_bounds__(256) simt_shrink_kernel(const T* __restrict__ 
       for (int o = 16; o > 0; o >>= 1) acc[jj] += __shfl_xor_sync(0xffffffffu, acc[jj], o);
     }
     if (lane < 16) {
-      float v = acc[0];
+      double v = acc[0];
 #pragma unroll
       for (int jj = 1; jj < 16; ++jj)
         if (lane == jj) v = acc[jj];
-      out[j0 + lane] = scale * v;
+      out[j0 + lane] = static_cast<double>(scale) * v;
     }
   }
 }
@@ -79,7 +81,7 @@ constexpr int SG_BM = 64, SG_BN = 64, SG_BK = 16;
 template <typename T>
 __global__ void __launch_bounds__(256) simt_gemm_kernel(const T* __restrict__ P, int64_t ldp,
                                                         const T* __restrict__ Q, int64_t qsn, int64_t qsk, int Trows,
-                                                        int Nout, int Kred, const float* __restrict__ s_ext,
+                                                        int Nout, int Kred, const double* __restrict__ s_ext,
                                                         const T* __restrict__ lpk, Tables tb, T* __restrict__ out,
                                                         int64_t ldo) {
   __shared__ float ps[SG_BK][SG_BM + 4];
@@ -87,7 +89,7 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const T* __restrict__ P,
   const int m0 = blockIdx.y * SG_BM, n0 = blockIdx.x * SG_BN;
   const int tid = threadIdx.x;
   const int tr = tid / 16, tc = tid % 16;  // 16x16 threads, 4x4 each
-  float acc[4][4] = {};
+  double acc[4][4] = {};
   for (int k0 = 0; k0 < Kred; k0 += SG_BK) {
     for (int e = tid; e < SG_BM * SG_BK; e += 256) {
       const int r = e / SG_BK, k = e % SG_BK;
@@ -118,7 +120,7 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const T* __restrict__ P,
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        for (int j = 0; j < 4; ++j) acc[i][j] = fma(static_cast<double>(a[i]), static_cast<double>(b[j]), acc[i][j]);
     }
     __syncthreads();
   }
@@ -136,14 +138,15 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const T* __restrict__ P,
       for (int j = st_b; j < st_e; ++j)
         if (row >= tb.st_lo(j) && row < tb.st_hi(j)) st = j;
       if (st < 0) continue;
-      const float* srow = s_ext + (static_cast<int64_t>(st) * LF_TILE_ROWS + row) * r_pad;
+      const double* srow = s_ext + (static_cast<int64_t>(st) * LF_TILE_ROWS + row) * r_pad;
       const T* lb = lpk + static_cast<int64_t>(tb.st_slot(st)) * Nout * r_pad;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int gn = n0 + tc * 4 + j;
         if (gn >= Nout) continue;
-        float d = 0.f;
-        for (int q = 0; q < r_pad; ++q) d = fmaf(srow[q], to_f(lb[static_cast<int64_t>(gn) * r_pad + q]), d);
+        double d = 0.0;
+        for (int q = 0; q < r_pad; ++q)
+          d = fma(srow[q], static_cast<double>(to_f(lb[static_cast<int64_t>(gn) * r_pad + q])), d);
         acc[i][j] += d;
       }
     }
@@ -155,60 +158,60 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const T* __restrict__ P,
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int gn = n0 + tc * 4 + j;
-      if (gn < Nout) out[static_cast<int64_t>(gr) * ldo + gn] = from_f<T>(acc[i][j]);
+      if (gn < Nout) out[static_cast<int64_t>(gr) * ldo + gn] = from_f<T>(static_cast<float>(acc[i][j]));
     }
   }
 }
 
-// One thread per output column c of one slot; accumulators over the padded rank.
-template <typename T, int R>
+// One thread per output column c of one slot; accumulators over the padded rank.  O: output type.
+template <typename T, typename O, int R>
 __global__ void __launch_bounds__(128) simt_gram_kernel(const T* __restrict__ D, int64_t ldd, int C,
-                                                        const float* __restrict__ s_ext, Tables tb,
-                                                        T* __restrict__ out, int transpose_out) {
+                                                        const double* __restrict__ s_ext, Tables tb,
+                                                        O* __restrict__ out, int transpose_out) {
   const int slot = blockIdx.x;
   const int c = blockIdx.y * 128 + threadIdx.x;
-  float acc[R];
+  double acc[R];
 #pragma unroll
-  for (int j = 0; j < R; ++j) acc[j] = 0.f;
+  for (int j = 0; j < R; ++j) acc[j] = 0.0;
   const int b = tb.slot_st(slot), e = tb.slot_st(slot + 1);
   for (int i = b; i < e; ++i) {
     const int st = tb.slot_list(i);
     const int lo = tb.st_lo(st), hi = tb.st_hi(st);
     const int64_t row0 = static_cast<int64_t>(tb.st_tile(st)) * LF_TILE_ROWS;
     for (int r = lo; r < hi; ++r) {
-      const float d = (c < C) ? to_f(D[(row0 + r) * ldd + c]) : 0.f;
-      const float* s = s_ext + (static_cast<int64_t>(st) * LF_TILE_ROWS + r) * R;
+      const double d = (c < C) ? static_cast<double>(to_f(D[(row0 + r) * ldd + c])) : 0.0;
+      const double* s = s_ext + (static_cast<int64_t>(st) * LF_TILE_ROWS + r) * R;
 #pragma unroll
-      for (int j = 0; j < R; ++j) acc[j] = fmaf(d, s[j], acc[j]);
+      for (int j = 0; j < R; ++j) acc[j] = fma(d, s[j], acc[j]);
     }
   }
   if (c >= C) return;
   const int rank = tb.slot_rank(slot);
-  T* o = out + static_cast<int64_t>(tb.rank_prefix(slot)) * C;
+  O* o = out + static_cast<int64_t>(tb.rank_prefix(slot)) * C;
 #pragma unroll
   for (int j = 0; j < R; ++j) {
     if (j >= rank) break;
     if (transpose_out)
-      o[static_cast<int64_t>(j) * C + c] = from_f<T>(acc[j]);
+      o[static_cast<int64_t>(j) * C + c] = from_f<O>(static_cast<float>(acc[j]));
     else
-      o[static_cast<int64_t>(c) * rank + j] = from_f<T>(acc[j]);
+      o[static_cast<int64_t>(c) * rank + j] = from_f<O>(static_cast<float>(acc[j]));
   }
 }
 
-template <typename T>
-cudaError_t gram_dispatch(const void* D, int64_t ldd, int C, const float* s_ext, const Tables& tb, void* out,
+template <typename T, typename O>
+cudaError_t gram_dispatch(const void* D, int64_t ldd, int C, const double* s_ext, const Tables& tb, void* out,
                           int transpose_out, cudaStream_t st) {
   dim3 grid(tb.n_slots, (C + 127) / 128);
   if (tb.n_slots == 0 || C == 0) return cudaSuccess;
   switch (tb.r_pad) {
     case 16:
-      simt_gram_kernel<T, 16><<<grid, 128, 0, st>>>((const T*)D, ldd, C, s_ext, tb, (T*)out, transpose_out);
+      simt_gram_kernel<T, O, 16><<<grid, 128, 0, st>>>((const T*)D, ldd, C, s_ext, tb, (O*)out, transpose_out);
       break;
     case 32:
-      simt_gram_kernel<T, 32><<<grid, 128, 0, st>>>((const T*)D, ldd, C, s_ext, tb, (T*)out, transpose_out);
+      simt_gram_kernel<T, O, 32><<<grid, 128, 0, st>>>((const T*)D, ldd, C, s_ext, tb, (O*)out, transpose_out);
       break;
     default:
-      simt_gram_kernel<T, 64><<<grid, 128, 0, st>>>((const T*)D, ldd, C, s_ext, tb, (T*)out, transpose_out);
+      simt_gram_kernel<T, O, 64><<<grid, 128, 0, st>>>((const T*)D, ldd, C, s_ext, tb, (O*)out, transpose_out);
       break;
   }
   return cudaGetLastError();
@@ -217,7 +220,7 @@ cudaError_t gram_dispatch(const void* D, int64_t ldd, int C, const float* s_ext,
 }  // namespace
 
 cudaError_t simt_shrink(int dtype, const void* P, int64_t ldp, int Kred, const void* apk, const Tables& tb,
-                        float* s_ext, cudaStream_t st) {
+                        double* s_ext, cudaStream_t st) {
   if (tb.n_segtiles == 0) return cudaSuccess;
   dim3 grid(tb.n_segtiles, LF_TILE_ROWS / 8);
   switch (dtype) {
@@ -236,7 +239,7 @@ cudaError_t simt_shrink(int dtype, const void* P, int64_t ldp, int Kred, const v
 }
 
 cudaError_t simt_gemm(int dtype, const void* P, int64_t ldp, const void* Q, int64_t qsn, int64_t qsk, int T, int Nout,
-                      int Kred, const float* s_ext, const void* lpk, const Tables& tb, void* out, int64_t ldo,
+                      int Kred, const double* s_ext, const void* lpk, const Tables& tb, void* out, int64_t ldo,
                       cudaStream_t st) {
   if (T == 0 || Nout == 0) return cudaSuccess;
   dim3 grid((Nout + SG_BN - 1) / SG_BN, (T + SG_BM - 1) / SG_BM);
@@ -258,15 +261,17 @@ cudaError_t simt_gemm(int dtype, const void* P, int64_t ldp, const void* Q, int6
   return cudaGetLastError();
 }
 
-cudaError_t simt_gram(int dtype, const void* D, int64_t ldd, int C, const float* s_ext, const Tables& tb, void* out,
-                      int transpose_out, cudaStream_t st) {
+cudaError_t simt_gram(int dtype, const void* D, int64_t ldd, int C, const double* s_ext, const Tables& tb, void* out,
+                      int transpose_out, int out_f32, cudaStream_t st) {
   switch (dtype) {
     case LF_F32:
-      return gram_dispatch<float>(D, ldd, C, s_ext, tb, out, transpose_out, st);
+      return gram_dispatch<float, float>(D, ldd, C, s_ext, tb, out, transpose_out, st);
     case LF_BF16:
-      return gram_dispatch<__nv_bfloat16>(D, ldd, C, s_ext, tb, out, transpose_out, st);
+      return out_f32 ? gram_dispatch<__nv_bfloat16, float>(D, ldd, C, s_ext, tb, out, transpose_out, st)
+                     : gram_dispatch<__nv_bfloat16, __nv_bfloat16>(D, ldd, C, s_ext, tb, out, transpose_out, st);
     default:
-      return gram_dispatch<__half>(D, ldd, C, s_ext, tb, out, transpose_out, st);
+      return out_f32 ? gram_dispatch<__half, float>(D, ldd, C, s_ext, tb, out, transpose_out, st)
+                     : gram_dispatch<__half, __half>(D, ldd, C, s_ext, tb, out, transpose_out, st);
   }
 }
 

@@ -51,6 +51,32 @@ template <>
 __device__ __forceinline__ __half cvt_out<__half>(float v) {
   return __float2half_rn(v);
 }
+__device__ __forceinline__ float cvt_in(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float cvt_in(__half v) { return __half2float(v); }
+
+// S values enter the dA/dB sums as hi + lo (both in the input type): hi = round(v) is what the
+// LoRA expand reads, lo = round(v - hi) restores the bits hi dropped.
+template <typename OutT>
+__device__ __forceinline__ void split_hi_lo(float v, OutT& hi, OutT& lo) {
+  hi = cvt_out<OutT>(v);
+  lo = cvt_out<OutT>(v - cvt_in(hi));
+}
+// Pack 8 values as hi (pk_hi) and lo (pk_lo) halves of two uint4 each.
+template <typename OutT>
+__device__ __forceinline__ void pack8_hi_lo(const float* v, uint4& pk_hi, uint4& pk_lo) {
+  uint32_t* h = reinterpret_cast<uint32_t*>(&pk_hi);
+  uint32_t* l = reinterpret_cast<uint32_t*>(&pk_lo);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    OutT h0, l0, h1, l1;
+    split_hi_lo<OutT>(v[2 * e], h0, l0);
+    split_hi_lo<OutT>(v[2 * e + 1], h1, l1);
+    h[e] = static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&h0)) |
+           (static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&h1)) << 16);
+    l[e] = static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&l0)) |
+           (static_cast<uint32_t>(*reinterpret_cast<uint16_t*>(&l1)) << 16);
+  }
+}
 
 // Time-bounded wait used only while unwinding after an abort: ignores the abort flag.
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* err) {
@@ -481,8 +507,9 @@ __device__ __forceinline__ bool wait_units_ready(const uint64_t* ready, int u0, 
 
 // Shrink role of the co-scheduled pair kernel, run by CTAs [0, 2*n_shrink_pairs) for the whole
 // launch, or (kPrologue) by every CTA before its GEMM tiles: items (job, unit = row tile and
-// <= 64/r_pad segment tiles, K half) on single CTAs, S written straight from TMEM (scaled, masked
-// per segment, bf16/f16), then the item's ready flag is released.  The epilogue warps of CTA 0
+// <= 64/r_pad segment tiles, K half h) on single CTAs, S written straight from TMEM (scaled,
+// masked per segment) as hi in plane h and lo in plane 2 + h (bf16/f16), then the item's ready
+// flag is released.  The epilogue warps of CTA 0
 // also write the all-zero block before releasing item 0.  In prologue mode the role keeps the
 // TMEM allocation permit (the GEMM allocates after it) and its barriers are its own.
 template <typename OutT, bool kPrologue>
@@ -657,18 +684,21 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
                         row < (j == 0 ? hi[0] : j == 1 ? hi[1] : j == 2 ? hi[2] : hi[3]);
         const float scale = j == 0 ? sc[0] : j == 1 ? sc[1] : j == 2 ? sc[2] : sc[3];
         OutT* dst = s_out + h * plane_elems + (static_cast<int64_t>(st0 + j) * kBM + row) * r_pad;
+        OutT* dst_lo = dst + 2 * plane_elems;
         for (int c = 0; c < r_pad; c += 16) {
           uint32_t v[16];
           tmem_ld16(tbase + j * r_pad + c, v);
           tmem_wait_ld();
-          uint4 pk[2];
-          uint32_t* w32 = reinterpret_cast<uint32_t*>(pk);
+          float f[16];
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            w32[e] = pack2<OutT>(in ? scale * __uint_as_float(v[2 * e]) : 0.f,
-                                 in ? scale * __uint_as_float(v[2 * e + 1]) : 0.f);
-          *reinterpret_cast<uint4*>(dst + c) = pk[0];
-          *reinterpret_cast<uint4*>(dst + c + 8) = pk[1];
+          for (int e = 0; e < 16; ++e) f[e] = in ? scale * __uint_as_float(v[e]) : 0.f;
+          uint4 hi0, lo0, hi1, lo1;
+          pack8_hi_lo<OutT>(f, hi0, lo0);
+          pack8_hi_lo<OutT>(f + 8, hi1, lo1);
+          *reinterpret_cast<uint4*>(dst + c) = hi0;
+          *reinterpret_cast<uint4*>(dst + c + 8) = hi1;
+          *reinterpret_cast<uint4*>(dst_lo + c) = lo0;
+          *reinterpret_cast<uint4*>(dst_lo + c + 8) = lo1;
         }
       }
       tc_fence_before();
@@ -1092,7 +1122,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ========================================================================== shrink
 struct ShrinkParams {
-  void* s_ext;
+  void* s_ext;           // hi plane; the lo plane follows at + plane_elems
+  int64_t plane_elems;
   int ab_fmt;
   int Kred;
   int kb_per_split;
@@ -1278,7 +1309,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int st = st0 + j;
       const bool in = row >= seg_lo[j] && row < seg_hi[j];
       const float v = in ? seg_scale[j] * sum : 0.f;
-      out[(static_cast<int64_t>(st) * kBM + row) * r_pad + jj] = cvt_out<OutT>(v);
+      OutT hi, lo;
+      split_hi_lo<OutT>(v, hi, lo);
+      const int64_t idx = (static_cast<int64_t>(st) * kBM + row) * r_pad + jj;
+      out[idx] = hi;
+      out[prm.plane_elems + idx] = lo;
     }
   }
 
@@ -1300,7 +1335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // launch (the backward's dB: D = g, C = N, S = s.x.A^T; and dA: D = x, C = K, S = s.g.B).
 struct GramJob {
   void* out;
-  int C, n_cblk, transpose_out;
+  int C, n_cblk, transpose_out, out_f32;
 };
 struct GramParams {
   GramJob job[2];
@@ -1668,15 +1703,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const GramJob& jb = prm.job[g.job];
       const int c = g.cb * 128 + col;
       const int rank = g.rank;
-      OutT* o = reinterpret_cast<OutT*>(jb.out) + static_cast<int64_t>(g.rank_prefix) * jb.C;
+      // element (j, c) of this slot's block: [rank, C] (transposed) or [C, rank], in the input
+      // type or (out_f32) in float
+      const int64_t obase = static_cast<int64_t>(g.rank_prefix) * jb.C;
+      auto store = [&](int j, float v) {
+        const int64_t idx = obase + (jb.transpose_out ? static_cast<int64_t>(j) * jb.C + c : static_cast<int64_t>(c) * rank + j);
+        if (jb.out_f32)
+          reinterpret_cast<float*>(jb.out)[idx] = v;
+        else
+          reinterpret_cast<OutT*>(jb.out)[idx] = cvt_out<OutT>(v);
+      };
       if (g.b == g.e) {
         if (c < jb.C)
-          for (int j = 0; j < rank; ++j) {
-            if (jb.transpose_out)
-              o[static_cast<int64_t>(j) * jb.C + c] = cvt_out<OutT>(0.f);
-            else
-              o[static_cast<int64_t>(c) * rank + j] = cvt_out<OutT>(0.f);
-          }
+          for (int j = 0; j < rank; ++j) store(j, 0.f);
         continue;
       }
       const int buf = it % prm.n_bufs;
@@ -1744,13 +1783,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) {
               const int j = j0 + jj;
-              if (j < rank) {
-                const OutT val = cvt_out<OutT>(acc[jj]);
-                if (jb.transpose_out)
-                  o[static_cast<int64_t>(j) * jb.C + c] = val;
-                else
-                  o[static_cast<int64_t>(c) * rank + j] = val;
-              }
+              if (j < rank) store(j, acc[jj]);
             }
           }
         }
@@ -1763,13 +1796,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int jj = 0; jj < 16; ++jj) {
             const int j = j0 + jj;
-            if (j < rank) {
-              const OutT val = cvt_out<OutT>(v[jj]);
-              if (jb.transpose_out)
-                o[static_cast<int64_t>(j) * jb.C + c] = val;
-              else
-                o[static_cast<int64_t>(c) * rank + j] = val;
-            }
+            if (j < rank) store(j, v[jj]);
           }
         }
       }
@@ -1990,6 +2017,7 @@ cudaError_t tc_shrink(int dtype, const CUtensorMap& p_map, const CUtensorMap& a_
   while (cluster < kMaxShrCluster && tb.n_units * cluster * 2 <= num_sms && nkb >= 4 * cluster * 2) cluster *= 2;
   ShrinkParams p{};
   p.s_ext = s_ext;
+  p.plane_elems = static_cast<int64_t>(tb.n_segtiles + 1) * kBM * tb.r_pad;
   p.ab_fmt = dtype == LF_BF16 ? 1 : 0;
   p.Kred = Kred;
   p.cluster = cluster;
@@ -2033,6 +2061,7 @@ cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables
     p.job[j].C = jobs[j].C;
     p.job[j].n_cblk = (jobs[j].C + 127) / 128;
     p.job[j].transpose_out = jobs[j].transpose_out;
+    p.job[j].out_f32 = jobs[j].out_f32;
     steps += static_cast<int64_t>(tb.n_segtiles) * p.job[j].n_cblk;
     most += static_cast<int64_t>(tb.n_segtiles + tb.n_slots) * p.job[j].n_cblk;  // units once split
   }

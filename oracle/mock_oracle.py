@@ -1,8 +1,10 @@
 """numpy restatement of lorafusion's CPU reference op (TEST INFRASTRUCTURE ONLY).
 
 Follows ``lorafusion/ops/mock_ops.py`` step by step, in the dtype of the
-inputs (float32 for every comparison in this repository; bf16 problems are
-compared by running this oracle in float32 on the bf16-rounded values):
+inputs.  The parity tests run it in float64 on the very values the GPU gets
+(bf16/f16 problems: the bf16/f16-rounded values), i.e. as the exact math of
+the reference's formula, and compare with the plain elementwise rule of
+:func:`allclose_report`:
 
 * :func:`fused_lora_forward` — ``mock_ops.py:15-48``: ``out = x @ W.T`` then,
   route by route, ``out[rows] += scaling * ((x[rows] @ A.T) @ B.T)``.
@@ -77,14 +79,18 @@ def bf16_round(a: np.ndarray) -> np.ndarray:
     return np.where(nan, np.float32(np.nan), out)
 
 
-def allclose_report(got: np.ndarray, ref: np.ndarray, rtol: float, atol: float) -> tuple[bool, str]:
-    """Elementwise ``|got-ref| <= rtol*|ref| + atol*max(1, max|ref|)``; returns (ok, summary).
+def as_f64(d):
+    """A dict of arrays (or one array) as float64 copies."""
+    if isinstance(d, dict):
+        return {k: np.asarray(v, dtype=np.float64) for k, v in d.items()}
+    return np.asarray(d, dtype=np.float64)
 
-    The absolute term is scaled by the tensor's largest magnitude: the gradient
-    sums reach |ref| ~ 1e2 and cancel, so any implementation that sums in
-    another order (another BLAS included) differs from the reference by about
-    eps * sum|terms| in near-zero entries, which a fixed atol cannot absorb.
-    """
+
+def allclose_report(got: np.ndarray, ref: np.ndarray, rtol: float, atol: float,
+                    bound: np.ndarray | None = None) -> tuple[bool, str]:
+    """Elementwise ``|got - ref| <= atol + rtol * |ref|`` (plus ``bound`` when given); returns
+    (ok, summary).  The summary gives the worst ratio ``|got - ref| / (atol + rtol |ref|)``: at
+    most 1 means every element is within tolerance."""
     got = np.asarray(got, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     if got.shape != ref.shape:
@@ -92,8 +98,37 @@ def allclose_report(got: np.ndarray, ref: np.ndarray, rtol: float, atol: float) 
     if not np.all(np.isfinite(got)):
         return False, f"{int((~np.isfinite(got)).sum())} non-finite values"
     err = np.abs(got - ref)
-    scale = max(1.0, float(np.abs(ref).max())) if ref.size else 1.0
-    bad = err > atol * scale + rtol * np.abs(ref)
-    n_bad = int(bad.sum())
-    worst = float(err.max()) if err.size else 0.0
-    return n_bad == 0, f"{n_bad}/{err.size} outside tol, max abs err {worst:.3e}"
+    lim = atol + rtol * np.abs(ref)
+    if bound is not None:
+        lim = lim + np.asarray(bound, dtype=np.float64)
+    n_bad = int((err > lim).sum())
+    worst = float((err / lim).max()) if err.size else 0.0
+    return n_bad == 0, f"{n_bad}/{err.size} outside tol, worst |err|/tol {worst:.3f}, max abs err " \
+                       f"{float(err.max()) if err.size else 0.0:.3e}"
+
+
+_U32 = 2.0 ** -24  # unit roundoff of float32
+
+
+def fp32_forward_error_bounds(x, w, lora_a, lora_b, scaling, routes, g=None):
+    """Elementwise bounds on how far a float32 evaluation of the reference's formula (any
+    summation order) can be from the exact value: gamma_L * M, where M is the same computation on
+    absolute values (the sum of |terms| of every dot product on the path) and
+    gamma_L = L u / (1 - L u) with L the longest chain of roundings on any path (at most
+    K + N + T + max rank + routes + 4), u = 2^-24 (the classic forward error bound of summation
+    and dot products).  Used only to pin this oracle against the reference's own float32
+    outputs.  Returns (y_bound,) or, with ``g``, (y_bound, gx_bound, ga_bounds, gb_bounds)."""
+    T, K = np.shape(x)
+    N = np.shape(w)[0]
+    max_rank = max((np.shape(a)[0] for a in lora_a.values()), default=0)
+    L = K + N + T + max_rank + len(routes) + 4
+    gamma = L * _U32 / (1.0 - L * _U32)
+    ab = lambda d: {k: np.abs(np.asarray(v, dtype=np.float64)) for k, v in d.items()}  # noqa: E731
+    sc = {k: abs(float(v)) for k, v in scaling.items()}
+    xa, wa = np.abs(np.asarray(x, dtype=np.float64)), np.abs(np.asarray(w, dtype=np.float64))
+    my = fused_lora_forward(xa, wa, ab(lora_a), ab(lora_b), sc, routes)
+    if g is None:
+        return (gamma * my,)
+    mgx, mga, mgb = fused_lora_backward(np.abs(np.asarray(g, dtype=np.float64)), xa, wa, ab(lora_a), ab(lora_b), sc,
+                                        routes)
+    return (gamma * my, gamma * mgx, {k: gamma * v for k, v in mga.items()}, {k: gamma * v for k, v in mgb.items()})

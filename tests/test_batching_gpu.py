@@ -158,7 +158,9 @@ def test_coordinator_end_to_end_matches_oracle():
     for r in reqs:
         x = xs[r.request_id]
         aid = r.adapter_id
-        ref = mock_oracle.fused_lora_forward(x, w, {aid: a[aid]}, {aid: b[aid]}, {aid: 2.0}, [(0, r.num_rows, aid)])
+        f = mock_oracle.as_f64
+        ref = mock_oracle.fused_lora_forward(f(x), f(w), {aid: f(a[aid])}, {aid: f(b[aid])}, {aid: 2.0},
+                                             [(0, r.num_rows, aid)])
         ok, msg = mock_oracle.allclose_report(out[r.request_id].float().cpu().numpy(), ref, **BF16_TOL)
         assert ok, f"request {r.request_id}: {msg}"
     from lorafusion_b200 import _native as nat
