@@ -374,10 +374,28 @@ LF_API int lf_assign_rows(const int32_t* bin_start, const int32_t* entry_adapter
                           int64_t* range_start, int64_t* range_end, int32_t* range_rank, int32_t* n_ranges);
 
 /*
- * Read and clear the device-side error word (bounded-wait timeouts inside kernels).
- * Synchronizes the current device.  *code = 0 when no kernel reported a problem.
+ * Read and clear the device-side error word (bounded-wait timeouts inside kernels: codes 0x101 ..
+ * 0x105).  Synchronizes the current device.  *code = 0 when no kernel reported a problem; after a
+ * nonzero code the outputs of the calls since the previous read are undefined.
  */
 LF_API int lf_device_error(int32_t* code);
+
+/*
+ * Bound of every wait inside this library's kernels on the current device, in nanoseconds
+ * (0 = the default, about 1 s; otherwise 1 ms .. 60 s).  A wait that runs out records its code in
+ * the device status word (lf_device_error), makes its CTA stop, lets the copies and MMAs it
+ * started finish, frees its tensor memory and returns; nothing traps.  Synchronous; call it while
+ * no kernel of this library runs on the device.  No counterpart in the reference.
+ */
+LF_API int lf_set_wait_limit(uint64_t limit_ns);
+
+/*
+ * Test hook for the failure path: the next `launches` co-scheduled GEMM launches (shrink inside the
+ * GEMM launch) make their GEMM CTAs wait for a ready value that no shrink item publishes, so those
+ * waits run out after the wait limit and the launch reports a timeout through lf_device_error; the
+ * launch's outputs are then undefined.  0 cancels.  No counterpart in the reference.
+ */
+LF_API int lf_inject_stale_ready(int32_t launches);
 
 /* Static description of a status code. */
 LF_API const char* lf_status_string(int status);

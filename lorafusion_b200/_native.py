@@ -118,6 +118,10 @@ def _declare(L: ctypes.CDLL) -> None:
     L.lf_backward_sf.restype = ctypes.c_int
     L.lf_forward_noalloc.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p]
     L.lf_forward_noalloc.restype = ctypes.c_int
+    L.lf_set_wait_limit.argtypes = [ctypes.c_uint64]
+    L.lf_set_wait_limit.restype = ctypes.c_int
+    L.lf_inject_stale_ready.argtypes = [_c_i32]
+    L.lf_inject_stale_ready.restype = ctypes.c_int
     L.lf_device_error.argtypes = [P(_c_i32)]
     L.lf_device_error.restype = ctypes.c_int
     L.lf_status_string.argtypes = [ctypes.c_int]
@@ -169,6 +173,15 @@ def co_scheduling() -> tuple[int, int]:
     mode, refused = _c_i32(0), _c_i32(0)
     check(lib().lf_get_co_scheduling(ctypes.byref(mode), ctypes.byref(refused)), "lf_get_co_scheduling")
     return int(mode.value), int(refused.value)
+
+
+# device status codes of bounded waits that ran out (lf_ptx.cuh DeviceErr)
+ERR_TIMEOUT_FULL, ERR_TIMEOUT_EMPTY, ERR_TIMEOUT_ACC, ERR_TIMEOUT_DRAIN, ERR_TIMEOUT_FLAG = 0x101, 0x102, 0x103, 0x104, 0x105
+
+
+def set_wait_limit(limit_ns: int) -> None:
+    """Bound of every in-kernel wait on the current device (0: the default, about 1 s)."""
+    check(lib().lf_set_wait_limit(int(limit_ns)), "lf_set_wait_limit")
 
 
 def device_error() -> int:

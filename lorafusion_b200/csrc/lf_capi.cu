@@ -11,11 +11,13 @@
 #include <vector>
 
 #include "lf_internal.cuh"
+#include "lf_ptx.cuh"
 
 namespace lf {
 
-// Device status word written by bounded waits inside the kernels (one per device context).
-__device__ int g_device_status = 0;
+// Device control word (one per device context): the status bounded waits inside the kernels
+// record, and the wait limit they read.
+__device__ DeviceCtl g_device_ctl = {0, 0, kWaitLimitNs};
 
 namespace {
 
@@ -26,7 +28,7 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
 struct DeviceState {
   bool ready = false;
   int num_sms = 0;
-  int* status = nullptr;      // address of g_device_status on this device
+  int* status = nullptr;      // address of g_device_ctl.status on this device
   std::atomic<bool> no_cosched{false};  // the co-scheduled (cooperative) launch was refused here once
   std::atomic<int> refusal{0};          // the cudaError_t that refused launch returned
   std::vector<cudaEvent_t> events;  // lf_forward_host's stream-ordering events (grown on demand)
@@ -45,6 +47,16 @@ int default_cosched_mode() {
 }
 // process-wide switch (lf_set_co_scheduling): 0 off, 1 dedicated, 2 prologue
 std::atomic<int> g_cosched_mode{default_cosched_mode()};
+
+// Test hook (lf_inject_stale_ready): co-scheduled launches that still make their GEMM CTAs wait
+// for a ready value no shrink item publishes.
+std::atomic<int> g_stale_ready{0};
+uint64_t wait_generation(uint64_t gen) {
+  int n = g_stale_ready.load();
+  while (n > 0 && !g_stale_ready.compare_exchange_weak(n, n - 1)) {
+  }
+  return n > 0 ? gen + 2 : gen;
+}
 
 bool cosched_allowed(const DeviceState* ds) { return !ds->no_cosched.load() && g_cosched_mode.load() != 0; }
 
@@ -73,7 +85,7 @@ cudaError_t device_state(DeviceState** out) {
   if (!d.ready) {
     e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (e != cudaSuccess) return e;
-    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.status), g_device_status);
+    e = cudaGetSymbolAddress(reinterpret_cast<void**>(&d.status), g_device_ctl);
     if (e != cudaSuccess) return e;
     d.ready = true;
   }
@@ -305,6 +317,7 @@ int forward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_t
       sh.s_ext = workspace_dev;
       sh.unit_ready = reinterpret_cast<uint64_t*>(static_cast<char*>(workspace_dev) + sext_bytes(info));
       sh.gen = next_generation();
+      sh.wait_gen = wait_generation(sh.gen);
       sh.n_pairs = spare;
       sh.prologue = cosched_prologue();
       e = tc_gemm_pair(dt, false, maps, T, N, K, lora, tb, y_dev, N, ds->num_sms, st, &sh, &tail);
@@ -398,6 +411,22 @@ extern "C" int lf_backward_launch_count(const lf_problem* prob, const lf_plan_in
 extern "C" int lf_set_co_scheduling(int32_t enable) {
   if (enable < 0 || enable > 2) return LF_ERR_INVALID_ARG;
   g_cosched_mode.store(enable);
+  return LF_OK;
+}
+
+extern "C" int lf_set_wait_limit(uint64_t limit_ns) {
+  if (limit_ns != 0 && (limit_ns < 1000000ull || limit_ns > 60000000000ull)) return LF_ERR_INVALID_ARG;
+  const unsigned long long v = limit_ns == 0 ? kWaitLimitNs : limit_ns;
+  DeviceState* ds = nullptr;
+  if (device_state(&ds) != cudaSuccess) return LF_ERR_CUDA;
+  if (cudaMemcpyToSymbol(g_device_ctl, &v, sizeof(v), offsetof(DeviceCtl, wait_limit_ns)) != cudaSuccess)
+    return LF_ERR_CUDA;
+  return LF_OK;
+}
+
+extern "C" int lf_inject_stale_ready(int32_t launches) {
+  if (launches < 0) return LF_ERR_INVALID_ARG;
+  g_stale_ready.store(launches);
   return LF_OK;
 }
 
@@ -571,6 +600,7 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
         sh.s_ext = s_b;
         sh.unit_ready = reinterpret_cast<uint64_t*>(ws + 2 * sb);
         sh.gen = next_generation();
+        sh.wait_gen = wait_generation(sh.gen);
         sh.n_pairs = spare;
         sh.prologue = cosched_prologue();
         sh.job2 = !reuse_sf;
@@ -685,9 +715,11 @@ extern "C" int lf_device_error(int32_t* code) {
   if (device_state(&ds) != cudaSuccess) return LF_ERR_CUDA;
   if (cudaDeviceSynchronize() != cudaSuccess) return LF_ERR_CUDA;
   int v = 0;
-  if (cudaMemcpyFromSymbol(&v, g_device_status, sizeof(int)) != cudaSuccess) return LF_ERR_CUDA;
+  if (cudaMemcpyFromSymbol(&v, g_device_ctl, sizeof(int), offsetof(DeviceCtl, status)) != cudaSuccess)
+    return LF_ERR_CUDA;
   const int zero = 0;
-  if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)) != cudaSuccess) return LF_ERR_CUDA;
+  if (cudaMemcpyToSymbol(g_device_ctl, &zero, sizeof(int), offsetof(DeviceCtl, status)) != cudaSuccess)
+    return LF_ERR_CUDA;
   *code = v;
   return LF_OK;
 }

@@ -78,6 +78,7 @@ struct PairShrink {
   void* s_ext;           // two K-half planes written by the launch, job 1
   uint64_t* unit_ready;  // [2*n_units] ready flags of job 1 (then [2*n_units] of job 2)
   uint64_t gen;          // value the flags take in this launch
+  uint64_t wait_gen;     // value the GEMM CTAs wait for (gen; a test hook makes it one nobody writes)
   int n_pairs;           // CTA pairs given to the shrink (dedicated mode)
   bool prologue;         // instead: every CTA runs its share of the shrink before its GEMM tiles
   bool job2;             // second job present

@@ -6,6 +6,7 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <stddef.h>
 #include <stdint.h>
 
 namespace lf {
@@ -21,6 +22,19 @@ enum DeviceErr : int {
 
 // ~1 s of wall time: far above any legitimate wait in these kernels.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+// The library's per-device control word: kernels get the address of `status` (Tables::err) and
+// read the wait limit beside it, so a host can shorten every bounded wait (lf_set_wait_limit).
+struct DeviceCtl {
+  int status;                        // first error code a kernel recorded (0: none)
+  int reserved;
+  unsigned long long wait_limit_ns;  // bound of every wait; read only once a wait did not succeed at once
+};
+static_assert(offsetof(DeviceCtl, status) == 0, "Tables::err points at the control word");
+
+__device__ __forceinline__ uint64_t wait_limit(const int* err) {
+  return err ? reinterpret_cast<const volatile DeviceCtl*>(err)->wait_limit_ns : kWaitLimitNs;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -83,10 +97,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
                                           int err_code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit(err);
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) return true;
     if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit) {
       record_error(err, err_code);
       *abort_flag = 1;
       return false;

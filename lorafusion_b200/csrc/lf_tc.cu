@@ -81,8 +81,9 @@ __device__ __forceinline__ void pack8_hi_lo(const float* v, uint4& pk_hi, uint4&
 // Time-bounded wait used only while unwinding after an abort: ignores the abort flag.
 __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* err) {
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit(err);
   while (!mbar_try_wait_sleep(bar, parity, kWaitSleepNs)) {
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > limit) {
       record_error(err, kErrTimeoutDrain);
       return;
     }
@@ -382,6 +383,13 @@ constexpr int kPairOutBytes = 4 * 2 * 32 * 64 * 2;  // epilogue staging: 4 warps
 // <= 64 rows of packed A (8 KB): more bytes in flight per SM while it competes with the GEMM.
 constexpr int kRoleStageBytes = kPairABytes + 64 * kBK * 2;
 constexpr int kRoleStages = 9;
+// Accumulation chains of one shrink item: K step i of the item goes to accumulator i % chains and
+// the epilogue adds the chains in fixed order.  A tcgen05 fp32 accumulation adds an error of
+// about 2^-25 of the running sum per MMA, with a bias that does not average out, so a sum over
+// thousands of K steps (K = 28672 is 1792 of them) loses ~1e-4 relative; c chains cut that c-fold
+// (each chain's sum is shorter and smaller, and their errors have independent signs).
+constexpr int kRoleChains = 4;                   // x 2 accumulator buffers x 64 columns = 512
+constexpr int kShrChains = 8;                    // standalone shrink: 8 x 64 columns = 512
 constexpr int kPairBars = kRoleStages;  // barrier array length shared by both roles
 static_assert(kRoleStages * kRoleStageBytes <= kPairStages * (kPairABytes + kPairBBytes) + kPairOutBytes,
               "shrink-role stages must fit the pair kernel's shared memory");
@@ -421,6 +429,7 @@ struct PairParams {
   void* s_ext;
   uint64_t* unit_ready;  // one flag per (unit, K half) item
   uint64_t gen;
+  uint64_t ready_gen;    // value GEMM CTAs wait for on unit_ready: gen (a test hook may change it)
   // S_ext planes the LoRA stages sum: 1 = the full product; 2 = two K-half partial products
   // (written by the co-scheduled shrink), plane p starting at S map row p * s_plane_rows
   int s_planes, s_plane_rows;
@@ -492,9 +501,10 @@ __device__ __forceinline__ bool wait_units_ready(const uint64_t* ready, int u0, 
   for (int u = u0; u < u1; ++u) {
     if (ld_acquire_u64(ready + u) == gen) continue;
     const uint64_t t0 = globaltimer_ns();
+    const uint64_t limit = wait_limit(err);
     while (ld_acquire_u64(ready + u) != gen) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > limit) {
         record_error(err, kErrTimeoutFlag);
         *abort_flag = 1;
         return false;
@@ -548,7 +558,7 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
   }
   if (warp == 1) {
     __syncwarp();
-    tmem_alloc(tmem_slot, 128);
+    tmem_alloc(tmem_slot, 2 * kRoleChains * 64);
     if (!kPrologue) tmem_relinquish();
   }
   tc_fence_before();
@@ -618,8 +628,9 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
           break;
         }
         tc_fence_after();
-        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * 64);
-        uint32_t acc = 0;
+        const uint32_t d = tmem_base + static_cast<uint32_t>(buf * kRoleChains * 64);
+        uint32_t started = 0;  // chains holding a partial sum
+        int step = 0;
         const int kb_end = min(nkb, (h + 1) * nkb_half);
         for (int kb = h * nkb_half; kb < kb_end; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, tb.err, kErrTimeoutFull)) {
@@ -629,9 +640,11 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
           tc_fence_after();
           const uint32_t a0 = a_base + stage * kRoleStageBytes, b0 = a0 + kPairABytes;
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            umma_f16(d, umma_sdesc(a0 + k * 32, 16, 1024, 2), umma_sdesc(b0 + k * 32, 16, 1024, 2), idesc, acc);
-            acc = 1;
+          for (int k = 0; k < kBK / 16; ++k, ++step) {
+            const int ch = step % kRoleChains;
+            umma_f16(d + ch * 64, umma_sdesc(a0 + k * 32, 16, 1024, 2), umma_sdesc(b0 + k * 32, 16, 1024, 2), idesc,
+                     (started >> ch) & 1u);
+            started |= 1u << ch;
           }
           issued_any = true;
           umma_commit(&empty[stage]);
@@ -676,9 +689,12 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
         sc[j] = tb.st_scale(st);
       }
       const int buf = it & 1;
+      // chains the MMA thread started for this item (4 K steps per k-block)
+      const int n_ch = has_k ? min(kRoleChains, 4 * (min(nkb, (h + 1) * nkb_half) - h * nkb_half)) : 0;
       if (!warp_wait(&tfull[buf], (it >> 1) & 1, abort_flag, tb.err, kErrTimeoutAcc)) break;
       tc_fence_after();
-      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * 64);
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * kRoleChains * 64);
       for (int j = 0; j < nst; ++j) {
         const bool in = has_k && row >= (j == 0 ? lo[0] : j == 1 ? lo[1] : j == 2 ? lo[2] : lo[3]) &&
                         row < (j == 0 ? hi[0] : j == 1 ? hi[1] : j == 2 ? hi[2] : hi[3]);
@@ -686,12 +702,18 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
         OutT* dst = s_out + h * plane_elems + (static_cast<int64_t>(st0 + j) * kBM + row) * r_pad;
         OutT* dst_lo = dst + 2 * plane_elems;
         for (int c = 0; c < r_pad; c += 16) {
-          uint32_t v[16];
-          tmem_ld16(tbase + j * r_pad + c, v);
-          tmem_wait_ld();
           float f[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) f[e] = in ? scale * __uint_as_float(v[e]) : 0.f;
+          for (int e = 0; e < 16; ++e) f[e] = 0.f;
+          for (int ch = 0; ch < n_ch; ++ch) {  // chains added in fixed order
+            uint32_t v[16];
+            tmem_ld16(tbase + ch * 64 + j * r_pad + c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) f[e] += __uint_as_float(v[e]);
+          }
+#pragma unroll
+          for (int e = 0; e < 16; ++e) f[e] = in ? scale * f[e] : 0.f;
           uint4 hi0, lo0, hi1, lo1;
           pack8_hi_lo<OutT>(f, hi0, lo0);
           pack8_hi_lo<OutT>(f + 8, hi1, lo1);
@@ -727,7 +749,7 @@ __device__ __forceinline__ void pair_shrink_role(const PairParams& prm, const CU
   if (!kPrologue) cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 128);
+    tmem_dealloc(tmem_base, 2 * kRoleChains * 64);
   }
   if (kPrologue) __syncthreads();
 }
@@ -849,7 +871,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           it1 = 2 * ld_early(tb.base + tb.off_tile_unit + min(2 * mp + 2, tb.n_tiles));
           fl[0] = ld_relaxed_u64(prm.unit_ready);
 #pragma unroll
-          for (int q = 0; q < 8; ++q) fl[q + 1] = it0 + q < it1 ? ld_relaxed_u64(prm.unit_ready + it0 + q) : prm.gen;
+          for (int q = 0; q < 8; ++q)
+            fl[q + 1] = it0 + q < it1 ? ld_relaxed_u64(prm.unit_ready + it0 + q) : prm.ready_gen;
         }
         for (int kb = un.kb0; kb < un.kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, tb.err, kErrTimeoutEmpty)) {
@@ -891,11 +914,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if ((prm.n_shrink_pairs > 0 || prm.shrink_prologue) && pe > pb) {  // S_ext of both row tiles (and the zero block) published?
           bool seen = it1 - it0 <= 8;
 #pragma unroll
-          for (int q = 0; q < 9; ++q) seen = seen && fl[q] == prm.gen;
+          for (int q = 0; q < 9; ++q) seen = seen && fl[q] == prm.ready_gen;
           if (seen) {
             fence_acquire_gpu();  // the early loads saw every release: acquire them
-          } else if (!wait_units_ready(prm.unit_ready, 0, 1, prm.gen, abort_flag, tb.err) ||
-                     !wait_units_ready(prm.unit_ready, it0, it1, prm.gen, abort_flag, tb.err)) {
+          } else if (!wait_units_ready(prm.unit_ready, 0, 1, prm.ready_gen, abort_flag, tb.err) ||
+                     !wait_units_ready(prm.unit_ready, it0, it1, prm.ready_gen, abort_flag, tb.err)) {
             ok = false;
           }
           fence_proxy_async_global();
@@ -1190,7 +1213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 1) {
     __syncwarp();
-    tmem_alloc(tmem_slot, 64);
+    tmem_alloc(tmem_slot, kShrChains * 64);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -1237,7 +1260,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true, issued_any = false;
       const uint32_t idesc = umma_idesc_f16(kBM, N, prm.ab_fmt, 0, 0);
       const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
-      uint32_t acc = 0;
+      uint32_t started = 0;  // accumulation chains holding a partial sum
+      int step = 0;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag, prm.tb.err, kErrTimeoutFull)) {
           ok = false;
@@ -1246,9 +1270,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t a0 = a_base + stage * kShrABytes, b0 = b_base + stage * kShrBBytes;
 #pragma unroll
-        for (int k = 0; k < kBK / 16; ++k) {
-          umma_f16(tmem_base, umma_sdesc(a0 + k * 32, 16, 1024, 2), umma_sdesc(b0 + k * 32, 16, 1024, 2), idesc, acc);
-          acc = 1;
+        for (int k = 0; k < kBK / 16; ++k, ++step) {
+          const int ch = step % kShrChains;
+          umma_f16(tmem_base + ch * 64, umma_sdesc(a0 + k * 32, 16, 1024, 2), umma_sdesc(b0 + k * 32, 16, 1024, 2),
+                   idesc, (started >> ch) & 1u);
+          started |= 1u << ch;
         }
         issued_any = true;
         umma_commit(&empty[stage]);
@@ -1273,12 +1299,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok && has_k) {
       tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+      const int n_ch = min(kShrChains, 4 * (kb1 - kb0));
       for (int c = 0; c < N; c += 16) {
-        uint32_t v[16];
-        tmem_ld16(tbase + c, v);
-        tmem_wait_ld();
+        float f[16];
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) partial[(c + jj) * kPartLd + row] = __uint_as_float(v[jj]);
+        for (int jj = 0; jj < 16; ++jj) f[jj] = 0.f;
+        for (int ch = 0; ch < n_ch; ++ch) {  // chains added in fixed order
+          uint32_t v[16];
+          tmem_ld16(tbase + ch * 64 + c, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) f[jj] += __uint_as_float(v[jj]);
+        }
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) partial[(c + jj) * kPartLd + row] = f[jj];
       }
     } else {
       for (int c = 0; c < N; ++c) partial[c * kPartLd + row] = 0.f;
@@ -1326,7 +1360,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 64);
+    tmem_dealloc(tmem_base, kShrChains * 64);
   }
 }
 
@@ -1936,6 +1970,7 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
     p.s_ext = shrink->s_ext;
     p.unit_ready = shrink->unit_ready;
     p.gen = shrink->gen;
+    p.ready_gen = shrink->wait_gen;
     a_map = &shrink->a_map;
     if (shrink->job2) {
       p.job2 = 1;
@@ -2073,8 +2108,11 @@ cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables
   if (p.n_stages > kGramMaxStages) p.n_stages = kGramMaxStages;
   const int fmt = dtype == LF_BF16 ? 1 : 0;
   const int width = planes * tb.r_pad;  // MMA N
+  // at least two accumulation chains (rotating over K steps, added in fixed order: see kRoleChains)
+  // where they fit, then two accumulator buffers where they fit
   p.chains = 4;
-  while (p.chains > 1 && 2 * p.chains * width > 512) p.chains >>= 1;
+  while (p.chains > 2 && 2 * p.chains * width > 512) p.chains >>= 1;
+  while (p.chains > 1 && p.chains * width > 512) p.chains >>= 1;
   p.acc_cols = p.chains * width;
   p.tmem_cols = 512;  // one CTA per SM: the whole TMEM, as many accumulators as fit
   p.n_bufs = p.tmem_cols / p.acc_cols;

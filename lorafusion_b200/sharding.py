@@ -142,13 +142,18 @@ def allreduce_spanning_grads(plan: ShardPlan, grad_a: dict[int, torch.Tensor], g
     Every rank packs the spanning adapters in ascending id order into one
     float32 buffer (zeros for adapters it does not hold), runs one
     ``all_reduce(SUM)`` and unpacks; afterwards every rank holds the full
-    gradient of each spanning adapter (inserted if it had none).
+    gradient of each spanning adapter (inserted if it had none).  Pass the
+    gradients of ``fused_lora_backward(..., grad_dtype=torch.float32)`` to sum
+    unrounded partials; bf16 ones are widened first.  With a gloo group the
+    buffer lives in host memory.
     """
     import torch.distributed as dist
 
     if not plan.spanning or plan.world_size == 1:
         return
     K, N = in_features, out_features
+    if dist.get_backend(group) == "gloo":
+        device = torch.device("cpu")
     sizes = [ranks[a] * (K + N) for a in plan.spanning]
     buf = torch.zeros(sum(sizes), dtype=torch.float32, device=device)
     dst, src, off = [], [], 0

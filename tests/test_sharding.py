@@ -167,3 +167,56 @@ def test_only_adapters_larger_than_a_share_span():
     _, packing = _packing(counts, wl.tile_capacity)
     plan = assign_bins(packing.bins, 8)
     assert len(plan.spanning) <= 8 + sum(c > 4096 for c in counts)
+
+
+def _failing_worker(rank, world, port, result_q):
+    """Rank 1 raises before the gradient all-reduce (a failed step); rank 0 must get an error from
+    its collective, bounded by the group's short timeout, not hang."""
+    import datetime
+    import time
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    counts = [300, 90, 60, 33, 20, 9]
+    _, packing = _packing(counts, 64)
+    plan = assign_bins(packing.bins, world)
+    ranks = {i: 4 for i in range(len(counts))}
+    K, N = 16, 8
+    ga = {a: torch.ones(4, K) for a in plan.spanning}
+    gb = {a: torch.ones(N, 4) for a in plan.spanning}
+    dist.barrier()
+    if rank == 1:
+        result_q.put((rank, "raised", 0.0))
+        raise SystemExit(3)  # the failing rank leaves between steps, with nothing in flight
+    t0 = time.monotonic()
+    try:
+        allreduce_spanning_grads(plan, ga, gb, ranks, K, N, torch.device("cpu"))
+        outcome = "no error"
+    except Exception as e:  # noqa: BLE001 - the collective's error type depends on the backend
+        outcome = f"error: {type(e).__name__}"
+    result_q.put((rank, outcome, time.monotonic() - t0))
+
+
+def test_rank_failure_before_allreduce_is_reported_not_hung():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        r, outcome, dt = q.get(timeout=120)
+        results[r] = (outcome, dt)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert results[1][0] == "raised"
+    assert results[0][0].startswith("error"), results
+    assert results[0][1] < 60.0, results
+    assert procs[1].exitcode == 3
