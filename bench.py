@@ -1,31 +1,40 @@
 #!/usr/bin/env python
-"""Benchmark of the fused multi-adapter LoRA forward on B200 (one process per GPU).
+"""Benchmark of the fused multi-adapter LoRA op on B200 (one process per GPU).
 
-Workload (default): one bf16 projection 4096 -> 4096, 16 adapters of rank 16,
-4096 tokens per GPU whose per-adapter row counts follow Zipf(1.1), packed into
-128-row bins by the scheduler.  With N GPUs the global batch holds N x 4096
-tokens; every rank computes the same packing and takes whole bins (weak
-scaling: fixed work per GPU, no communication in the forward).
+Headline workload (default, cfg2): one bf16 projection 4096 -> 4096, 16 adapters of rank 16,
+4096 tokens per GPU whose per-adapter row counts follow Zipf(1.1), packed into 128-row bins by
+the scheduler.  With N GPUs the global batch holds N x 4096 tokens; every rank computes the same
+packing and takes its rows (weak scaling: fixed work per GPU, no communication in the forward).
 
 Printed by rank 0, one JSON line:
-  value        whole-job tokens/s of the forward with inputs resident in HBM, CUDA
-               events around each step (routed shrink + fused base GEMM/LoRA expand),
-               L2 flushed (256 MiB write) before every step, max over ranks
-  e2e          the same through the public plugin call (b200_ops.fused_lora_forward)
-               with pinned host buffers: host->device copy of x, the op, device->host
-               copy of y inside the timed region
-  roofline     the fused GEMM kernel: algorithmic FLOPs / its event-timed duration
-               against the measured bf16 peak; the shrink's HBM figure alongside
-  cpu_baseline the CPU oracle (numpy float32 restatement of the reference op) on the
-               host cores, rank 0 at N=1, a bounded sample of the same workload
+  value        whole-job tokens/s of the forward with inputs resident in HBM, CUDA events around
+               each step (routed shrink + fused base GEMM/LoRA expand), L2 flushed (256 MiB write)
+               before every step, max over ranks
+  e2e          the same through the public host-batch call (b200_ops.fused_lora_forward_host):
+               pinned host x in, pinned host y out, timed by the host wall clock from before the
+               call to after the stream synchronize, max over ranks
+  roofline     the fused GEMM kernel: algorithmic FLOPs / its event-timed duration against the
+               measured bf16 peak
+  backward     the backward's stages as launches of their own (routed shrinks, grad_x GEMM, dA/dB
+               grams), event-timed, and the grams' HBM roofline
+  fwd_bwd      forward + backward through the plugin calls (+ the all-reduce of spanning adapters'
+               gradients at N > 1)
+  workloads    cfg3 (Llama-3-8B projections, 64 mixed-rank adapters) and cfg5 (70B projections,
+               256 adapters of rank 64): forward + backward over every projection per step, the
+               workload's tokens split over the N GPUs (strong scaling), all-reduce included
+  cpu_baseline the CPU oracle (numpy float32 restatement of the reference op) on the host cores,
+               rank 0 at N = 1, a bounded sample of the same workload
 
-``--impl reference`` times that CPU restatement of the reference's op instead.
+``--impl reference`` times that CPU restatement of the reference's op instead, on the same global
+token count; it imports nothing of this package (the workload shapes are read from the plain file
+lorafusion_b200/workloads.py, the layout comes from oracle/scheduler_oracle.py).
 """
 
 from __future__ import annotations
 
 import argparse
 import datetime
+import importlib.util
 import json
 import math
 import os
@@ -35,13 +44,18 @@ import sys
 import threading
 import time
 
+import numpy as np
+
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 METRIC = "fused LoRA tokens/sec/GPU fwd & fwd+bwd; % bf16 roofline; 1/2/4/8 GPU"
 WORKLOAD = "cfg2_h4096_a16_r16"
-FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+EXTRA = "cfg3_llama8b_a64_mixed,cfg5_70b_a256_r64"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_FLUSH_BYTES = 256 << 20
+# bounded CPU samples of the multi-projection workloads: leading rows of the packed global batch
+CPU_SAMPLE_ROWS = {"cfg3_llama8b_a64_mixed": 512, "cfg5_70b_a256_r64": 128}
 
 
 def parse_args():
@@ -51,12 +65,24 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", default=WORKLOAD)
+    ap.add_argument("--extra", default=EXTRA, help="comma-separated fwd+bwd workloads timed after the headline "
+                                                   "(all projections, strong scaling); 'none' to skip")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-fwd-bwd", action="store_true")
     ap.add_argument("--separate-launches", action="store_true",
-                    help="shrink and fused GEMM as two ordinary launches (profilers refuse the cooperative one)")
+                    help="no cooperative launches (profilers refuse them): shrinks as launches of their own")
     return ap.parse_args()
+
+
+def load_workloads_module():
+    """lorafusion_b200/workloads.py loaded as a plain file (numpy only), not through the package."""
+    spec = importlib.util.spec_from_file_location("lf_workload_shapes", os.path.join(REPO, "lorafusion_b200",
+                                                                                       "workloads.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod
+    spec.loader.exec_module(mod)
+    return mod
 
 
 def load_peaks():
@@ -64,7 +90,9 @@ def load_peaks():
     try:
         with open(path) as f:
             p = json.load(f)
-        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]), "source": "measured"}
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "measured"}
     except (OSError, KeyError, ValueError):
         return dict(FALLBACK_PEAKS, source="fallback")
 
@@ -80,6 +108,19 @@ def load_traffic(kernel: str, workload: str):
     except OSError:
         pass
     return None
+
+
+def repo_libraries_mapped() -> list[str]:
+    """Shared libraries of this repository mapped into the process (evidence of which code ran)."""
+    out = set()
+    try:
+        for line in open("/proc/self/maps"):
+            path = line.split()[-1] if len(line.split()) >= 6 else ""
+            if path.startswith(REPO) and ".so" in os.path.basename(path):
+                out.add(os.path.relpath(path, REPO))
+    except OSError:
+        pass
+    return sorted(out)
 
 
 class ClockSampler:
@@ -137,86 +178,21 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-# --------------------------------------------------------------------------- workload
-def global_layout(wl, n_gpus: int):
-    from lorafusion_b200.scheduler import Request, bucket_by_adapter, greedy_pack
-    from lorafusion_b200.workloads import row_counts
-    counts = row_counts(wl, wl.total_rows * n_gpus)
-    requests = [Request(i, i, c) for i, c in enumerate(counts)]
-    groups = bucket_by_adapter(requests)
-    packing = greedy_pack({g.adapter_id: g.total_rows for g in groups}, wl.tile_capacity)
-    return packing
-
-
-def local_problem(wl, n_gpus: int, rank: int, device):
-    import torch
-    from lorafusion_b200.config import AdapterSpec
-    from lorafusion_b200.sharding import assign_bins, local_layout
-    from lorafusion_b200.workloads import adapter_ranks
-    packing = global_layout(wl, n_gpus)
-    plan = assign_bins(packing.bins, n_gpus)
-    rows, routing = local_layout(plan, packing.bins, rank, wl.tile_capacity)
-    _, K, N = wl.projections[0]
-    ranks = adapter_ranks(wl)
-    g = torch.Generator(device=device).manual_seed(1000 + rank)
-    gw = torch.Generator(device=device).manual_seed(0)
-    T = len(rows)
-    x = torch.randn(T, K, device=device, generator=g).to(torch.bfloat16)
-    grad = torch.randn(T, N, device=device, generator=g).to(torch.bfloat16)
-    w = (torch.randn(N, K, device=device, generator=gw) / math.sqrt(K)).to(torch.bfloat16)
-    lora_a = {i: (torch.randn(r, K, device=device, generator=gw) / math.sqrt(K)).to(torch.bfloat16)
-              for i, r in enumerate(ranks)}
-    lora_b = {i: (0.02 * torch.randn(N, r, device=device, generator=gw)).to(torch.bfloat16)
-              for i, r in enumerate(ranks)}
-    adapters = {i: AdapterSpec(i, r, float(2 * r), K, N) for i, r in enumerate(ranks)}
-    return dict(x=x, grad=grad, w=w, lora_a=lora_a, lora_b=lora_b, adapters=adapters, routing=routing,
-                plan=plan, T=T, K=K, N=N, global_T=sum(e - s for s, e in plan.bin_rows), ranks=ranks)
-
-
-def algorithmic_counts(routing, ranks, K, N, T):
-    R = sum((r.row_end - r.row_start) * ranks[r.adapter_id] for r in routing.routes)
-    active = sorted({r.adapter_id for r in routing.routes})
+def algorithmic_counts(routes, ranks, K, N, T):
+    """Per-launch algorithmic work: routes are (start, end, adapter) triples."""
+    R = sum((e - s) * ranks[a] for s, e, a in routes)
+    active = sorted({a for s, e, a in routes if e > s})
+    rsum = sum(ranks[a] for a in active)
     gemm_flops = 2.0 * T * K * N + 2.0 * R * N
     shrink_flops = 2.0 * R * K
-    shrink_bytes = T * K * 2 + sum(ranks[a] * K * 2 for a in active) + R * 2
+    shrink_bytes = T * K * 2 + rsum * K * 2 + R * 2
+    gram_bytes = T * K * 2 + T * N * 2 + 2 * R * 2 + rsum * (K + N) * 4
     return dict(R=R, gemm_flops=gemm_flops, shrink_flops=shrink_flops, shrink_bytes=shrink_bytes,
-                fwd_flops=gemm_flops + shrink_flops, fwdbwd_flops=4.0 * T * K * N + 6.0 * R * (K + N))
+                gram_bytes=gram_bytes, fwd_flops=gemm_flops + shrink_flops,
+                fwdbwd_flops=4.0 * T * K * N + 6.0 * R * (K + N))
 
 
-# --------------------------------------------------------------------------- CPU oracle timing
-def cpu_oracle_sample(wl, budget_s: float, max_steps: int | None = None):
-    """Time the numpy restatement of the reference forward on full workload batches."""
-    import numpy as np
-    from oracle import mock_oracle
-    from lorafusion_b200.workloads import adapter_ranks
-    packing = global_layout(wl, 1)
-    routes, cur = [], 0
-    for entries in packing.bins:
-        for a, n in entries:
-            routes.append((cur, cur + n, a))
-            cur += n
-    _, K, N = wl.projections[0]
-    rng = np.random.default_rng(0)
-    x = mock_oracle.bf16_round(rng.standard_normal((cur, K), dtype=np.float32))
-    w = mock_oracle.bf16_round(rng.standard_normal((N, K), dtype=np.float32) / np.sqrt(K))
-    ranks = adapter_ranks(wl)
-    a = {i: mock_oracle.bf16_round(rng.standard_normal((r, K), dtype=np.float32) / np.sqrt(K))
-         for i, r in enumerate(ranks)}
-    b = {i: mock_oracle.bf16_round(0.02 * rng.standard_normal((N, r), dtype=np.float32)) for i, r in enumerate(ranks)}
-    sc = {i: 2.0 for i in range(len(ranks))}
-    times = []
-    t_start = time.perf_counter()
-    while True:
-        t0 = time.perf_counter()
-        mock_oracle.fused_lora_forward(x, w, a, b, sc, routes)
-        times.append(time.perf_counter() - t0)
-        if max_steps is not None and len(times) >= max_steps:
-            break
-        if max_steps is None and time.perf_counter() - t_start > budget_s:
-            break
-    return cur, times
-
-
+# =============================================================================== CPU (oracle) side
 def cpu_threads() -> int:
     try:
         from threadpoolctl import threadpool_info
@@ -228,44 +204,188 @@ def cpu_threads() -> int:
     return os.cpu_count() or 1
 
 
-# --------------------------------------------------------------------------- reference arm
+def use_all_host_cores():
+    """BLAS threads = the host's cores (torchrun sets OMP_NUM_THREADS=1 in every rank)."""
+    try:
+        from threadpoolctl import threadpool_limits
+        return threadpool_limits(limits=os.cpu_count() or 1, user_api="blas")
+    except Exception:  # noqa: BLE001
+        return None
+
+
+def oracle_layout(wlm, wl, total_rows):
+    """The packed global batch's routes from the oracle's scheduler restatement."""
+    from oracle.scheduler_oracle import bucket_rows, greedy_bins
+    counts = wlm.row_counts(wl, total_rows)
+    bins = greedy_bins(bucket_rows([(i, i, c) for i, c in enumerate(counts)]), wl.tile_capacity)
+    routes, cur = [], 0
+    for entries in bins:
+        for a, n in entries:
+            routes.append((cur, cur + n, a))
+            cur += n
+    return routes, cur
+
+
+def leading_routes(routes, n):
+    return [(s, min(e, n), a) for s, e, a in routes if s < n]
+
+
+class OracleProblem:
+    """bf16-rounded float32 inputs of one projection for the numpy oracle (adapters in `routes` only).
+    ``tiled_w``: the base weight repeats one random 256-row block (its values do not change the
+    oracle's arithmetic work; generating a 28672 x 8192 matrix would dominate a short sample)."""
+
+    def __init__(self, rng, T, K, N, ranks, routes, with_grad, tiled_w=False):
+        from oracle import mock_oracle
+        r16 = mock_oracle.bf16_round
+        self.x = r16(rng.standard_normal((T, K), dtype=np.float32))
+        if tiled_w and N > 256:
+            blk = r16(rng.standard_normal((256, K), dtype=np.float32) / np.float32(math.sqrt(K)))
+            self.w = np.ascontiguousarray(np.tile(blk, (-(-N // 256), 1))[:N])
+        else:
+            self.w = r16(rng.standard_normal((N, K), dtype=np.float32) / np.float32(math.sqrt(K)))
+        ids = sorted({a for _, _, a in routes})
+        self.a = {i: r16(rng.standard_normal((ranks[i], K), dtype=np.float32) / np.float32(math.sqrt(K))) for i in ids}
+        self.b = {i: r16(np.float32(0.02) * rng.standard_normal((N, ranks[i]), dtype=np.float32)) for i in ids}
+        self.g = r16(rng.standard_normal((T, N), dtype=np.float32)) if with_grad else None
+        self.sc = {i: 2.0 for i in ids}
+        self.routes = routes
+
+    def forward(self):
+        from oracle import mock_oracle
+        return mock_oracle.fused_lora_forward(self.x, self.w, self.a, self.b, self.sc, self.routes)
+
+    def backward(self):
+        from oracle import mock_oracle
+        return mock_oracle.fused_lora_backward(self.g, self.x, self.w, self.a, self.b, self.sc, self.routes)
+
+
+def cpu_headline_sample(wlm, wl, n_gpus, steps=None, budget_s=None, with_grad=False):
+    """Times of full forwards of the global batch (N x tokens per GPU) by the numpy oracle."""
+    routes, T = oracle_layout(wlm, wl, wl.total_rows * n_gpus)
+    _, K, N = wl.projections[0]
+    pb = OracleProblem(np.random.default_rng(0), T, K, N, wlm.adapter_ranks(wl), routes, with_grad)
+    times = []
+    t_start = time.perf_counter()
+    while True:
+        t0 = time.perf_counter()
+        pb.forward()
+        times.append(time.perf_counter() - t0)
+        if steps is not None and len(times) >= steps:
+            break
+        if steps is None and time.perf_counter() - t_start > budget_s:
+            break
+    return T, times, pb
+
+
+def cpu_workload_sample(wlm, wl, steps):
+    """Forward + backward over every projection of the leading CPU_SAMPLE_ROWS rows of the packed batch."""
+    routes, _ = oracle_layout(wlm, wl, wl.total_rows)
+    n = CPU_SAMPLE_ROWS.get(wl.name, 256)
+    sroutes = leading_routes(routes, n)
+    ranks = wlm.adapter_ranks(wl)
+    rng = np.random.default_rng(1)
+    probs = [OracleProblem(rng, n, K, N, ranks, sroutes, True, tiled_w=True) for _, K, N in wl.projections]
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        for pb in probs:
+            pb.forward()
+            pb.backward()
+        times.append(time.perf_counter() - t0)
+    return n, times
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
-        return 0
-    from lorafusion_b200.workloads import WORKLOADS
-    wl = WORKLOADS[args.workload]
-    T, warm = cpu_oracle_sample(wl, 0.0, max_steps=max(1, args.warmup))
-    _, times = cpu_oracle_sample(wl, 0.0, max_steps=args.steps)
+        return 0  # rank 0 alone times the CPU arm; the other ranks exit without work
+    limiter = use_all_host_cores()  # noqa: F841 - keeps the BLAS thread limit in force
+    wlm = load_workloads_module()
+    wl = wlm.WORKLOADS[args.workload]
+    n_gpus = args.gpus
+    _, _, _ = cpu_headline_sample(wlm, wl, n_gpus, steps=max(1, args.warmup))
+    T, times, pb = cpu_headline_sample(wlm, wl, n_gpus, steps=args.steps, with_grad=not args.no_fwd_bwd)
     ms = 1e3 * statistics.mean(times)
     value = T / (ms / 1e3)
     cores = cpu_threads()
     _, K, N = wl.projections[0]
+    fwd_bwd = None
+    if not args.no_fwd_bwd:
+        fb = []
+        for _ in range(2):  # bounded: two full forward + backward steps of the global batch
+            t0 = time.perf_counter()
+            pb.forward()
+            pb.backward()
+            fb.append(time.perf_counter() - t0)
+        fwd_bwd = {"value": T / statistics.mean(fb), "unit": "tokens/s", "ms_per_step": 1e3 * statistics.mean(fb),
+                   "sample": f"2 full forward+backward steps of {T} tokens"}
+    workloads = {}
+    for name in [e for e in args.extra.split(",") if e and e != "none"]:
+        wx = wlm.WORKLOADS[name]
+        n, wt = cpu_workload_sample(wlm, wx, steps=2)
+        workloads[name] = {"value": n / statistics.mean(wt), "unit": "tokens/s", "ms_per_step":
+                           1e3 * statistics.mean(wt), "pass": "forward+backward, every projection",
+                           "sample": f"leading {n} rows of the packed {wx.total_rows}-token batch, 2 steps "
+                                     "(base weights: one random 256-row block repeated)"}
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": n_gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": args.workload, "tokens_per_step": T, "in_features": K, "out_features": N,
-                   "adapters": wl.n_adapters, "rank": 16, "tile_rows": wl.tile_capacity,
+        "config": {"workload": args.workload, "tokens_per_gpu": wl.total_rows, "global_tokens": T,
+                   "in_features": K, "out_features": N, "adapters": wl.n_adapters, "rank": wl.rank_choices[0],
+                   "tile_rows": wl.tile_capacity,
                    "what": "numpy float32 restatement of lorafusion mock_ops.fused_lora_forward on bf16-rounded "
-                           "inputs, host cores, one full 4096-token forward per step"},
+                           "inputs, host cores, one full forward of the global batch per step"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"{args.steps} full forwards of {T} tokens"},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "fwd_bwd": fwd_bwd,
+        "workloads": workloads,
+        "repo_libraries_mapped": repo_libraries_mapped(),
+        "lorafusion_b200_imported": any(m == "lorafusion_b200" or m.startswith("lorafusion_b200.")
+                                        for m in sys.modules),
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
-# --------------------------------------------------------------------------- our arm
+# =============================================================================== GPU side
+def global_packing(wl, total_rows):
+    from lorafusion_b200.scheduler import Request, bucket_by_adapter, greedy_pack
+    from lorafusion_b200.workloads import row_counts
+    counts = row_counts(wl, total_rows)
+    requests = [Request(i, i, c) for i, c in enumerate(counts)]
+    groups = bucket_by_adapter(requests)
+    return greedy_pack({g.adapter_id: g.total_rows for g in groups}, wl.tile_capacity)
+
+
+def rank_projection(wl, projection, rows, routing, ranks, device, seed):
+    """On-device bf16 tensors of one projection for a rank's rows (x, grad, W, adapters)."""
+    import torch
+    from lorafusion_b200.config import AdapterSpec
+    _, K, N = wl.projections[projection]
+    g = torch.Generator(device=device).manual_seed(seed)
+    gw = torch.Generator(device=device).manual_seed(1000 + projection)
+    T = len(rows)
+    bf = torch.bfloat16
+    x = torch.randn(T, K, device=device, generator=g, dtype=bf)
+    grad = torch.randn(T, N, device=device, generator=g, dtype=bf)
+    w = (torch.randn(N, K, device=device, generator=gw) / math.sqrt(K)).to(bf)
+    lora_a = {i: (torch.randn(r, K, device=device, generator=gw) / math.sqrt(K)).to(bf) for i, r in enumerate(ranks)}
+    lora_b = {i: (0.02 * torch.randn(N, r, device=device, generator=gw)).to(bf) for i, r in enumerate(ranks)}
+    adapters = {i: AdapterSpec(i, r, float(2 * r), K, N) for i, r in enumerate(ranks)}
+    return dict(x=x, grad=grad, w=w, lora_a=lora_a, lora_b=lora_b, adapters=adapters, routing=routing, T=T, K=K, N=N)
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
 
     from lorafusion_b200 import _native as nat
     from lorafusion_b200 import b200_ops
-    from lorafusion_b200.sharding import allreduce_spanning_grads
-    from lorafusion_b200.workloads import WORKLOADS
+    from lorafusion_b200.sharding import allreduce_spanning_grads, assign_bins, local_layout
+    from lorafusion_b200.workloads import WORKLOADS, adapter_ranks
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -292,9 +412,15 @@ def run_ours(args):
     if args.separate_launches:
         b200_ops.use_cooperative_launch(False)
     wl = WORKLOADS[args.workload]
-    pr = local_problem(wl, world, rank, device)
+    ranks = adapter_ranks(wl)
+    packing = global_packing(wl, wl.total_rows * world)
+    plan = assign_bins(packing.bins, world)
+    rows, routing = local_layout(plan, packing.bins, rank, wl.tile_capacity)
+    pr = rank_projection(wl, 0, rows, routing, ranks, device, seed=1000 + rank)
     T, K, N = pr["T"], pr["K"], pr["N"]
-    counts = algorithmic_counts(pr["routing"], pr["ranks"], K, N, T)
+    global_T = sum(e - s for s, e in plan.bin_rows)
+    routes = [(r.row_start, r.row_end, r.adapter_id) for r in routing.routes]
+    counts = algorithmic_counts(routes, ranks, K, N, T)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     prep = b200_ops.prepare_forward(pr["x"], pr["w"], pr["lora_a"], pr["lora_b"], pr["adapters"], pr["routing"])
     y = prep.new_output()
@@ -314,14 +440,16 @@ def run_ours(args):
         barrier()
         return [[ev[i][j].elapsed_time(ev[i][j + 1]) for j in range(n_events - 1)] for i in range(steps)]
 
-    default_stages = SH | EX | (nat.LF_STAGE_SEPARATE if args.separate_launches else 0)
+    def bracket(fn):
+        def step(ev):
+            if ev:
+                ev[0].record()
+            fn()
+            if ev:
+                ev[1].record()
+        return step
 
-    def fwd_default(ev):
-        if ev:
-            ev[0].record()
-        prep.launch(y, default_stages)
-        if ev:
-            ev[1].record()
+    default_stages = SH | EX | (nat.LF_STAGE_SEPARATE if args.separate_launches else 0)
 
     def fwd_staged(ev):
         if ev:
@@ -335,42 +463,43 @@ def run_ours(args):
 
     sampler = ClockSampler(local_rank)
     sampler.start()
-    t = timed(fwd_default, args.steps, args.warmup, 2)
+    t = timed(bracket(lambda: prep.launch(y, default_stages)), args.steps, args.warmup, 2)
     clocks = sampler.stop()
     n_launch = prep.launch_count()  # reflects the path actually taken (co-scheduling switch included)
     step_local_ms = statistics.mean(s[0] for s in t)
     step_ms = rank_max(step_local_ms)
-    value = pr["global_T"] / (step_ms / 1e3)
+    value = global_T / (step_ms / 1e3)
     gpu_launches = n_launch * args.steps
-    # breakdown with the shrink and the fused GEMM as separate launches
-    tsplit = timed(fwd_staged, max(5, args.steps // 2), 2, 3)
+    short = max(5, args.steps // 2)
+    tsplit = timed(fwd_staged, short, 2, 3)  # the shrink and the fused GEMM as separate launches
     shrink_ms = statistics.mean(s[0] for s in tsplit)
     gemm_ms = statistics.mean(s[1] for s in tsplit)
-
     # yardsticks: our GEMM with LoRA disabled, and cuBLAS x @ W^T
-    tb = timed(lambda ev: (ev and ev[0].record(), prep.launch(y, BA), ev and ev[1].record()),
-               max(5, args.steps // 2), 2, 2)
-    own_base_ms = statistics.mean(s[0] for s in tb)
-    xw = pr["x"]
-    wt = pr["w"].t()
-    tc = timed(lambda ev: (ev and ev[0].record(), torch.matmul(xw, wt), ev and ev[1].record()),
-               max(5, args.steps // 2), 2, 2)
-    cublas_ms = statistics.mean(s[0] for s in tc)
+    own_base_ms = statistics.mean(s[0] for s in timed(bracket(lambda: prep.launch(y, BA)), short, 2, 2))
+    xw, wt = pr["x"], pr["w"].t()
+    cublas_ms = statistics.mean(s[0] for s in timed(bracket(lambda: torch.matmul(xw, wt)), short, 2, 2))
 
-    # e2e through the plugin call with pinned host buffers
+    # e2e through the public host-batch call, host wall clock around call + synchronize
     x_host = pr["x"].cpu().pin_memory()
     y_host = torch.empty((T, N), dtype=torch.bfloat16).pin_memory()
+    cur = torch.cuda.current_stream()
 
-    def e2e(ev):
-        if ev:
-            ev[0].record()
+    def e2e_call():
         b200_ops.fused_lora_forward_host(x_host, pr["w"], pr["lora_a"], pr["lora_b"], pr["adapters"], pr["routing"],
                                          out=y_host)
-        if ev:
-            ev[1].record()
 
-    te = timed(e2e, max(5, args.steps // 2), 2, 2)
-    e2e_ms = rank_max(statistics.mean(s[0] for s in te))
+    for _ in range(2):
+        e2e_call()
+    barrier()
+    wall = []
+    for _ in range(short):
+        flush.zero_()
+        cur.synchronize()
+        t0 = time.perf_counter()
+        e2e_call()
+        cur.synchronize()
+        wall.append(time.perf_counter() - t0)
+    e2e_ms = rank_max(1e3 * statistics.mean(wall))
 
     # requests in, per-request results out (one device): C++ packing, lf_copy_rows gather,
     # fused forward, lf_copy_rows scatter
@@ -384,55 +513,64 @@ def run_ours(args):
         req_x = {r.request_id: torch.randn(r.num_rows, K, device=device, generator=gq).to(torch.bfloat16)
                  for r in reqs}
         coord = Coordinator(pr["w"], pr["adapters"], pr["lora_a"], pr["lora_b"], tile_capacity=wl.tile_capacity)
-
-        def cstep(ev):
-            if ev:
-                ev[0].record()
-            coord.run_batch(reqs, req_x)
-            if ev:
-                ev[1].record()
-
-        tco = timed(cstep, max(5, args.steps // 2), 2, 2)
-        co_ms = statistics.mean(s[0] for s in tco)
+        co_ms = statistics.mean(s[0] for s in timed(bracket(lambda: coord.run_batch(reqs, req_x)), short, 2, 2))
         coordinator = {"value": sum(r.num_rows for r in reqs) / (co_ms / 1e3), "unit": "tokens/s", "ms_per_step": co_ms,
                        "requests": len(reqs),
                        "path": "Coordinator.run_batch: greedy_pack (C++), lf_copy_rows gather, fused forward, "
                                "lf_copy_rows scatter; request tensors resident on the device"}
 
-    # forward + backward (with the all-reduce of spanning adapter gradients when N > 1)
+    peaks = load_peaks()
+    backward = None
     fwd_bwd = None
+    grad_dtype = torch.float32 if world > 1 else None
+    rank_of = dict(enumerate(ranks))
     if not args.no_fwd_bwd:
-        def fb(ev):
+        # the backward's stages as launches of their own: routed shrinks, grad_x GEMM, dA/dB grams
+        bprep = b200_ops.prepare_backward(pr["grad"], pr["x"], pr["w"], pr["lora_a"], pr["lora_b"], pr["adapters"],
+                                          pr["routing"])
+        BS, BX, BG = nat.LF_BSTAGE_SHRINK, nat.LF_BSTAGE_GRAD_X, nat.LF_BSTAGE_GRAD_AB
+
+        def bwd_staged(ev):
+            for j, st in enumerate((BS, BX, BG)):
+                if ev:
+                    ev[j].record()
+                bprep.launch(st)
             if ev:
-                ev[0].record()
+                ev[3].record()
+
+        tbs = timed(bwd_staged, short, 2, 4)
+        b_shrink, b_gx, b_gram = (statistics.mean(s[j] for s in tbs) for j in range(3))
+        gram_gbs = counts["gram_bytes"] / (b_gram / 1e3) / 1e9
+        backward = {"stages_ms": {"routed_shrinks": b_shrink, "grad_x_gemm": b_gx, "grams_dA_dB": b_gram},
+                    "gram_roofline": {"kernel": "tc_gram_kernel (dA and dB, one launch)", "bound": "hbm",
+                                      "achieved": gram_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                                      "frac": gram_gbs / peaks["hbm_gbs"], "bytes_per_launch": counts["gram_bytes"],
+                                      "ms_per_launch": b_gram}}
+
+        def fb():
             b200_ops.fused_lora_forward(pr["x"], pr["w"], pr["lora_a"], pr["lora_b"], pr["adapters"], pr["routing"])
             gx, ga, gb = b200_ops.fused_lora_backward(pr["grad"], pr["x"], pr["w"], pr["lora_a"], pr["lora_b"],
-                                                      pr["adapters"], pr["routing"])
-            allreduce_spanning_grads(pr["plan"], ga, gb, dict(enumerate(pr["ranks"])), K, N, device)
-            if ev:
-                ev[1].record()
+                                                      pr["adapters"], pr["routing"], grad_dtype=grad_dtype)
+            allreduce_spanning_grads(plan, ga, gb, rank_of, K, N, device)
 
-        tfb = timed(fb, max(5, args.steps // 2), 2, 2)
-        fb_ms = rank_max(statistics.mean(s[0] for s in tfb))
+        fb_ms = rank_max(statistics.mean(s[0] for s in timed(bracket(fb), short, 2, 2)))
         bwd_launches = b200_ops.last_launch_count()
-
-        def bwd_only(ev):
-            if ev:
-                ev[0].record()
-            b200_ops.fused_lora_backward(pr["grad"], pr["x"], pr["w"], pr["lora_a"], pr["lora_b"], pr["adapters"],
-                                         pr["routing"])
-            if ev:
-                ev[1].record()
-
-        tbo = timed(bwd_only, max(5, args.steps // 2), 2, 2)
-        bwd_ms = rank_max(statistics.mean(s[0] for s in tbo))
-        fwd_bwd = {"value": pr["global_T"] / (fb_ms / 1e3), "unit": "tokens/s", "ms_per_step": fb_ms,
+        bwd_ms = rank_max(statistics.mean(s[0] for s in timed(bracket(
+            lambda: b200_ops.fused_lora_backward(pr["grad"], pr["x"], pr["w"], pr["lora_a"], pr["lora_b"],
+                                                 pr["adapters"], pr["routing"], grad_dtype=grad_dtype)), short, 2, 2)))
+        fwd_bwd = {"value": global_T / (fb_ms / 1e3), "unit": "tokens/s", "ms_per_step": fb_ms,
                    "launches_per_step": n_launch + bwd_launches, "backward_ms": bwd_ms,
                    "tflops": counts["fwdbwd_flops"] * world / (fb_ms / 1e3) / 1e12,
-                   "spanning_adapters": len(pr["plan"].spanning)}
+                   "spanning_adapters": len(plan.spanning)}
+    del prep, y, pr
+
+    # multi-projection workloads, forward + backward, strong scaling over the N GPUs
+    workloads = {}
+    for name in [e for e in args.extra.split(",") if e and e != "none"]:
+        workloads[name] = run_workload(name, WORKLOADS[name], world, rank, device, args, flush, barrier, rank_max,
+                                       peaks)
 
     err = nat.device_error()
-    peaks = load_peaks()
     if n_launch == 1:  # one kernel does the whole forward: shrink on spare CTA pairs, GEMM + expand
         dom_kernel = "tc_gemm_pair_kernel (co-scheduled routed shrink + base GEMM + LoRA expand)"
         dom_flops, dom_ms = counts["fwd_flops"], step_local_ms
@@ -441,14 +579,13 @@ def run_ours(args):
         dom_flops, dom_ms = counts["gemm_flops"], gemm_ms
     gemm_tflops = dom_flops / (dom_ms / 1e3) / 1e12
     shrink_gbs = counts["shrink_bytes"] / (shrink_ms / 1e3) / 1e9
-    # ncu cannot capture the co-scheduled (cooperative) launch; its DRAM traffic is unmeasured and
-    # the two-launch path's capture of the fused GEMM is reported beside it
     pair_traffic = load_traffic("tc_gemm_pair_kernel", args.workload)
-    traffic = pair_traffic if n_launch == 2 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        Tc, times = cpu_oracle_sample(wl, args.cpu_seconds)
+        limiter = use_all_host_cores()  # noqa: F841
+        wlm = load_workloads_module()
+        Tc, times, _ = cpu_headline_sample(wlm, wlm.WORKLOADS[args.workload], 1, budget_s=args.cpu_seconds)
         cpu = {"value": Tc / statistics.mean(times), "unit": "tokens/s", "cores": cpu_threads(), "kind": "port",
                "sample": f"{len(times)} full {Tc}-token forwards of the numpy float32 oracle "
                          f"({sum(times):.1f} s of CPU work)"}
@@ -458,18 +595,20 @@ def run_ours(args):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_ms, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": args.workload, "tokens_per_gpu": wl.total_rows, "global_tokens": pr["global_T"],
-                       "in_features": K, "out_features": N, "adapters": wl.n_adapters, "rank": 16,
-                       "tile_rows": wl.tile_capacity, "routes_rank0": len(pr["routing"].routes),
+            "config": {"workload": args.workload, "tokens_per_gpu": wl.total_rows, "global_tokens": global_T,
+                       "in_features": K, "out_features": N, "adapters": wl.n_adapters, "rank": ranks[0],
+                       "tile_rows": wl.tile_capacity, "routes_rank0": len(routes),
                        "parallelism": f"dp{world} over packed bins (no forward communication)",
                        "l2": "flushed (256 MiB write) before every timed step",
                        "pass": "forward (routed shrink + fused base GEMM/LoRA expand)"},
             "roofline": {"kernel": dom_kernel, "bound": "tensor",
                          "achieved": gemm_tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                         "frac": gemm_tflops / peaks["bf16_tflops"], "traffic": traffic,
+                         "frac": gemm_tflops / peaks["bf16_tflops"], "traffic": pair_traffic,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the fused GEMM "
+                                           "launch of the two-launch forward (profiles/ncu_traffic.txt); ncu "
+                                           "cannot capture the cooperative one-launch forward",
                          "peak_source": f"{peaks['source']} bf16 dense (burst)",
-                         "flops_per_launch": dom_flops, "ms_per_launch": dom_ms, "launches_per_step": n_launch,
-                         "traffic_two_launch_gemm": pair_traffic},
+                         "flops_per_launch": dom_flops, "ms_per_launch": dom_ms, "launches_per_step": n_launch},
             "split_launches": {"shrink_ms": shrink_ms, "gemm_ms": gemm_ms, "total_ms": shrink_ms + gemm_ms},
             "shrink_roofline": {"kernel": "tc_shrink_kernel (standalone launch)", "bound": "hbm", "achieved": shrink_gbs,
                                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": shrink_gbs / peaks["hbm_gbs"],
@@ -477,12 +616,15 @@ def run_ours(args):
             "vs_base_gemm": {"fused_fwd_ms": step_ms, "own_base_gemm_ms": own_base_ms, "cublas_base_gemm_ms": cublas_ms,
                              "fused_over_own_base": step_ms / own_base_ms, "fused_over_cublas": step_ms / cublas_ms,
                              "cublas_tflops": 2.0 * T * K * N / (cublas_ms / 1e3) / 1e12},
-            "e2e": {"value": pr["global_T"] / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+            "e2e": {"value": global_T / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": T * K * 2, "d2h_bytes_per_step": T * N * 2,
+                    "timing": "host wall clock from before the call to after the stream synchronize, max over ranks",
                     "path": "b200_ops.fused_lora_forward_host -> lf_forward_host: pinned host x/y, 1024-row "
                             "chunks enqueued by one native call, copies in both directions overlapped with the "
-                            "fused forward"},
+                            "fused forward; at N > 1 every rank's copies share the host's PCIe and memory"},
+            "backward": backward,
             "fwd_bwd": fwd_bwd,
+            "workloads": workloads,
             "coordinator": coordinator,
             "cpu_baseline": cpu,
             "clocks": clocks,
@@ -494,6 +636,105 @@ def run_ours(args):
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def run_workload(name, wl, world, rank, device, args, flush, barrier, rank_max, peaks):
+    """Forward + backward over every projection of `wl`, its tokens split over the ranks; at N > 1
+    float32 adapter gradients and the all-reduce of spanning adapters per projection."""
+    import torch
+
+    from lorafusion_b200 import b200_ops
+    from lorafusion_b200.sharding import allreduce_spanning_grads, assign_bins, local_layout
+    from lorafusion_b200.workloads import adapter_ranks
+
+    ranks = adapter_ranks(wl)
+    rank_of = dict(enumerate(ranks))
+    packing = global_packing(wl, wl.total_rows)
+    plan = assign_bins(packing.bins, world)
+    rows, routing = local_layout(plan, packing.bins, rank, wl.tile_capacity)
+    routes = [(r.row_start, r.row_end, r.adapter_id) for r in routing.routes]
+    projs = [rank_projection(wl, p, rows, routing, ranks, device, seed=7 * p + 31 * rank)
+             for p in range(len(wl.projections))]
+    flops = sum(algorithmic_counts(routes, ranks, p["K"], p["N"], p["T"])["fwdbwd_flops"] for p in projs)
+    grad_dtype = torch.float32 if world > 1 else None
+
+    def step(ev):
+        if ev:
+            ev[0].record()
+        for p in projs:
+            b200_ops.fused_lora_forward(p["x"], p["w"], p["lora_a"], p["lora_b"], p["adapters"], p["routing"])
+        if ev:
+            ev[1].record()
+        grads = []
+        for p in projs:
+            grads.append(b200_ops.fused_lora_backward(p["grad"], p["x"], p["w"], p["lora_a"], p["lora_b"],
+                                                      p["adapters"], p["routing"], grad_dtype=grad_dtype))
+        if ev:
+            ev[2].record()
+        for p, (_, ga, gb) in zip(projs, grads):
+            allreduce_spanning_grads(plan, ga, gb, rank_of, p["K"], p["N"], device)
+        if ev:
+            ev[3].record()
+
+    steps = max(3, args.steps // 3)
+    for _ in range(2):
+        flush.zero_()
+        step(None)
+    barrier()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        torch.cuda._sleep(100_000)
+        step(ev[i])
+    barrier()
+    per = [[ev[i][j].elapsed_time(ev[i][j + 1]) for j in range(3)] for i in range(steps)]
+    fwd_ms, bwd_ms, ar_ms = (statistics.mean(s[j] for s in per) for j in range(3))
+    # per projection, stages as launches of their own (this rank): forward shrink / fused GEMM,
+    # backward shrinks / grad_x GEMM / grams
+    from lorafusion_b200 import _native as nat
+    stages = {}
+    for (pname, _, _), p in zip(wl.projections, projs):
+        fp = b200_ops.prepare_forward(p["x"], p["w"], p["lora_a"], p["lora_b"], p["adapters"], p["routing"])
+        bp = b200_ops.prepare_backward(p["grad"], p["x"], p["w"], p["lora_a"], p["lora_b"], p["adapters"],
+                                       p["routing"], grad_dtype=grad_dtype)
+        yp = fp.new_output()
+        launches = [lambda: fp.launch(yp, nat.LF_STAGE_SHRINK), lambda: fp.launch(yp, nat.LF_STAGE_EXPAND),
+                    lambda: bp.launch(nat.LF_BSTAGE_SHRINK), lambda: bp.launch(nat.LF_BSTAGE_GRAD_X),
+                    lambda: bp.launch(nat.LF_BSTAGE_GRAD_AB)]
+        for f in launches:
+            f()
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(launches) + 1)]
+        flush.zero_()
+        evs[0].record()
+        for j, f in enumerate(launches):
+            f()
+            evs[j + 1].record()
+        torch.cuda.synchronize()
+        t_ = [evs[j].elapsed_time(evs[j + 1]) for j in range(len(launches))]
+        stages[pname] = {"fwd_shrink": t_[0], "fwd_gemm": t_[1], "bwd_shrinks": t_[2], "bwd_grad_x": t_[3],
+                         "bwd_grams": t_[4]}
+        del fp, bp, yp
+    local = fwd_ms + bwd_ms + ar_ms
+    ms = rank_max(local)
+    total_flops = flops
+    if world > 1:
+        t = torch.tensor([flops], dtype=torch.float64, device=device)
+        torch.distributed.all_reduce(t)
+        total_flops = float(t.item())
+    tflops = total_flops / (ms / 1e3) / 1e12
+    out = {"value": wl.total_rows / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+           "scaling": "strong", "global_tokens": wl.total_rows, "projections": [p[0] for p in wl.projections],
+           "adapters": wl.n_adapters, "pass": "forward + backward over every projection per step",
+           "rank0_ms": {"forward": fwd_ms, "backward": bwd_ms, "allreduce": ar_ms},
+           "rank0_stage_ms": stages,
+           "spanning_adapters": len(plan.spanning),
+           "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops_sustained"],
+                        "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops_sustained"],
+                        "peak_source": f"{peaks['source']} bf16 dense (sustained: seconds-long step)"},
+           "l2": "flushed (256 MiB write) before every timed step; inputs larger than L2"}
+    del projs
+    torch.cuda.empty_cache()
+    return out
 
 
 def main():

@@ -275,6 +275,27 @@ LF_API int lf_backward_ex(const lf_problem* prob, const lf_plan_info* info, cons
                           size_t workspace_bytes, lf_stream_t stream);
 
 /*
+ * The backward in separately launchable stages (arguments as lf_backward_ex), for callers that
+ * time them or overlap them with other work (e.g. a gradient all-reduce with the grad_x GEMM).
+ * `stages` is a bit mask; each stage is a launch of its own and the routed shrinks are never
+ * co-scheduled inside the grad_x launch:
+ *   LF_BSTAGE_SHRINK   S_b = s_i g B_i (and S_f = s_i x A_i^T unless s_f_dev is given) into the
+ *                      workspace
+ *   LF_BSTAGE_GRAD_X   grad_x = g W + S_b A (reads S_b from the workspace)
+ *   LF_BSTAGE_GRAD_AB  grad_a / grad_b, the segmented grams (read S_f and S_b)
+ * A GRAD_X or GRAD_AB call reads what an earlier SHRINK call on the same workspace, tables and
+ * inputs left there; stages passed together run in the order above.  No counterpart in the
+ * reference.
+ */
+#define LF_BSTAGE_SHRINK 1
+#define LF_BSTAGE_GRAD_X 2
+#define LF_BSTAGE_GRAD_AB 4
+LF_API int lf_backward_stages(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
+                              const void* grad_out_dev, const void* s_f_dev, int32_t s_f_planes,
+                              int32_t grad_ab_dtype, void* grad_x_dev, void* grad_a_dev, void* grad_b_dev,
+                              void* workspace_dev, size_t workspace_bytes, int32_t stages, lf_stream_t stream);
+
+/*
  * Forward of a batch that lives in host memory, streamed in row chunks: chunk i is copied to
  * x_dev on `h2d_stream` while chunk i-1 is computed on `stream` and chunk i-2 is copied back to
  * y_host on `d2h_stream`, so both PCIe directions and the GPU work overlap.  All copies and

@@ -26,6 +26,7 @@ LF_ERR_DEVICE = 6
 
 LF_F32, LF_BF16, LF_F16 = 0, 1, 2
 LF_STAGE_SHRINK, LF_STAGE_EXPAND, LF_STAGE_BASE, LF_STAGE_SINGLE_CTA, LF_STAGE_SEPARATE = 1, 2, 4, 8, 16
+LF_BSTAGE_SHRINK, LF_BSTAGE_GRAD_X, LF_BSTAGE_GRAD_AB = 1, 2, 4
 TILE_ROWS = 128
 
 _c_i32 = ctypes.c_int32
@@ -111,6 +112,9 @@ def _declare(L: ctypes.CDLL) -> None:
     L.lf_backward_ex.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_p, _c_p,
                                  ctypes.c_size_t, _c_p]
     L.lf_backward_ex.restype = ctypes.c_int
+    L.lf_backward_stages.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_p,
+                                     _c_p, ctypes.c_size_t, _c_i32, _c_p]
+    L.lf_backward_stages.restype = ctypes.c_int
     L.lf_backward.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, ctypes.c_size_t, _c_p]
     L.lf_backward.restype = ctypes.c_int
     L.lf_backward_sf.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_i32, _c_p, _c_p, _c_p, _c_p,

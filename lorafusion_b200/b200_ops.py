@@ -30,6 +30,7 @@ from __future__ import annotations
 import ctypes
 import warnings
 import weakref
+from collections import OrderedDict
 
 import numpy as np
 import torch
@@ -39,8 +40,8 @@ from lorafusion_b200 import _native as nat
 _DTYPE_CODE = {torch.float32: nat.LF_F32, torch.bfloat16: nat.LF_BF16, torch.float16: nat.LF_F16}
 
 __all__ = ["fused_lora_forward", "fused_lora_backward", "fused_lora_forward_host", "prepare_forward",
-           "PreparedForward", "clear_weight_cache", "release", "last_launch_count", "use_cooperative_launch",
-           "CudaCorePathWarning"]
+           "PreparedForward", "prepare_backward", "PreparedBackward", "clear_weight_cache", "release",
+           "last_launch_count", "use_cooperative_launch", "CudaCorePathWarning"]
 
 
 class CudaCorePathWarning(UserWarning):
@@ -68,16 +69,21 @@ def _warn_if_cuda_core(dtype, K: int, N: int, tensors) -> None:
 
 # --------------------------------------------------------------------------- caches
 _ROUTE_CACHE: dict[int, "_Routes"] = {}
-_ADAPTER_CACHE: dict[tuple, list] = {}
+# adapter records by (slots, id of the first A, id of the first B), least recently used first; a
+# model calls the op with one routing and many adapter sets (layers x projections), so every set
+# keeps its record and packed slabs until _ADAPTER_CACHE_MAX sets are cached
+_ADAPTER_CACHE: "OrderedDict[tuple, _AdapterSet]" = OrderedDict()
+_ADAPTER_CACHE_MAX = 4096
 _WEIGHT_CACHE: dict[tuple, tuple] = {}
 _PLAN_BY_CONTENT: dict[tuple, "_Plan"] = {}
 _CACHE_MAX = 256
-_ADAPTER_SETS_PER_KEY = 4
 _last_launches = 0
-# S_f = s x A^T left in recent forwards' workspaces, for a backward on the same inputs:
-# id(x) -> (weakref x, x version, route record, plan, adapter record, workspace, planes)
-_SAVED_SF: dict[int, tuple] = {}
-_SAVED_MAX = 4
+# S_f = s x A^T left by forwards, for a backward on the same inputs (what autograd would save as
+# the activation x A^T): (id(x), id(route record), id(adapter record)) -> (weakref x, x version,
+# route record, plan, adapter record, workspace, planes), least recently used first; entries whose
+# x has died are dropped on the next insertion
+_SAVED_SF: "OrderedDict[tuple, tuple]" = OrderedDict()
+_SAVED_MAX = 1024
 _VERSION = torch.Tensor._version.__get__
 _DATA_PTR = torch.Tensor.data_ptr
 
@@ -209,22 +215,21 @@ def _adapters(rts: _Routes, lora_a, lora_b, adapters) -> _AdapterSet:
     b_list = list(map(lora_b.__getitem__, slots))
     a_ids = list(map(id, a_list))
     b_ids = list(map(id, b_list))
-    recs = _ADAPTER_CACHE.get(slots)
-    if recs is None:
-        if len(_ADAPTER_CACHE) >= _CACHE_MAX:
-            _ADAPTER_CACHE.clear()
-        recs = _ADAPTER_CACHE[slots] = []
-    for i, rec in enumerate(recs):
-        if rec.a_ids == a_ids and rec.b_ids == b_ids:
-            if not rec.unchanged(a_list, b_list):
-                rec = recs[i] = _AdapterSet(a_list, b_list, a_ids, b_ids, specs)  # same tensors, updated
-            elif list(map(id, specs)) != rec.spec_ids:
-                rec.spec_ids = list(map(id, specs))
-                rec.scales = tuple(float(sp.scaling) for sp in specs)
-            return rec
-    rec = _AdapterSet(a_list, b_list, a_ids, b_ids, specs)
-    recs.insert(0, rec)
-    del recs[_ADAPTER_SETS_PER_KEY:]
+    # the record holds the tensors, so an id in a live record cannot be reused by another tensor
+    key = (slots, a_ids[0], b_ids[0]) if slots else (slots,)
+    rec = _ADAPTER_CACHE.get(key)
+    if rec is not None and rec.a_ids == a_ids and rec.b_ids == b_ids:
+        _ADAPTER_CACHE.move_to_end(key)
+        if not rec.unchanged(a_list, b_list):
+            rec = _ADAPTER_CACHE[key] = _AdapterSet(a_list, b_list, a_ids, b_ids, specs)  # same tensors, updated
+        elif list(map(id, specs)) != rec.spec_ids:
+            rec.spec_ids = list(map(id, specs))
+            rec.scales = tuple(float(sp.scaling) for sp in specs)
+        return rec
+    rec = _ADAPTER_CACHE[key] = _AdapterSet(a_list, b_list, a_ids, b_ids, specs)
+    _ADAPTER_CACHE.move_to_end(key)
+    while len(_ADAPTER_CACHE) > _ADAPTER_CACHE_MAX:
+        _ADAPTER_CACHE.popitem(last=False)
     return rec
 
 
@@ -421,10 +426,15 @@ def fused_lora_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> tor
 def _save_sf(x, rts, plan, aset, ws, planes: int) -> None:
     """Remember this forward's S_f (the fixed part of its workspace: S_ext planes and flags, not
     the K-split tail's scratch) for a backward on the same inputs."""
+    dead = [k for k, v in _SAVED_SF.items() if v[0]() is None]
+    for k in dead:
+        del _SAVED_SF[k]
     while len(_SAVED_SF) >= _SAVED_MAX:
-        _SAVED_SF.pop(next(iter(_SAVED_SF)))
+        _SAVED_SF.popitem(last=False)
     try:
-        _SAVED_SF[id(x)] = (weakref.ref(x), x._version, rts, plan, aset, ws, planes)
+        key = (id(x), id(rts), id(aset))
+        _SAVED_SF[key] = (weakref.ref(x), x._version, rts, plan, aset, ws, planes)
+        _SAVED_SF.move_to_end(key)
     except TypeError:  # pragma: no cover - objects without weakref support
         pass
 
@@ -432,7 +442,7 @@ def _save_sf(x, rts, plan, aset, ws, planes: int) -> None:
 def _saved_sf(x, rts, plan, aset):
     """(workspace, planes) of a forward on this very x (unchanged since), with the same validated
     routes, plan and adapter record (every A and B tensor unchanged since), or None."""
-    hit = _SAVED_SF.get(id(x))
+    hit = _SAVED_SF.get((id(x), id(rts), id(aset)))
     if hit is None:
         return None
     xref, ver, r0, p0, a0, ws, planes = hit
@@ -544,6 +554,62 @@ def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, rout
     n_launch = max(0, int(L.lf_backward_launch_count(ctypes.byref(prob), ctypes.byref(info))))
     _last_launches = n_launch - 1 if saved is not None and n_launch == 4 else n_launch
     return grad_x, *_grad_dicts(plan, ga_flat, gb_flat, K, N)
+
+
+class PreparedBackward:
+    """A backward call with tables, slabs, outputs and workspace resolved once.
+
+    ``launch(stages)`` enqueues ``lf_backward_stages`` (``LF_BSTAGE_*`` bits: routed shrinks,
+    grad_x GEMM, dA/dB grams, each a launch of its own) on the current stream with no Python-side
+    checks, so a caller can time the stages or order them around other work (a gradient
+    all-reduce that overlaps the grad_x GEMM).  ``grads()`` returns ``(grad_x, grad_a, grad_b)``
+    views of the outputs in the layout ``fused_lora_backward`` returns.  The caller keeps the
+    inputs alive and unchanged.
+    """
+
+    def __init__(self, grad_out, x, base_weight, lora_a, lora_b, adapters, routing, grad_dtype=None):
+        rts = _routes(routing, x.shape[0])
+        self.x = _activation(x, "x")
+        self.g = _activation(grad_out, "grad_out")
+        self.device = self.x.device
+        T, K = self.x.shape
+        N = base_weight.shape[0]
+        self.T, self.K, self.N = T, K, N
+        dtype = self.x.dtype
+        if self.g.dtype != dtype:
+            self.g = self.g.to(dtype)
+        gdt = dtype if grad_dtype is None else grad_dtype
+        if gdt not in (dtype, torch.float32):
+            raise ValueError(f"grad_dtype must be None, x.dtype or torch.float32, got {grad_dtype}")
+        aset = _adapters(rts, lora_a, lora_b, adapters)
+        self.w = _weight(base_weight, dtype, self.device)
+        self.plan = _plan(rts, aset, T, self.device)
+        self.packs = _pack(self.plan, aset, dtype, K, N, self.device, backward=True)
+        code = _DTYPE_CODE[dtype]
+        self.gcode = _DTYPE_CODE[gdt]
+        rtot = self.plan.info.rank_total
+        self.grad_x = torch.empty((T, K), dtype=dtype, device=self.device)
+        self.ga_flat = torch.empty(max(rtot * K, 1), dtype=gdt, device=self.device)
+        self.gb_flat = torch.empty(max(rtot * N, 1), dtype=gdt, device=self.device)
+        ws_bytes = nat.lib().lf_backward_workspace_bytes(ctypes.byref(self.plan.info), code)
+        self.ws = torch.empty(max(ws_bytes, 256), dtype=torch.uint8, device=self.device)
+        self.prob = _problem(code, T, K, N, self.x, self.w, self.packs)
+
+    def launch(self, stages: int) -> None:
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        rc = nat.lib().lf_backward_stages(
+            ctypes.byref(self.prob), ctypes.byref(self.plan.info), self.plan.table_dev.data_ptr(), self.g.data_ptr(),
+            None, 0, self.gcode, self.grad_x.data_ptr(), self.ga_flat.data_ptr(), self.gb_flat.data_ptr(),
+            self.ws.data_ptr(), self.ws.numel(), stages, stream)
+        nat.check(rc, "lf_backward_stages")
+
+    def grads(self):
+        return self.grad_x, *_grad_dicts(self.plan, self.ga_flat, self.gb_flat, self.K, self.N)
+
+
+def prepare_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, routing, grad_dtype=None) -> PreparedBackward:
+    """Resolve a backward call once (see :class:`PreparedBackward`)."""
+    return PreparedBackward(grad_out, x, base_weight, lora_a, lora_b, adapters, routing, grad_dtype)
 
 
 def _grad_dicts(plan: _Plan, ga_flat, gb_flat, K: int, N: int):

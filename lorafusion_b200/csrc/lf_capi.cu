@@ -531,11 +531,18 @@ extern "C" int lf_forward(const lf_problem* prob, const lf_plan_info* info, cons
 namespace {
 // The backward; `sf_given` (planes `sf_planes`) is S_f = s x A_i^T as a forward left it in its
 // workspace (tensor-core path only), or null to compute it here.
+// `stages` 0: the whole backward (routed shrinks inside the grad_x launch when co-scheduling
+// allows); otherwise the LF_BSTAGE_* bits, each a launch of its own (shrinks never co-scheduled).
 int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, const void* grad_out_dev,
                   const void* sf_given, int sf_planes, int grad_f32, void* grad_x_dev, void* grad_a_dev,
-                  void* grad_b_dev, void* workspace_dev, size_t workspace_bytes, lf_stream_t stream) {
+                  void* grad_b_dev, void* workspace_dev, size_t workspace_bytes, lf_stream_t stream,
+                  int stages = 0) {
   int rc = check_problem(prob, info, table_dev);
   if (rc != LF_OK) return rc;
+  const bool staged = stages != 0;
+  const bool do_shrink = !staged || (stages & LF_BSTAGE_SHRINK) != 0;
+  const bool do_gx = !staged || (stages & LF_BSTAGE_GRAD_X) != 0;
+  const bool do_gab = !staged || (stages & LF_BSTAGE_GRAD_AB) != 0;
   const int T = prob->T, K = prob->K, N = prob->N;
   const size_t sb = sext_bytes(info);
   if (workspace_bytes < backward_min_workspace_bytes(info) || !workspace_dev) return LF_ERR_CAPACITY;
@@ -545,15 +552,15 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int dt = prob->dtype;
   const size_t es = static_cast<size_t>(elem_bytes(dt));
-  if (info->n_slots > 0 && (!grad_a_dev || !grad_b_dev)) return LF_ERR_INVALID_ARG;
-  if (T == 0 || info->n_segtiles == 0) {  // adapters whose routes are all empty still get (zero) gradients
+  if (do_gab && info->n_slots > 0 && (!grad_a_dev || !grad_b_dev)) return LF_ERR_INVALID_ARG;
+  if (do_gab && (T == 0 || info->n_segtiles == 0)) {  // adapters whose routes are all empty: zero gradients
     const size_t ra = static_cast<size_t>(info->rank_total);
     const size_t gs = grad_f32 ? 4 : es;
     if (ra > 0 && K > 0 && cudaMemsetAsync(grad_a_dev, 0, ra * K * gs, st) != cudaSuccess) return LF_ERR_CUDA;
     if (ra > 0 && N > 0 && cudaMemsetAsync(grad_b_dev, 0, ra * N * gs, st) != cudaSuccess) return LF_ERR_CUDA;
-    if (T == 0) return LF_OK;
   }
-  if (!prob->x_dev || !prob->w_dev || !grad_out_dev || !grad_x_dev) return LF_ERR_INVALID_ARG;
+  if (T == 0) return LF_OK;
+  if (!prob->x_dev || !prob->w_dev || !grad_out_dev || (do_gx && !grad_x_dev)) return LF_ERR_INVALID_ARG;
   if (info->n_slots > 0 && (!prob->a_pack_dev || !prob->bt_pack_dev || !prob->at_pack_dev))
     return LF_ERR_INVALID_ARG;
   Tables tb = make_tables(info, table_dev);
@@ -582,12 +589,22 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
            make_map(&sf_map, dt, s_f, rp, s_rows, rp * es, rp, 128) &&
            make_map(&sb_map, dt, s_b, rp, s_rows, rp * es, rp, 128) &&
            make_map(&dx.l, dt, prob->at_pack_dev, rp, static_cast<uint64_t>(info->n_slots) * K, rp * es, rp, 128);
-    ok = ok && make_map(&dx.o, dt, grad_x_dev, K, T, K * es, 64, 32);
+    if (do_gx) ok = ok && make_map(&dx.o, dt, grad_x_dev, K, T, K * es, 64, 32);
     if (!ok) return LF_ERR_UNSUPPORTED;
     dx.p = p_g;
     int planes = 1;  // S_b's K-half planes (S_f's: sf_planes when reused, else the same as S_b's)
-    bool gemm_done = false;
-    if (lora) {
+    bool gemm_done = !do_gx;
+    if (lora && staged) {
+      dx.s = sb_map;
+      if (do_shrink) {
+        if (!reuse_sf) {
+          e = tc_shrink(dt, p_x, a_map, K, tb, s_f, ds->num_sms, st);
+          if (e != cudaSuccess) return LF_ERR_CUDA;
+        }
+        e = tc_shrink(dt, p_g, bt_map, N, tb, s_b, ds->num_sms, st);
+        if (e != cudaSuccess) return LF_ERR_CUDA;
+      }
+    } else if (lora) {
       dx.s = sb_map;
       // The shrinks inside the dX GEMM launch, on CTA pairs its round count leaves idle: job 1 =
       // S_b (g . B_i, needed by the dX tiles), job 2 = S_f (x . A_i^T, read by the dB gram) unless
@@ -636,7 +653,7 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
       }
       if (e != cudaSuccess) return LF_ERR_CUDA;
     }
-    if (lora) {  // dB and dA in one launch
+    if (lora && do_gab) {  // dB and dA in one launch
       GramJobDesc jobs[2];
       jobs[0].d_map = p_g;
       jobs[0].s_map = sf_map;
@@ -667,16 +684,21 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
 
   double* sf = reinterpret_cast<double*>(ws);  // the CUDA-core path computes its own f64 S_f
   double* sbp = static_cast<double*>(s_b);
-  e = simt_shrink(dt, prob->x_dev, K, K, prob->a_pack_dev, tb, sf, st);
-  if (e != cudaSuccess) return LF_ERR_CUDA;
-  e = simt_shrink(dt, grad_out_dev, N, N, prob->bt_pack_dev, tb, sbp, st);
-  if (e != cudaSuccess) return LF_ERR_CUDA;
-  // grad_x = g W + S_b . A   (Q(c, m) = W[m][c])
-  e = simt_gemm(dt, grad_out_dev, N, prob->w_dev, 1, K, T, K, N, sbp, prob->at_pack_dev, tb, grad_x_dev, K, st);
-  if (e != cudaSuccess) return LF_ERR_CUDA;
-  e = simt_gram(dt, grad_out_dev, N, N, sf, tb, grad_b_dev, 0, grad_f32, st);
-  if (e != cudaSuccess) return LF_ERR_CUDA;
-  e = simt_gram(dt, prob->x_dev, K, K, sbp, tb, grad_a_dev, 1, grad_f32, st);
+  if (do_shrink) {
+    e = simt_shrink(dt, prob->x_dev, K, K, prob->a_pack_dev, tb, sf, st);
+    if (e != cudaSuccess) return LF_ERR_CUDA;
+    e = simt_shrink(dt, grad_out_dev, N, N, prob->bt_pack_dev, tb, sbp, st);
+    if (e != cudaSuccess) return LF_ERR_CUDA;
+  }
+  if (do_gx) {  // grad_x = g W + S_b . A   (Q(c, m) = W[m][c])
+    e = simt_gemm(dt, grad_out_dev, N, prob->w_dev, 1, K, T, K, N, sbp, prob->at_pack_dev, tb, grad_x_dev, K, st);
+    if (e != cudaSuccess) return LF_ERR_CUDA;
+  }
+  if (do_gab) {
+    e = simt_gram(dt, grad_out_dev, N, N, sf, tb, grad_b_dev, 0, grad_f32, st);
+    if (e != cudaSuccess) return LF_ERR_CUDA;
+    e = simt_gram(dt, prob->x_dev, K, K, sbp, tb, grad_a_dev, 1, grad_f32, st);
+  }
   return to_status(e);
 }
 }  // namespace
@@ -695,6 +717,19 @@ extern "C" int lf_backward_sf(const lf_problem* prob, const lf_plan_info* info, 
   if (!s_f_dev || (s_f_planes != 1 && s_f_planes != 2)) return LF_ERR_INVALID_ARG;
   return backward_impl(prob, info, table_dev, grad_out_dev, s_f_dev, s_f_planes, 0, grad_x_dev, grad_a_dev,
                        grad_b_dev, workspace_dev, workspace_bytes, stream);
+}
+
+extern "C" int lf_backward_stages(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
+                                  const void* grad_out_dev, const void* s_f_dev, int32_t s_f_planes,
+                                  int32_t grad_ab_dtype, void* grad_x_dev, void* grad_a_dev, void* grad_b_dev,
+                                  void* workspace_dev, size_t workspace_bytes, int32_t stages, lf_stream_t stream) {
+  if (!prob) return LF_ERR_INVALID_ARG;
+  if (stages <= 0 || stages > (LF_BSTAGE_SHRINK | LF_BSTAGE_GRAD_X | LF_BSTAGE_GRAD_AB)) return LF_ERR_INVALID_ARG;
+  if (s_f_dev && s_f_planes != 1 && s_f_planes != 2) return LF_ERR_INVALID_ARG;
+  if (grad_ab_dtype != prob->dtype && grad_ab_dtype != LF_F32) return LF_ERR_INVALID_ARG;
+  return backward_impl(prob, info, table_dev, grad_out_dev, s_f_dev, s_f_dev ? s_f_planes : 0,
+                       grad_ab_dtype == LF_F32 ? 1 : 0, grad_x_dev, grad_a_dev, grad_b_dev, workspace_dev,
+                       workspace_bytes, stream, stages);
 }
 
 extern "C" int lf_backward_ex(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,

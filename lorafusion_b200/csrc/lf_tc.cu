@@ -1400,7 +1400,7 @@ constexpr int kGramRingBytes = 3 * (kGramDBytes + 2 * kBM * 64 * 2);  // 3 stage
 
 // Work units of one CTA (job, slot part, column block), staged in shared memory once with the
 // segment tiles each one streams, so no role waits on a dependent table load per unit.
-constexpr int kGramMaxUnits = 128;
+constexpr int kGramMaxUnits = 64;
 constexpr int kGramMaxSt = 1024;   // segment tiles whose list entry and row tile are staged (16-bit)
 constexpr int kGramMaxBufs = 8;    // TMEM accumulators (as many as 512 columns hold)
 struct GramUnit {
@@ -1428,8 +1428,11 @@ struct GramSegs {
   uint16_t st[kGramMaxSt];
   uint16_t tile[kGramMaxSt];
 };
+// epilogue staging of a [rank, C] block in the input type: per epilogue warp 16 ranks x 32 columns
+constexpr int kGramStageTrBytes = 4 * 16 * 32 * 2;
 constexpr int kGramSmem = 1024 + kGramRingBytes + kGramMaxUnits * static_cast<int>(sizeof(GramUnit)) +
-                          static_cast<int>(sizeof(GramSlotPrefix)) + static_cast<int>(sizeof(GramSegs)) + 512;
+                          static_cast<int>(sizeof(GramSlotPrefix)) + static_cast<int>(sizeof(GramSegs)) +
+                          kGramStageTrBytes + 512;
 static_assert(kGramSmem <= 227 * 1024, "gram kernel shared memory");
 
 // Unit k of the combined list (job 0's units, then job 1's): part k / n_cblk of the job's parts,
@@ -1509,7 +1512,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   GramUnit* units = reinterpret_cast<GramUnit*>(ring + kGramRingBytes);
   GramSlotPrefix& sp = *reinterpret_cast<GramSlotPrefix*>(units + kGramMaxUnits);
   GramSegs& segs = *reinterpret_cast<GramSegs*>(&sp + 1);
-  uint64_t* full = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(&segs + 1) + 7) & ~uintptr_t(7));
+  OutT* stage_tr = reinterpret_cast<OutT*>((reinterpret_cast<uintptr_t>(&segs + 1) + 15) & ~uintptr_t(15));
+  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(stage_tr) + kGramStageTrBytes);
   uint64_t* empty = full + kGramMaxStages;
   uint64_t* tfull = empty + kGramMaxStages;
   uint64_t* tempty = tfull + kGramMaxBufs;
@@ -1549,32 +1553,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   const bool seg_cached = tb.n_segtiles <= kGramMaxSt;
-  if (warp >= 3 && seg_cached)  // slot-list entries and row tiles of every segment tile
-    for (int j = threadIdx.x - 96; j < tb.n_segtiles; j += kThreads - 96) {
+  const bool cached = tb.n_slots <= kGramMaxSlots;
+  // Every thread reads table entries in parallel (one short chain of dependent loads each): the
+  // slot-list entry and row tile of every segment tile, and each slot position's metadata.
+  if (seg_cached)
+    for (int j = threadIdx.x; j < tb.n_segtiles; j += kThreads) {
       segs.st[j] = static_cast<uint16_t>(tb.slot_list(j));
       segs.tile[j] = static_cast<uint16_t>(tb.st_tile(j));
     }
-  // Slot metadata and parts per slot position (warp 2): slots with more than `cap` segment tiles
-  // are split, unless the partial blocks or counters that needs would not fit; every CTA decides
-  // the same way.
+  if (cached)
+    for (int i = threadIdx.x; i < tb.n_slots; i += kThreads) {
+      const int sl = tb.slot_order(i);
+      const int b0 = tb.slot_st(sl);
+      sp.slot[i] = sl;
+      sp.b0[i] = b0;
+      sp.nst[i] = tb.slot_st(sl + 1) - b0;
+      sp.rank[i] = tb.slot_rank(sl);
+      sp.rprefix[i] = tb.rank_prefix(sl);
+    }
+  __syncthreads();
+  // Parts per slot position (warp 2, from shared memory): slots with more than `cap` segment
+  // tiles are split, unless the partial blocks or counters that needs would not fit; every CTA
+  // decides the same way.
   if (warp == 2) {
     int tp[2] = {0, 0}, ts[2] = {0, 0}, tss[2] = {0, 0};
-    const bool cached = tb.n_slots <= kGramMaxSlots;
     const bool try_split = cached && prm.cap > 0 && prm.partial != nullptr;
     if (cached) {
       for (int i0 = 0; i0 < tb.n_slots; i0 += 32) {
         const int i = i0 + lane;
-        int nst = 0;
-        if (i < tb.n_slots) {
-          const int sl = tb.slot_order(i);
-          const int b0 = tb.slot_st(sl);
-          nst = tb.slot_st(sl + 1) - b0;
-          sp.slot[i] = sl;
-          sp.b0[i] = b0;
-          sp.nst[i] = nst;
-          sp.rank[i] = tb.slot_rank(sl);
-          sp.rprefix[i] = tb.rank_prefix(sl);
-        }
+        const int nst = i < tb.n_slots ? sp.nst[i] : 0;
         // parts are the same for both jobs (one cap); lanes past the end count nothing
         const int P = i >= tb.n_slots ? 0 : (try_split && nst > prm.cap) ? (nst + prm.cap - 1) / prm.cap : 1;
         int a = P, b = P > 1 ? P : 0, c = P > 1 ? 1 : 0;  // inclusive warp scans
@@ -1737,19 +1744,76 @@ __global__ void __launch_bounds__(kThreads, 1)
       const GramJob& jb = prm.job[g.job];
       const int c = g.cb * 128 + col;
       const int rank = g.rank;
-      // element (j, c) of this slot's block: [rank, C] (transposed) or [C, rank], in the input
-      // type or (out_f32) in float
+      // Elements (j0 .. j0+15, c) of this slot's block, [rank, C] (transposed) or [C, rank], in the
+      // input type or (out_f32) in float, written with 16-byte stores where the layout allows
+      // (C is a multiple of 8 on this path): a [C, rank] row segment from registers; a [rank, C]
+      // block in the input type through this warp's staging tile (16 ranks x 32 columns) as 16-byte
+      // row pieces; [rank, C] in float as one 128-byte row piece per warp and rank.  The whole warp
+      // calls it (same unit, converged).
       const int64_t obase = static_cast<int64_t>(g.rank_prefix) * jb.C;
-      auto store = [&](int j, float v) {
-        const int64_t idx = obase + (jb.transpose_out ? static_cast<int64_t>(j) * jb.C + c : static_cast<int64_t>(c) * rank + j);
-        if (jb.out_f32)
-          reinterpret_cast<float*>(jb.out)[idx] = v;
-        else
-          reinterpret_cast<OutT*>(jb.out)[idx] = cvt_out<OutT>(v);
+      auto store16 = [&](int j0, const float* v) {
+        if (jb.transpose_out && !jb.out_f32) {
+          OutT* stg = stage_tr + (warp - 2) * 16 * 32;
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) stg[jj * 32 + lane] = cvt_out<OutT>(v[jj]);
+          __syncwarp();
+          OutT* o = reinterpret_cast<OutT*>(jb.out) + obase;
+          const int cw = g.cb * 128 + q * 32;
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int idx = lane + 32 * t, rr = idx >> 2, ch = idx & 3;
+            const int j = j0 + rr, c8 = cw + ch * 8;
+            if (j < rank && c8 < jb.C)
+              *reinterpret_cast<uint4*>(o + static_cast<int64_t>(j) * jb.C + c8) =
+                  *reinterpret_cast<const uint4*>(stg + rr * 32 + ch * 8);
+          }
+          __syncwarp();
+          return;
+        }
+        if (c >= jb.C) return;
+        if (jb.transpose_out) {
+          float* o = reinterpret_cast<float*>(jb.out) + obase;
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj)
+            if (j0 + jj < rank) o[static_cast<int64_t>(j0 + jj) * jb.C + c] = v[jj];
+          return;
+        }
+        const int64_t row = obase + static_cast<int64_t>(c) * rank;
+        if (jb.out_f32) {
+          float* o = reinterpret_cast<float*>(jb.out) + row;
+#pragma unroll
+          for (int q4 = 0; q4 < 16; q4 += 4) {
+            const int j = j0 + q4;
+            if (rank % 4 == 0 && j + 4 <= rank)
+              *reinterpret_cast<float4*>(o + j) = make_float4(v[q4], v[q4 + 1], v[q4 + 2], v[q4 + 3]);
+            else
+              for (int e = 0; e < 4; ++e)
+                if (j + e < rank) o[j + e] = v[q4 + e];
+          }
+          return;
+        }
+        OutT* o = reinterpret_cast<OutT*>(jb.out) + row;
+#pragma unroll
+        for (int q8 = 0; q8 < 16; q8 += 8) {
+          const int j = j0 + q8;
+          if (rank % 8 == 0 && j + 8 <= rank) {
+            uint4 pk;
+            pk.x = pack2<OutT>(v[q8], v[q8 + 1]);
+            pk.y = pack2<OutT>(v[q8 + 2], v[q8 + 3]);
+            pk.z = pack2<OutT>(v[q8 + 4], v[q8 + 5]);
+            pk.w = pack2<OutT>(v[q8 + 6], v[q8 + 7]);
+            *reinterpret_cast<uint4*>(o + j) = pk;
+          } else {
+            for (int e = 0; e < 8; ++e)
+              if (j + e < rank) o[j + e] = cvt_out<OutT>(v[q8 + e]);
+          }
+        }
       };
       if (g.b == g.e) {
-        if (c < jb.C)
-          for (int j = 0; j < rank; ++j) store(j, 0.f);
+        float zeros[16];
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) zeros[jj] = 0.f;
+        for (int j0 = 0; j0 < rank; j0 += 16) store16(j0, zeros);
         continue;
       }
       const int buf = it % prm.n_bufs;
@@ -1813,26 +1877,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               acc[4 * t + 3] += v4[t].w;
             }
           }
-          if (c < jb.C) {
-#pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-              const int j = j0 + jj;
-              if (j < rank) store(j, acc[jj]);
-            }
-          }
+          if (j0 < rank) store16(j0, acc);
         }
         continue;
       }
       for (int j0 = 0; j0 < r_pad; j0 += 16) {
         float v[16];
         load_sum16(j0, v);
-        if (c < jb.C) {
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) {
-            const int j = j0 + jj;
-            if (j < rank) store(j, v[jj]);
-          }
-        }
+        if (j0 < rank) store16(j0, v);
       }
       tc_fence_before();
       mbar_arrive(&tempty[buf]);

@@ -26,10 +26,10 @@ import math
 from dataclasses import dataclass, field
 
 import numpy as np
-import torch
 
-from lorafusion_b200.config import AdapterSpec
-from lorafusion_b200.scheduler import Request, build_microbatch, bucket_by_adapter, greedy_pack
+# Only numpy and the standard library at import time: the benchmark's CPU arm loads this file by
+# itself, without the package or its native library.  torch and the scheduler are imported by the
+# functions that build tensors or packings.
 
 
 @dataclass(frozen=True)
@@ -40,7 +40,7 @@ class Workload:
     projections: tuple[tuple[str, int, int], ...]  # (name, in_features K, out_features N)
     n_adapters: int
     tile_capacity: int
-    dtype: torch.dtype
+    dtype: str  # "float32" or "bfloat16" (the torch dtype: torch_dtype())
     row_law: str  # "fixed", "zipf" or "skew"
     zipf_s: float = 1.1
     fixed_rows: tuple[int, ...] = ()
@@ -53,25 +53,25 @@ class Workload:
 WORKLOADS: dict[str, Workload] = {
     "cfg1_fp32_small": Workload(
         "cfg1_fp32_small", "fp32 fwd+bwd, x[128,256], 4 adapters rank 8, rows [48,40,24,16], 16-row tiles",
-        128, (("proj", 256, 256),), 4, 16, torch.float32, "fixed", fixed_rows=(48, 40, 24, 16),
+        128, (("proj", 256, 256),), 4, 16, "float32", "fixed", fixed_rows=(48, 40, 24, 16),
         rank_choices=(8,)),
     "cfg2_h4096_a16_r16": Workload(
         "cfg2_h4096_a16_r16", "bf16 4096->4096, 16 adapters rank 16, 4096 tokens Zipf(1.1), 128-row tiles, fwd",
-        4096, (("proj", 4096, 4096),), 16, 128, torch.bfloat16, "zipf", zipf_s=1.1,
+        4096, (("proj", 4096, 4096),), 16, 128, "bfloat16", "zipf", zipf_s=1.1,
         rank_choices=(16,), backward=False),
     "cfg3_llama8b_a64_mixed": Workload(
         "cfg3_llama8b_a64_mixed", "bf16 Llama-3-8B projections, 64 adapters ranks U{8,16,32,64}, 8192 tokens Zipf(1.1)",
         8192, (("q", 4096, 4096), ("k", 4096, 1024), ("v", 4096, 1024), ("o", 4096, 4096),
                ("gate", 4096, 14336), ("up", 4096, 14336), ("down", 14336, 4096)),
-        64, 128, torch.bfloat16, "zipf", zipf_s=1.1, rank_choices=(8, 16, 32, 64)),
+        64, 128, "bfloat16", "zipf", zipf_s=1.1, rank_choices=(8, 16, 32, 64)),
     "cfg4_decode_skew_a512": Workload(
         "cfg4_decode_skew_a512", "bf16 4096->4096, 512 adapters rank 16, 16384 tokens, one dominant adapter, 64-row tiles",
-        16384, (("proj", 4096, 4096),), 512, 64, torch.bfloat16, "skew", rank_choices=(16,)),
+        16384, (("proj", 4096, 4096),), 512, 64, "bfloat16", "skew", rank_choices=(16,)),
     "cfg5_70b_a256_r64": Workload(
         "cfg5_70b_a256_r64", "bf16 70B projections, 256 adapters rank 64, 32768 tokens Zipf(1.0)",
         32768, (("q", 8192, 8192), ("o", 8192, 8192), ("gate", 8192, 28672), ("up", 8192, 28672),
                 ("down", 28672, 8192)),
-        256, 128, torch.bfloat16, "zipf", zipf_s=1.0, rank_choices=(64,)),
+        256, 128, "bfloat16", "zipf", zipf_s=1.0, rank_choices=(64,)),
 }
 
 
@@ -107,8 +107,14 @@ def adapter_ranks(wl: Workload) -> list[int]:
     return [int(r) for r in rng.choice(np.array(wl.rank_choices), size=wl.n_adapters)]
 
 
+def torch_dtype(wl: Workload):
+    import torch
+    return getattr(torch, wl.dtype)
+
+
 def layout(wl: Workload, total_rows: int | None = None):
-    """Requests, packing, routing and row order for a workload (no tensors)."""
+    """Requests and packing of a workload (no tensors): the scheduler's bins."""
+    from lorafusion_b200.scheduler import Request, bucket_by_adapter, greedy_pack
     counts = row_counts(wl, total_rows)
     requests = [Request(request_id=i, adapter_id=i, num_rows=c) for i, c in enumerate(counts)]
     groups = bucket_by_adapter(requests)
@@ -116,33 +122,38 @@ def layout(wl: Workload, total_rows: int | None = None):
     return requests, packing
 
 
-def _randn(gen: torch.Generator, *shape: int) -> torch.Tensor:
+def _randn(gen, *shape: int):
+    import torch
     return torch.randn(*shape, generator=gen, dtype=torch.float32)
 
 
 @dataclass
 class Problem:
-    x: torch.Tensor
-    base_weight: torch.Tensor
-    lora_a: dict[int, torch.Tensor]
-    lora_b: dict[int, torch.Tensor]
-    adapters: dict[int, AdapterSpec]
+    x: object                # torch.Tensor [T, K]
+    base_weight: object      # [N, K]
+    lora_a: dict             # adapter id -> [r, K]
+    lora_b: dict             # adapter id -> [N, r]
+    adapters: dict           # adapter id -> AdapterSpec
     routing: object
     row_order: list[int]
-    grad_out: torch.Tensor | None
+    grad_out: object | None  # [T, N]
 
 
 def make_problem(
     wl: Workload,
     projection: int = 0,
-    device: str | torch.device = "cpu",
-    dtype: torch.dtype | None = None,
+    device="cpu",
+    dtype=None,
     total_rows: int | None = None,
     with_grad: bool | None = None,
     seed: int | None = None,
 ) -> Problem:
     """Materialise one projection of a workload with seeded tensors."""
-    dtype = wl.dtype if dtype is None else dtype
+    import torch
+
+    from lorafusion_b200.config import AdapterSpec
+    from lorafusion_b200.scheduler import build_microbatch
+    dtype = torch_dtype(wl) if dtype is None else dtype
     seed = wl.seed if seed is None else seed
     _, k_in, n_out = wl.projections[projection]
     ranks = adapter_ranks(wl)

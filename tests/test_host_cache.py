@@ -79,3 +79,42 @@ def test_grad_dicts_are_views_in_slot_order(ranks):
         assert torch.equal(db[aid], gb[off * N:(off + r) * N].view(N, r))
         assert da[aid].data_ptr() == ga[off * K:].data_ptr()  # views, no copies
         off += r
+
+
+def test_many_adapter_sets_on_one_routing_all_stay_cached():
+    """A model calls the op with one routing and many adapter sets (layers x projections): every
+    set keeps its record (and so its packed slabs) instead of being evicted in a cycle."""
+    ops.clear_weight_cache()
+    rt = ops._routes(_routing(), 12)
+    sets = []
+    for _ in range(40):
+        a = {0: torch.randn(4, 8), 2: torch.randn(8, 8)}
+        b = {0: torch.randn(6, 4), 2: torch.randn(6, 8)}
+        ad = {0: AdapterSpec(0, 4, 8.0, 8, 6), 2: AdapterSpec(2, 8, 4.0, 8, 6)}
+        sets.append((a, b, ad, ops._adapters(rt, a, b, ad)))
+    for a, b, ad, rec in sets:  # second pass, same order: every lookup hits
+        assert ops._adapters(rt, a, b, ad) is rec
+
+
+def test_saved_sf_is_kept_per_input_and_adapter_set():
+    """Forwards of several projections on the same x (q, k, v) each keep their own S_f; an entry
+    whose x has died is dropped."""
+    ops.clear_weight_cache()
+    rt = ops._routes(_routing(), 12)
+    x = torch.randn(12, 8)
+    recs = []
+    for _ in range(3):
+        a = {0: torch.randn(4, 8), 2: torch.randn(8, 8)}
+        b = {0: torch.randn(6, 4), 2: torch.randn(6, 8)}
+        ad = {0: AdapterSpec(0, 4, 8.0, 8, 6), 2: AdapterSpec(2, 8, 4.0, 8, 6)}
+        aset = ops._adapters(rt, a, b, ad)
+        ws = torch.empty(16, dtype=torch.uint8)
+        ops._save_sf(x, rt, "plan", aset, ws, 1)
+        recs.append((aset, ws))
+    for aset, ws in recs:
+        assert ops._saved_sf(x, rt, "plan", aset) == (ws, 1)
+    y = torch.randn(12, 8)
+    ops._save_sf(y, rt, "plan", recs[0][0], recs[0][1], 2)
+    del y
+    ops._save_sf(x, rt, "plan", recs[1][0], recs[1][1], 1)  # insertion drops the dead entry
+    assert len(ops._SAVED_SF) == 3

@@ -535,3 +535,27 @@ def test_cuda_core_path_warns_for_bf16():
     with pytest.warns(ops.CudaCorePathWarning):
         y = ops.fused_lora_forward(x, w, a, b, ad, routing)
     _check(y, case["y"], BF16_TOL, "forward")
+
+
+@pytest.mark.parametrize("order", ["shrink_gx_gab", "shrink_gab_gx", "all_at_once"])
+def test_backward_stages_match_oracle(order):
+    """lf_backward_stages: routed shrinks, grad_x GEMM and dA/dB grams as launches of their own, in
+    either order after the shrinks, match the oracle (float32 adapter gradients)."""
+    from lorafusion_b200 import _native as nat
+    ops = _ops()
+    routes = _routes_from_sizes([300, 5, 1, 94, 200, 100, 324], [0, 1, 2, 3, 0, 1, 2])
+    case = _random_case(59, 1024, 512, 768, routes, {0: 16, 1: 8, 2: 32, 3: 64}, torch.bfloat16)
+    x, w, a, b, ad, routing, g = _to_torch(case, torch.bfloat16)
+    prep = ops.prepare_backward(g, x, w, a, b, ad, routing, grad_dtype=torch.float32)
+    SH, GX, GAB = nat.LF_BSTAGE_SHRINK, nat.LF_BSTAGE_GRAD_X, nat.LF_BSTAGE_GRAD_AB
+    seq = {"shrink_gx_gab": [SH, GX, GAB], "shrink_gab_gx": [SH, GAB, GX], "all_at_once": [SH | GX | GAB]}[order]
+    for st in seq:
+        prep.launch(st)
+    gx, ga, gb = prep.grads()
+    _check(gx, case["gx"], BF16_TOL, "grad_x")
+    assert list(ga) == case["grad_keys"]
+    for k in case["grad_keys"]:
+        assert ga[k].dtype == torch.float32
+        _check(ga[k], case["ga"][k], BF16_TOL, f"grad_a[{k}]")
+        _check(gb[k], case["gb"][k], BF16_TOL, f"grad_b[{k}]")
+    assert nat.device_error() == 0
