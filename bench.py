@@ -561,6 +561,7 @@ def run_ours(args):
         fwd_bwd = {"value": global_T / (fb_ms / 1e3), "unit": "tokens/s", "ms_per_step": fb_ms,
                    "launches_per_step": n_launch + bwd_launches, "backward_ms": bwd_ms,
                    "tflops": counts["fwdbwd_flops"] * world / (fb_ms / 1e3) / 1e12,
+                   "tflops_note": "whole job (all GPUs)",
                    "spanning_adapters": len(plan.spanning)}
     del prep, y, pr
 
@@ -728,9 +729,10 @@ def run_workload(name, wl, world, rank, device, args, flush, barrier, rank_max, 
            "rank0_ms": {"forward": fwd_ms, "backward": bwd_ms, "allreduce": ar_ms},
            "rank0_stage_ms": stages,
            "spanning_adapters": len(plan.spanning),
-           "roofline": {"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops_sustained"],
-                        "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops_sustained"],
-                        "peak_source": f"{peaks['source']} bf16 dense (sustained: seconds-long step)"},
+           "roofline": {"bound": "tensor", "achieved": tflops, "peak": world * peaks["bf16_tflops_sustained"],
+                        "unit": "TFLOP/s", "frac": tflops / (world * peaks["bf16_tflops_sustained"]),
+                        "peak_source": f"{peaks['source']} bf16 dense (sustained: seconds-long step), "
+                                       f"x {world} GPU(s)"},
            "l2": "flushed (256 MiB write) before every timed step; inputs larger than L2"}
     del projs
     torch.cuda.empty_cache()
