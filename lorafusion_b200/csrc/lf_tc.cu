@@ -1401,7 +1401,6 @@ constexpr int kGramRingBytes = 3 * (kGramDBytes + 2 * kBM * 64 * 2);  // 3 stage
 // Work units of one CTA (job, slot part, column block), staged in shared memory once with the
 // segment tiles each one streams, so no role waits on a dependent table load per unit.
 constexpr int kGramMaxUnits = 64;
-constexpr int kGramMaxSt = 1024;   // segment tiles whose list entry and row tile are staged (16-bit)
 constexpr int kGramMaxBufs = 8;    // TMEM accumulators (as many as 512 columns hold)
 struct GramUnit {
   int job, slot, b, e, rank, rank_prefix, cb;
@@ -1422,17 +1421,15 @@ struct GramSlotPrefix {
   int pid_off, cid_off;   // job 1's partial blocks and counter rows follow job 0's
   int use_split, cached;
 };
-// The slot lists (segment tile of each entry) and each segment tile's row tile, read once per CTA
-// when the table has at most kGramMaxSt segment tiles (`seg_cached`).
-struct GramSegs {
-  uint16_t st[kGramMaxSt];
-  uint16_t tile[kGramMaxSt];
-};
+// Warps of the gram kernel: TMA producer, MMA issuer, then two sets of four epilogue warps that
+// drain alternate units (set s the units k = s, s + 2, ... through accumulator buffer s), so one
+// set's tensor-memory loads and global stores overlap the other's.
+constexpr int kGramEpiSets = 2;
+constexpr int kGramThreads = 64 + kGramEpiSets * 128;
 // epilogue staging of a [rank, C] block in the input type: per epilogue warp 16 ranks x 32 columns
-constexpr int kGramStageTrBytes = 4 * 16 * 32 * 2;
+constexpr int kGramStageTrBytes = kGramEpiSets * 4 * 16 * 32 * 2;
 constexpr int kGramSmem = 1024 + kGramRingBytes + kGramMaxUnits * static_cast<int>(sizeof(GramUnit)) +
-                          static_cast<int>(sizeof(GramSlotPrefix)) + static_cast<int>(sizeof(GramSegs)) +
-                          kGramStageTrBytes + 512;
+                          static_cast<int>(sizeof(GramSlotPrefix)) + kGramStageTrBytes + 512;
 static_assert(kGramSmem <= 227 * 1024, "gram kernel shared memory");
 
 // Unit k of the combined list (job 0's units, then job 1's): part k / n_cblk of the job's parts,
@@ -1502,7 +1499,7 @@ __device__ __forceinline__ uint32_t gen_arrive(uint64_t* ctr, uint32_t gen32, in
 }
 
 template <typename OutT>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kGramThreads)
     tc_gram_kernel(const __grid_constant__ CUtensorMap map_d0, const __grid_constant__ CUtensorMap map_s0,
                    const __grid_constant__ CUtensorMap map_d1, const __grid_constant__ CUtensorMap map_s1,
                    const GramParams prm) {
@@ -1511,8 +1508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* ring = smem;
   GramUnit* units = reinterpret_cast<GramUnit*>(ring + kGramRingBytes);
   GramSlotPrefix& sp = *reinterpret_cast<GramSlotPrefix*>(units + kGramMaxUnits);
-  GramSegs& segs = *reinterpret_cast<GramSegs*>(&sp + 1);
-  OutT* stage_tr = reinterpret_cast<OutT*>((reinterpret_cast<uintptr_t>(&segs + 1) + 15) & ~uintptr_t(15));
+  OutT* stage_tr = reinterpret_cast<OutT*>((reinterpret_cast<uintptr_t>(&sp + 1) + 15) & ~uintptr_t(15));
   uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(stage_tr) + kGramStageTrBytes);
   uint64_t* empty = full + kGramMaxStages;
   uint64_t* tfull = empty + kGramMaxStages;
@@ -1552,17 +1548,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_relinquish();
   }
 
-  const bool seg_cached = tb.n_segtiles <= kGramMaxSt;
   const bool cached = tb.n_slots <= kGramMaxSlots;
-  // Every thread reads table entries in parallel (one short chain of dependent loads each): the
-  // slot-list entry and row tile of every segment tile, and each slot position's metadata.
-  if (seg_cached)
-    for (int j = threadIdx.x; j < tb.n_segtiles; j += kThreads) {
-      segs.st[j] = static_cast<uint16_t>(tb.slot_list(j));
-      segs.tile[j] = static_cast<uint16_t>(tb.st_tile(j));
-    }
+  // Every thread reads table entries in parallel (one short chain of dependent loads each): each
+  // slot position's metadata.
   if (cached)
-    for (int i = threadIdx.x; i < tb.n_slots; i += kThreads) {
+    for (int i = threadIdx.x; i < tb.n_slots; i += kGramThreads) {
       const int sl = tb.slot_order(i);
       const int b0 = tb.slot_st(sl);
       sp.slot[i] = sl;
@@ -1637,7 +1627,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   for (int r = 0; r * G < total; ++r) n_mine += gram_zigzag(r, me, G) < total ? 1 : 0;
   const int n_staged = n_mine < kGramMaxUnits ? n_mine : kGramMaxUnits;
   if (warp >= 2) {  // stage this CTA's units
-    for (int k = threadIdx.x - 64; k < n_staged; k += kThreads - 64) units[k] = gram_unit(prm, sp, gram_zigzag(k, me, G));
+    for (int k = threadIdx.x - 64; k < n_staged; k += kGramThreads - 64)
+      units[k] = gram_unit(prm, sp, gram_zigzag(k, me, G));
   }
   tc_fence_before();
   __syncthreads();
@@ -1657,8 +1648,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const CUtensorMap* md = g.job ? &map_d1 : &map_d0;
         const CUtensorMap* ms = g.job ? &map_s1 : &map_s0;
         for (int i = g.b; i < g.e && ok; ++i) {
-          const int st = seg_cached ? segs.st[i] : tb.slot_list(i);
-          const int row0 = (seg_cached ? segs.tile[st] : tb.st_tile(st)) * kBM;
+          const int st = tb.slot_list(i);
+          const int row0 = tb.st_tile(st) * kBM;
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, tb.err, kErrTimeoutEmpty)) {
             ok = false;
             break;
@@ -1689,16 +1680,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true, issued_any = false;
       const uint32_t ring_base = smem_u32(ring);
       const uint32_t s_bytes = static_cast<uint32_t>(kBM * r_pad * 2);
-      int it = 0;
       for (int k = 0; k < n_mine && ok; ++k) {
         const GramUnit g = unit(k);
-        if (g.b == g.e) continue;  // adapter with only empty routes: epilogue writes zeros
-        const int buf = it % prm.n_bufs;
-        if (!mbar_wait(&tempty[buf], ((it / prm.n_bufs) & 1) ^ 1, abort_flag, tb.err, kErrTimeoutAcc)) {
+        const int buf = k & 1;  // unit k goes through buffer k % 2 to epilogue set k % 2
+        if (!mbar_wait(&tempty[buf], ((k >> 1) & 1) ^ 1, abort_flag, tb.err, kErrTimeoutAcc)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        if (g.b == g.e) {  // adapter with only empty routes: nothing to add, the epilogue writes zeros
+          mbar_arrive(&tfull[buf]);
+          continue;
+        }
         const uint32_t dt = tmem_base + static_cast<uint32_t>(buf * prm.acc_cols);
         const uint32_t chain_cols = static_cast<uint32_t>(prm.acc_cols / prm.chains);
         uint32_t started = 0;  // chains that hold a partial sum already
@@ -1727,7 +1720,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         umma_commit(&tfull[buf]);
-        ++it;
       }
       if (!ok && issued_any) {
         umma_commit(drain);
@@ -1736,12 +1728,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    const int q = warp & 3;
+    const int q = warp & 3;  // the TMEM lane quadrant this warp may access
     const int col = q * 32 + lane;
-    int it = 0;
-    for (int k = 0; k < n_mine; ++k) {
+    const int set = (warp - 2) >> 2;
+    for (int k = set; k < n_mine; k += kGramEpiSets) {
       const GramUnit g = unit(k);
       const GramJob& jb = prm.job[g.job];
+      const int buf = k & 1;
       const int c = g.cb * 128 + col;
       const int rank = g.rank;
       // Elements (j0 .. j0+15, c) of this slot's block, [rank, C] (transposed) or [C, rank], in the
@@ -1809,30 +1802,41 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       };
+      if (!warp_wait(&tfull[buf], (k >> 1) & 1, abort_flag, tb.err, kErrTimeoutAcc)) break;
+      tc_fence_after();
       if (g.b == g.e) {
         float zeros[16];
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) zeros[jj] = 0.f;
         for (int j0 = 0; j0 < rank; j0 += 16) store16(j0, zeros);
+        tc_fence_before();
+        mbar_arrive(&tempty[buf]);
         continue;
       }
-      const int buf = it % prm.n_bufs;
-      if (!warp_wait(&tfull[buf], (it / prm.n_bufs) & 1, abort_flag, tb.err, kErrTimeoutAcc)) break;
-      tc_fence_after();
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * prm.acc_cols);
       const int chain_cols = prm.acc_cols / prm.chains;
-      // 16 columns j0.. of this thread's row: chains and planes added in fixed order
+      // 16 columns j0.. of this thread's row: chains and planes added in fixed order (chain-major);
+      // two tensor-memory loads are in flight per wait
       auto load_sum16 = [&](int j0, float* out16) {
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) out16[jj] = 0.f;
-        for (int ch = 0; ch < prm.chains; ++ch)
-          for (int pl = 0; pl < prm.planes; ++pl) {
-            uint32_t v[16];
-            tmem_ld16(tbase + ch * chain_cols + pl * r_pad + j0, v);
-            tmem_wait_ld();
+        const int n = prm.chains * prm.planes;
+        for (int i0 = 0; i0 < n; i0 += 2) {
+          uint32_t v[2][16];
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) out16[jj] += __uint_as_float(v[jj]);
-          }
+          for (int u = 0; u < 2; ++u)
+            if (i0 + u < n) {
+              const int ch = (i0 + u) / prm.planes, pl = (i0 + u) - ch * prm.planes;
+              tmem_ld16(tbase + ch * chain_cols + pl * r_pad + j0, v[u]);
+            }
+          tmem_wait_ld();
+#pragma unroll
+          for (int u = 0; u < 2; ++u)
+            if (i0 + u < n) {
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) out16[jj] += __uint_as_float(v[u][jj]);
+            }
+        }
       };
       if (g.parts > 1) {
         // part of a split slot: fp32 partial of this warp's 32 columns; the last of the slot's
@@ -1847,7 +1851,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_before();
         mbar_arrive(&tempty[buf]);
-        ++it;
         __threadfence();
         __syncwarp();
         int last = 0;
@@ -1881,6 +1884,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         continue;
       }
+      // 16 rank columns at a time: their tensor-memory loads, then their 16-byte stores (measured
+      // faster than reading the whole row before the first store)
       for (int j0 = 0; j0 < r_pad; j0 += 16) {
         float v[16];
         load_sum16(j0, v);
@@ -1888,7 +1893,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&tempty[buf]);
-      ++it;
     }
   }
 
@@ -2160,15 +2164,13 @@ cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables
   if (p.n_stages > kGramMaxStages) p.n_stages = kGramMaxStages;
   const int fmt = dtype == LF_BF16 ? 1 : 0;
   const int width = planes * tb.r_pad;  // MMA N
-  // at least two accumulation chains (rotating over K steps, added in fixed order: see kRoleChains)
-  // where they fit, then two accumulator buffers where they fit
+  // two accumulator buffers (one per epilogue set), each with as many accumulation chains
+  // (rotating over K steps, added in fixed order: see kRoleChains) as fit, up to four
   p.chains = 4;
-  while (p.chains > 2 && 2 * p.chains * width > 512) p.chains >>= 1;
-  while (p.chains > 1 && p.chains * width > 512) p.chains >>= 1;
+  while (p.chains > 1 && 2 * p.chains * width > 512) p.chains >>= 1;
   p.acc_cols = p.chains * width;
-  p.tmem_cols = 512;  // one CTA per SM: the whole TMEM, as many accumulators as fit
-  p.n_bufs = p.tmem_cols / p.acc_cols;
-  if (p.n_bufs > kGramMaxBufs) p.n_bufs = kGramMaxBufs;
+  p.tmem_cols = 512;  // one CTA per SM: the whole TMEM
+  p.n_bufs = 2;
   p.idesc = umma_idesc_f16(kBM, width, fmt, 1, 1);
   p.s_layout = umma_layout_for_span(tb.r_pad * 2);
   p.s_sbo = sw_sbo(tb.r_pad);
@@ -2177,8 +2179,10 @@ cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables
   if (tb.n_slots == 0 || most == 0) return cudaSuccess;
   const int grid = static_cast<int>(most < num_sms ? most : num_sms);
   if (scratch != nullptr && tb.n_slots <= kGramMaxSlots) {
-    // Parts of at most ~half a CTA's even share of segment-tile steps.
-    const int64_t share = (steps + 2 * grid - 1) / (2 * grid);
+    // Parts of at most ~an eighth of a CTA's even share of segment-tile steps: dealt zig-zag,
+    // largest first, parts that small leave the busiest CTA within ~10% of the mean (a quarter
+    // share: ~25%; a half share: ~40% at 16 Zipf-sized adapters).
+    const int64_t share = (steps + 8 * grid - 1) / (8 * grid);
     p.cap = static_cast<int>(share < 2 ? 2 : share);
     p.partial = static_cast<float*>(scratch);
     p.counters = reinterpret_cast<uint64_t*>(static_cast<char*>(scratch) +
@@ -2191,11 +2195,11 @@ cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables
   if (dtype == LF_BF16) {
     e = ensure_smem(tc_gram_kernel<__nv_bfloat16>, kGramSmem);
     if (e != cudaSuccess) return e;
-    tc_gram_kernel<__nv_bfloat16><<<grid, kThreads, kGramSmem, st>>>(jobs[0].d_map, jobs[0].s_map, d1, s1, p);
+    tc_gram_kernel<__nv_bfloat16><<<grid, kGramThreads, kGramSmem, st>>>(jobs[0].d_map, jobs[0].s_map, d1, s1, p);
   } else {
     e = ensure_smem(tc_gram_kernel<__half>, kGramSmem);
     if (e != cudaSuccess) return e;
-    tc_gram_kernel<__half><<<grid, kThreads, kGramSmem, st>>>(jobs[0].d_map, jobs[0].s_map, d1, s1, p);
+    tc_gram_kernel<__half><<<grid, kGramThreads, kGramSmem, st>>>(jobs[0].d_map, jobs[0].s_map, d1, s1, p);
   }
   return cudaGetLastError();
 }
