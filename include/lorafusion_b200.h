@@ -336,6 +336,8 @@ LF_API int lf_forward_host(const lf_problem* prob, const lf_host_chunk* chunks, 
  *    current); make that first call before any stream capture.
  *  - All calls on a device share the one array: calls whose work overlaps on the GPU (other
  *    streams, other host threads) race on it and must be serialized by the caller.
+ *  - The array's address is kept per device ordinal for the life of the process: do not use this
+ *    entry point (or the library) across a cudaDeviceReset of that device.
  */
 #define LF_NOALLOC_SCRATCH_BYTES (16u << 20)
 LF_API int lf_forward_noalloc(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,

@@ -22,7 +22,9 @@ from lorafusion_b200.scheduler import Request, build_microbatch, bucket_by_adapt
 
 
 class Coordinator:
-    """Routes a batch of per-adapter requests through one fused forward pass."""
+    """Serves a list of requests, each tied to one adapter, with a single call of the backend's
+    fused forward: the requests' rows are packed into tiles, the op runs once on the packed batch,
+    and each request gets its own rows of the result back (keyed by request id)."""
 
     def __init__(
         self,

@@ -1,9 +1,8 @@
 """Generate golden fixtures by running lorafusion's own reference code.
 
-Run in a container that has the reference checkout (read-only) at
-``/root/reference`` (or pass ``--ref``):
+Run where a checkout of the reference is available (read-only), giving its path:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --ref <path of the reference checkout>
 
 It writes, next to this file:
 
@@ -41,7 +40,7 @@ def _bf16_bits(t: torch.Tensor) -> np.ndarray:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="path of a checkout of the reference (read only)")
     args = ap.parse_args()
     sys.path.insert(0, REPO)
     sys.path.insert(0, args.ref)
