@@ -58,11 +58,11 @@ typedef enum lf_dtype { LF_F32 = 0, LF_BF16 = 1, LF_F16 = 2 } lf_dtype;
 typedef struct lf_plan_info {
   int32_t total_rows;      /* T */
   int32_t n_routes;
-  int32_t n_slots;         /* adapters that own at least one route, in order of first appearance */
+  int32_t n_slots;         /* (virtual) slots: the input slots, one of rank r > 64 as ceil(r/64) */
   int32_t n_tiles;         /* ceil(T / LF_TILE_ROWS) */
   int32_t n_segtiles;      /* route x tile intersections ("segment tiles") */
-  int32_t r_pad;           /* padded rank shared by every slot: 16, 32 or 64 */
-  int32_t max_rank;
+  int32_t r_pad;           /* padded rank shared by every (virtual) slot: 16, 32 or 64 */
+  int32_t max_rank;        /* largest input slot rank */
   int32_t rank_total;      /* sum of slot ranks: rows of the concatenated grad_a blocks */
   int32_t n_shrink_units;  /* (tile, run of <= 64/r_pad segment tiles) work units of the shrink */
   int32_t table_words;     /* int32 words of the table in use */
@@ -93,7 +93,8 @@ typedef struct lf_plan_info {
   int32_t off_tile_unit;   /* [n_tiles+1]  CSR: shrink units of each row tile */
 } lf_plan_info;
 
-/* Upper bound on the int32 words lf_plan_tables needs. */
+/* Upper bound on the int32 words lf_plan_tables needs when every slot rank is at most 64 (with
+ * larger ranks lf_plan_tables reports the words it needs: LF_ERR_CAPACITY, info->table_words). */
 LF_API int32_t lf_plan_table_words(int32_t n_routes, int32_t total_rows, int32_t n_slots);
 
 /*
@@ -103,9 +104,16 @@ LF_API int32_t lf_plan_table_words(int32_t n_routes, int32_t total_rows, int32_t
  * TileRoutingConfig.routes (lorafusion/ops/config.py:29-47) mapped to adapter slots.
  * Checks what TileRoutingConfig.validate checks (config.py:55-69) -> LF_ERR_ROUTING.
  *   route_start/route_end/route_slot : [n_routes]
- *   slot_rank/slot_scale             : [n_slots] rank r_i and scaling alpha_i/r_i
+ *   slot_rank/slot_scale             : [n_slots] rank r_i (any positive rank, as mock_ops allows) and
+ *                                      scaling alpha_i/r_i
  *   table                            : host buffer of table_capacity int32 words
- * The caller copies `table` (info->table_words words) to device memory.
+ * A slot of rank r > 64 is carried as ceil(r/64) consecutive virtual slots of ranks 64, ..., 64,
+ * r - 64 (ceil(r/64) - 1): slot s's virtual slots follow those of slots < s, each over all of s's
+ * rows (the LoRA product is the sum over the chunks).  Everything indexed by slot below (the
+ * packed slabs of lf_pack_adapters, grad_a / grad_b blocks, info->n_slots) is per virtual slot;
+ * a slot's grad_a rows are its virtual slots' rows, consecutive.
+ * The caller copies `table` (info->table_words words) to device memory.  A table_capacity below the
+ * need returns LF_ERR_CAPACITY with info->table_words set to the need.
  */
 LF_API int lf_plan_tables(const int32_t* route_start, const int32_t* route_end, const int32_t* route_slot,
                    int32_t n_routes, int32_t total_rows, const int32_t* slot_rank, const float* slot_scale,

@@ -171,14 +171,49 @@ def _routes(routing, total_rows: int) -> _Routes:
     return rec
 
 
+MAX_SLOT_RANK = 64  # lf_plan_tables carries a slot of larger rank as several virtual slots
+
+
+def _virtual_slots(ranks):
+    """(slot index, first rank row, rank) of every virtual slot, in table order: a slot of rank
+    r > 64 becomes ceil(r/64) chunks of 64 ranks and a remainder (lf_plan_tables' rule)."""
+    return tuple((i, c0, min(MAX_SLOT_RANK, r - c0)) for i, r in enumerate(ranks) for c0 in range(0, r, MAX_SLOT_RANK))
+
+
+def _plan_tables(starts, ends, route_slot, total_rows, ranks, scales, n_slots):
+    """lf_plan_tables into a pinned host buffer (grown once when high ranks need more words)."""
+    L = nat.lib()
+    n_routes = len(starts)
+    cap = L.lf_plan_table_words(n_routes, total_rows, n_slots)
+    if cap < 0:
+        raise ValueError("routing too large for int32 tables")
+    rk = np.asarray(ranks, dtype=np.int32)
+    sc = np.asarray(scales, dtype=np.float32)
+    i32p = ctypes.POINTER(ctypes.c_int32)
+    for _ in range(2):
+        table = torch.empty(max(cap, 1), dtype=torch.int32, pin_memory=True)
+        info = nat.PlanInfo()
+        rc = L.lf_plan_tables(
+            starts.ctypes.data_as(i32p), ends.ctypes.data_as(i32p), route_slot.ctypes.data_as(i32p), n_routes,
+            total_rows, rk.ctypes.data_as(i32p), sc.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n_slots,
+            ctypes.cast(table.data_ptr(), i32p), cap, ctypes.byref(info))
+        if rc == nat.LF_ERR_CAPACITY and info.table_words > cap:
+            cap = info.table_words
+            continue
+        nat.check(rc, "lf_plan_tables")
+        return info, table
+    raise RuntimeError("lf_plan_tables: table size did not converge")
+
+
 class _Plan:
-    __slots__ = ("info", "table_dev", "slots", "ranks")
+    __slots__ = ("info", "table_dev", "slots", "ranks", "vslots")
 
     def __init__(self, info, table_dev, slots, ranks):
         self.info = info
         self.table_dev = table_dev
         self.slots = slots
         self.ranks = ranks
+        self.vslots = _virtual_slots(ranks)
 
 
 class _AdapterSet:
@@ -256,21 +291,7 @@ def _plan(rts: _Routes, aset: _AdapterSet, total_rows: int, device: torch.device
 
 
 def _build_plan(rts: _Routes, ranks, scales, total_rows: int, device) -> _Plan:
-    L = nat.lib()
-    n_routes = len(rts.starts)
-    cap = L.lf_plan_table_words(n_routes, total_rows, len(rts.slots))
-    if cap < 0:
-        raise ValueError("routing too large for int32 tables")
-    table = torch.empty(max(cap, 1), dtype=torch.int32, pin_memory=True)
-    info = nat.PlanInfo()
-    rk = np.asarray(ranks, dtype=np.int32)
-    sc = np.asarray(scales, dtype=np.float32)
-    i32p = ctypes.POINTER(ctypes.c_int32)
-    rc = L.lf_plan_tables(
-        rts.starts.ctypes.data_as(i32p), rts.ends.ctypes.data_as(i32p), rts.route_slot.ctypes.data_as(i32p),
-        n_routes, total_rows, rk.ctypes.data_as(i32p), sc.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
-        len(rts.slots), ctypes.cast(table.data_ptr(), i32p), cap, ctypes.byref(info))
-    nat.check(rc, "lf_plan_tables")
+    info, table = _plan_tables(rts.starts, rts.ends, rts.route_slot, total_rows, ranks, scales, len(rts.slots))
     table_dev = table[: max(info.table_words, 1)].to(device, non_blocking=True)
     return _Plan(info, table_dev, rts.slots, ranks)
 
@@ -287,8 +308,14 @@ def _pack(plan: _Plan, aset: _AdapterSet, dtype: torch.dtype, K: int, N: int, de
                     f"in_features={K}, out_features={N}")
             if a.device != device or b.device != device:
                 raise ValueError(f"adapter {aid}: LoRA weights must live on {device}")
-        a_src = [t if t.is_contiguous() else t.contiguous() for t in aset.a]
-        b_src = [t if t.is_contiguous() else t.contiguous() for t in aset.b]
+        # one source matrix per virtual slot: A_i's rank rows [c0, c0 + r), B_i's columns likewise
+        a_src, b_src = [], []
+        for i, c0, r in plan.vslots:
+            a, b = aset.a[i], aset.b[i]
+            if r != a.shape[0]:
+                a, b = a[c0:c0 + r], b[:, c0:c0 + r]
+            a_src.append(a if a.is_contiguous() else a.contiguous())
+            b_src.append(b if b.is_contiguous() else b.contiguous())
         entry = aset.packs[key] = {"src": (a_src, b_src)}
     want = ("a", "b", "bt", "at") if backward else ("a", "b")
     missing = [w for w in want if w not in entry]
@@ -300,9 +327,10 @@ def _pack(plan: _Plan, aset: _AdapterSet, dtype: torch.dtype, K: int, N: int, de
 def _fill_packs(entry, plan: _Plan, dtype, K, N, device, which) -> None:
     L = nat.lib()
     a_src, b_src = entry["src"]
-    n = len(plan.slots)
+    n = len(plan.vslots)
     rp = plan.info.r_pad
-    ranks_dev = torch.tensor(plan.ranks if n else [0], dtype=torch.int32).to(device, non_blocking=True)
+    vranks = [r for _, _, r in plan.vslots]
+    ranks_dev = torch.tensor(vranks if n else [0], dtype=torch.int32).to(device, non_blocking=True)
     stream = torch.cuda.current_stream(device).cuda_stream
     dst_code = _DTYPE_CODE[dtype]
     for w in which:
@@ -615,12 +643,23 @@ def prepare_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, routing
 def _grad_dicts(plan: _Plan, ga_flat, gb_flat, K: int, N: int):
     """Per-adapter views of the packed gradients: dA_i rows [rank_prefix_i, +r_i) of a
     [rank_total, K] matrix, dB_i the [N, r_i] block at element rank_prefix_i * N.  One split per
-    run of equal ranks keeps the view count per call, not per adapter, in Python."""
+    run of equal ranks keeps the view count per call, not per adapter, in Python.  An adapter of
+    rank > 64 (several virtual slots) gets its dB blocks joined along the rank dimension."""
     slots, ranks = plan.slots, plan.ranks
     rtot = plan.info.rank_total
     if not slots:
         return {}, {}
     grad_a = dict(zip(slots, ga_flat[:rtot * K].view(rtot, K).split(ranks)))
+    if len(plan.vslots) != len(slots):
+        grad_b, off = {}, 0
+        for aid, r in zip(slots, ranks):
+            blocks = []
+            for c0 in range(0, r, MAX_SLOT_RANK):
+                rv = min(MAX_SLOT_RANK, r - c0)
+                blocks.append(gb_flat[off * N:(off + rv) * N].view(N, rv))
+                off += rv
+            grad_b[aid] = blocks[0] if len(blocks) == 1 else torch.cat(blocks, dim=1)
+        return grad_a, grad_b
     grad_b: dict[int, torch.Tensor] = {}
     i, off, n = 0, 0, len(slots)
     while i < n:
@@ -649,7 +688,6 @@ class _ChunkPlans:
         rk = np.asarray(ranks, dtype=np.int32)
         sc = np.asarray(scales, dtype=np.float32)
         n_slots = len(rts.slots)
-        i32p = ctypes.POINTER(ctypes.c_int32)
         bounds = list(range(0, total_rows, chunk_rows))
         self.n = len(bounds)
         self.array = (nat.HostChunk * max(self.n, 1))()
@@ -660,16 +698,7 @@ class _ChunkPlans:
             starts = np.ascontiguousarray(np.maximum(rts.starts[sel], c0) - c0, dtype=np.int32)
             ends = np.ascontiguousarray(np.minimum(rts.ends[sel], c1) - c0, dtype=np.int32)
             rslot = np.ascontiguousarray(rts.route_slot[sel], dtype=np.int32)
-            cap = L.lf_plan_table_words(len(starts), c1 - c0, n_slots)
-            if cap < 0:
-                raise ValueError("routing too large for int32 tables")
-            table = torch.empty(max(cap, 1), dtype=torch.int32, pin_memory=True)
-            info = nat.PlanInfo()
-            rc = L.lf_plan_tables(starts.ctypes.data_as(i32p), ends.ctypes.data_as(i32p), rslot.ctypes.data_as(i32p),
-                                  len(starts), c1 - c0, rk.ctypes.data_as(i32p),
-                                  sc.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), n_slots,
-                                  ctypes.cast(table.data_ptr(), i32p), cap, ctypes.byref(info))
-            nat.check(rc, "lf_plan_tables")
+            info, table = _plan_tables(starts, ends, rslot, c1 - c0, rk, sc, n_slots)
             table_dev = table[: max(info.table_words, 1)].to(device, non_blocking=True)
             self.infos.append(info)
             self.tables.append(table_dev)

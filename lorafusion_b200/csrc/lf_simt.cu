@@ -124,7 +124,8 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const T* __restrict__ P,
     }
     __syncthreads();
   }
-  // LoRA expand: each row adds S_ext[st][row] . L[slot][n][:]
+  // LoRA expand: each row adds S_ext[st][row] . L[slot][n][:] for every segment tile st holding the
+  // row (one per virtual slot of its adapter), in segment-tile order
   const int r_pad = tb.r_pad;
   if (lpk != nullptr) {
     const int tile = m0 / LF_TILE_ROWS;
@@ -134,20 +135,19 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const T* __restrict__ P,
       const int gr = m0 + tr * 4 + i;
       if (gr >= Trows) continue;
       const int row = gr - tile * LF_TILE_ROWS;
-      int st = -1;
-      for (int j = st_b; j < st_e; ++j)
-        if (row >= tb.st_lo(j) && row < tb.st_hi(j)) st = j;
-      if (st < 0) continue;
-      const double* srow = s_ext + (static_cast<int64_t>(st) * LF_TILE_ROWS + row) * r_pad;
-      const T* lb = lpk + static_cast<int64_t>(tb.st_slot(st)) * Nout * r_pad;
+      for (int st = st_b; st < st_e; ++st) {
+        if (row < tb.st_lo(st) || row >= tb.st_hi(st)) continue;
+        const double* srow = s_ext + (static_cast<int64_t>(st) * LF_TILE_ROWS + row) * r_pad;
+        const T* lb = lpk + static_cast<int64_t>(tb.st_slot(st)) * Nout * r_pad;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int gn = n0 + tc * 4 + j;
-        if (gn >= Nout) continue;
-        double d = 0.0;
-        for (int q = 0; q < r_pad; ++q)
-          d = fma(srow[q], static_cast<double>(to_f(lb[static_cast<int64_t>(gn) * r_pad + q])), d);
-        acc[i][j] += d;
+        for (int j = 0; j < 4; ++j) {
+          const int gn = n0 + tc * 4 + j;
+          if (gn >= Nout) continue;
+          double d = 0.0;
+          for (int q = 0; q < r_pad; ++q)
+            d = fma(srow[q], static_cast<double>(to_f(lb[static_cast<int64_t>(gn) * r_pad + q])), d);
+          acc[i][j] += d;
+        }
       }
     }
   }

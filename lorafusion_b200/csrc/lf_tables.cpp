@@ -13,11 +13,12 @@
 
 namespace {
 
+constexpr int kMaxSlotRank = 64;  // largest rank one (virtual) slot carries
+
 int pad_rank(int r) {
   if (r <= 16) return 16;
   if (r <= 32) return 32;
-  if (r <= 64) return 64;
-  return -1;
+  return 64;
 }
 
 }  // namespace
@@ -52,17 +53,27 @@ extern "C" int lf_plan_tables(const int32_t* route_start, const int32_t* route_e
   }
   if (expect != total_rows) return LF_ERR_ROUTING;
 
+  // A slot of rank r > 64 becomes ceil(r / 64) consecutive virtual slots of ranks 64, ..., 64 and
+  // the remainder, over the same rows: y = sum over chunks c of s (x A_c^T) B_c^T is the same
+  // product, and every kernel adds all the LoRA terms of a row.  `vslot0[s]` is the first virtual
+  // slot of input slot s; the tables and info->n_slots count virtual slots.
+  std::vector<int32_t> vslot0(n_slots + 1, 0), vrank, vslot_of;
   int max_rank = 1;
   for (int32_t s = 0; s < n_slots; ++s) {
     if (slot_rank[s] <= 0) return LF_ERR_INVALID_ARG;
     max_rank = std::max(max_rank, static_cast<int>(slot_rank[s]));
+    for (int32_t c0 = 0; c0 < slot_rank[s]; c0 += kMaxSlotRank) {
+      vrank.push_back(std::min(kMaxSlotRank, slot_rank[s] - c0));
+      vslot_of.push_back(s);
+    }
+    vslot0[s + 1] = static_cast<int32_t>(vrank.size());
   }
-  const int r_pad = pad_rank(max_rank);
-  if (r_pad < 0) return LF_ERR_UNSUPPORTED;
+  const int32_t n_vslots = static_cast<int32_t>(vrank.size());
+  const int r_pad = pad_rank(std::min(max_rank, kMaxSlotRank));
 
   const int32_t n_tiles = (total_rows + LF_TILE_ROWS - 1) / LF_TILE_ROWS;
 
-  // segment tiles in route order == row order
+  // segment tiles in route order == row order (the virtual slots of a route one after another)
   std::vector<int32_t> st_tile, st_lo, st_hi, st_slot, st_route;
   std::vector<int32_t> tile_first(n_tiles + 1, 0);
   for (int32_t i = 0; i < n_routes; ++i) {
@@ -70,14 +81,17 @@ extern "C" int lf_plan_tables(const int32_t* route_start, const int32_t* route_e
     while (r0 < r1) {
       const int32_t t = r0 / LF_TILE_ROWS;
       const int32_t tile_end = std::min<int64_t>(static_cast<int64_t>(t + 1) * LF_TILE_ROWS, r1);
-      st_tile.push_back(t);
-      st_lo.push_back(r0 - t * LF_TILE_ROWS);
-      st_hi.push_back(tile_end - t * LF_TILE_ROWS);
-      st_slot.push_back(route_slot[i]);
-      st_route.push_back(i);
+      for (int32_t v = vslot0[route_slot[i]]; v < vslot0[route_slot[i] + 1]; ++v) {
+        st_tile.push_back(t);
+        st_lo.push_back(r0 - t * LF_TILE_ROWS);
+        st_hi.push_back(tile_end - t * LF_TILE_ROWS);
+        st_slot.push_back(v);
+        st_route.push_back(i);
+      }
       r0 = tile_end;
     }
   }
+  n_slots = n_vslots;  // from here on: virtual slots
   const int32_t n_st = static_cast<int32_t>(st_tile.size());
   for (int32_t j = 0; j < n_st; ++j) tile_first[st_tile[j] + 1]++;
   for (int32_t t = 0; t < n_tiles; ++t) tile_first[t + 1] += tile_first[t];
@@ -91,7 +105,7 @@ extern "C" int lf_plan_tables(const int32_t* route_start, const int32_t* route_e
     for (int32_t j = 0; j < n_st; ++j) slot_list[fill[st_slot[j]]++] = j;
   }
   std::vector<int32_t> rank_prefix(n_slots + 1, 0);
-  for (int32_t s = 0; s < n_slots; ++s) rank_prefix[s + 1] = rank_prefix[s] + slot_rank[s];
+  for (int32_t s = 0; s < n_slots; ++s) rank_prefix[s + 1] = rank_prefix[s] + vrank[s];
   std::vector<int32_t> order(n_slots);
   std::iota(order.begin(), order.end(), 0);
   std::stable_sort(order.begin(), order.end(), [&](int32_t a, int32_t b) {
@@ -169,7 +183,10 @@ extern "C" int lf_plan_tables(const int32_t* route_start, const int32_t* route_e
   info->off_pl_b = take(n_pl);
   info->off_pl_slot = take(n_pl);
   info->off_tile_unit = take(n_tiles + 1);
-  if (w > table_capacity) return LF_ERR_CAPACITY;
+  if (w > table_capacity) {
+    info->table_words = w;  // what a retry needs
+    return LF_ERR_CAPACITY;
+  }
 
   auto put = [&](int32_t off, const std::vector<int32_t>& v) {
     if (!v.empty()) std::memcpy(table + off, v.data(), v.size() * sizeof(int32_t));
@@ -181,12 +198,12 @@ extern "C" int lf_plan_tables(const int32_t* route_start, const int32_t* route_e
   put(info->off_st_slot, st_slot);
   put(info->off_st_route, st_route);
   for (int32_t j = 0; j < n_st; ++j) {
-    const float s = slot_scale[st_slot[j]];
+    const float s = slot_scale[vslot_of[st_slot[j]]];
     std::memcpy(table + info->off_st_scale + j, &s, sizeof(float));
   }
   put(info->off_slot_st, slot_first);
   put(info->off_slot_list, slot_list);
-  if (n_slots) std::memcpy(table + info->off_slot_rank, slot_rank, n_slots * sizeof(int32_t));
+  put(info->off_slot_rank, vrank);
   put(info->off_rank_prefix, rank_prefix);
   put(info->off_slot_order, order);
   put(info->off_unit_tile, u_tile);

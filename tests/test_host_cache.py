@@ -59,6 +59,7 @@ class _Info:
 class _PlanStub:
     def __init__(self, slots, ranks):
         self.slots, self.ranks, self.info = tuple(slots), tuple(ranks), _Info(sum(ranks))
+        self.vslots = ops._virtual_slots(ranks)
 
 
 @pytest.mark.parametrize("ranks", [[16] * 5, [16, 16, 8, 32, 32, 4, 4, 64], [1], []])
@@ -79,6 +80,24 @@ def test_grad_dicts_are_views_in_slot_order(ranks):
         assert torch.equal(db[aid], gb[off * N:(off + r) * N].view(N, r))
         assert da[aid].data_ptr() == ga[off * K:].data_ptr()  # views, no copies
         off += r
+
+
+def test_grad_dicts_of_ranks_above_64_join_virtual_slot_blocks():
+    """An adapter of rank 130 has three virtual slots (64, 64, 2): its dA rows are one view, its dB
+    is the three [N, r_v] blocks joined along the rank dimension."""
+    K, N = 8, 6
+    ranks = [16, 130, 8]
+    slots = [4, 9, 2]
+    plan = _PlanStub(slots, ranks)
+    assert plan.vslots == ((0, 0, 16), (1, 0, 64), (1, 64, 64), (1, 128, 2), (2, 0, 8))
+    rtot = sum(ranks)
+    ga = torch.arange(rtot * K, dtype=torch.float32)
+    gb = torch.arange(rtot * N, dtype=torch.float32)
+    da, db = ops._grad_dicts(plan, ga, gb, K, N)
+    assert da[9].shape == (130, K) and torch.equal(da[9], ga[16 * K:146 * K].view(130, K))
+    blocks = [gb[(16 + c0) * N:(16 + c0 + r) * N].view(N, r) for c0, r in ((0, 64), (64, 64), (128, 2))]
+    assert db[9].shape == (N, 130) and db[9].is_contiguous() and torch.equal(db[9], torch.cat(blocks, dim=1))
+    assert torch.equal(db[2], gb[146 * N:154 * N].view(N, 8)) and torch.equal(db[4], gb[:16 * N].view(N, 16))
 
 
 def test_many_adapter_sets_on_one_routing_all_stay_cached():

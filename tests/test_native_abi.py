@@ -17,13 +17,17 @@ def _tables(routes, total_rows, ranks, scales):
     rk = np.array(ranks, dtype=np.int32)
     sc = np.array(scales, dtype=np.float32)
     cap = L.lf_plan_table_words(len(routes), total_rows, len(ranks))
-    table = np.zeros(max(cap, 1), dtype=np.int32)
-    info = nat.PlanInfo()
     i32p = ctypes.POINTER(ctypes.c_int32)
-    rc = L.lf_plan_tables(starts.ctypes.data_as(i32p), ends.ctypes.data_as(i32p), slots.ctypes.data_as(i32p),
-                          len(routes), total_rows, rk.ctypes.data_as(i32p),
-                          sc.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), len(ranks),
-                          table.ctypes.data_as(i32p), cap, ctypes.byref(info))
+    for _ in range(2):  # ranks above 64 may need more than the bound: the call reports the need
+        table = np.zeros(max(cap, 1), dtype=np.int32)
+        info = nat.PlanInfo()
+        rc = L.lf_plan_tables(starts.ctypes.data_as(i32p), ends.ctypes.data_as(i32p), slots.ctypes.data_as(i32p),
+                              len(routes), total_rows, rk.ctypes.data_as(i32p),
+                              sc.ctypes.data_as(ctypes.POINTER(ctypes.c_float)), len(ranks),
+                              table.ctypes.data_as(i32p), cap, ctypes.byref(info))
+        if rc != nat.LF_ERR_CAPACITY or info.table_words <= cap:
+            break
+        cap = info.table_words
     return rc, info, table
 
 
@@ -118,7 +122,6 @@ def test_tables_errors_and_padding():
     assert _tables([(0, 10, 0), (12, 20, 0)], 20, [8], [2.0])[0] == nat.LF_ERR_ROUTING
     assert _tables([(0, 10, 0)], 20, [8], [2.0])[0] == nat.LF_ERR_ROUTING
     assert _tables([(0, 10, 1)], 10, [8], [2.0])[0] == nat.LF_ERR_ROUTING
-    assert _tables([(0, 10, 0)], 10, [65], [2.0])[0] == nat.LF_ERR_UNSUPPORTED
     for r, pad in [(1, 16), (16, 16), (17, 32), (32, 32), (33, 64), (64, 64)]:
         rc, info, _ = _tables([(0, 300, 0)], 300, [r], [1.0])
         assert rc == 0 and info.r_pad == pad and info.rank_total == r
@@ -196,3 +199,42 @@ def test_host_streamed_forward_rejects_bad_chunk_lists():
     assert call(2) == nat.LF_ERR_INVALID_ARG          # chunk rows differ from its tables'
     assert call(0, T=0) == 0                          # nothing to do
     assert L.lf_forward_host(None, chunks, 0, p, p, p, p, p, 64, None, None, None) == nat.LF_ERR_INVALID_ARG
+
+
+def test_ranks_above_64_become_virtual_slots():
+    """A slot of rank r > 64 is carried as ceil(r/64) consecutive virtual slots (64, ..., remainder)
+    over the same rows; the other slots keep their order; a too-small table buffer reports the need."""
+    routes = [(0, 100, 0), (100, 300, 1), (300, 310, 2)]
+    rc, info, table = _tables(routes, 310, [16, 130, 64], [2.0, 0.5, 1.0])
+    assert rc == 0
+    assert info.n_slots == 1 + 3 + 1 and info.r_pad == 64 and info.max_rank == 130 and info.rank_total == 210
+    assert _sec(info, table, "slot_rank", info.n_slots).tolist() == [16, 64, 64, 2, 64]
+    assert _sec(info, table, "rank_prefix", info.n_slots + 1).tolist() == [0, 16, 80, 144, 146, 210]
+    lo, hi = _sec(info, table, "st_lo", info.n_segtiles), _sec(info, table, "st_hi", info.n_segtiles)
+    tile, slot = _sec(info, table, "st_tile", info.n_segtiles), _sec(info, table, "st_slot", info.n_segtiles)
+    scale = _sec(info, table, "st_scale", info.n_segtiles).view(np.float32)
+    rows = {}
+    for j in range(info.n_segtiles):
+        rows.setdefault(int(slot[j]), []).append((int(tile[j]) * 128 + int(lo[j]), int(tile[j]) * 128 + int(hi[j])))
+    assert rows[0] == [(0, 100)]
+    for v in (1, 2, 3):  # the rank-130 slot: three virtual slots over rows 100..300, scaling 0.5
+        assert rows[v] == [(100, 128), (128, 256), (256, 300)]
+        assert np.all(scale[slot == v] == 0.5)
+    assert rows[4] == [(300, 310)]
+    # within a tile, the virtual slots of one route follow each other
+    t1 = [int(v) for v, t in zip(slot, tile) if t == 1]
+    assert t1 == [1, 2, 3]
+    # a buffer that is too small: LF_ERR_CAPACITY and the words needed
+    i32p = ctypes.POINTER(ctypes.c_int32)
+    starts = np.array([s for s, _, _ in routes], np.int32)
+    ends = np.array([e for _, e, _ in routes], np.int32)
+    slots = np.array([a for _, _, a in routes], np.int32)
+    rk = np.array([16, 700, 64], np.int32)
+    sc = np.array([2.0, 0.5, 1.0], np.float32)
+    cap = nat.lib().lf_plan_table_words(3, 310, 3)
+    buf = np.zeros(cap, np.int32)
+    inf = nat.PlanInfo()
+    rc = nat.lib().lf_plan_tables(starts.ctypes.data_as(i32p), ends.ctypes.data_as(i32p), slots.ctypes.data_as(i32p),
+                                  3, 310, rk.ctypes.data_as(i32p), sc.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
+                                  3, buf.ctypes.data_as(i32p), cap, ctypes.byref(inf))
+    assert rc == nat.LF_ERR_CAPACITY and inf.table_words > cap

@@ -559,3 +559,15 @@ def test_backward_stages_match_oracle(order):
         _check(ga[k], case["ga"][k], BF16_TOL, f"grad_a[{k}]")
         _check(gb[k], case["gb"][k], BF16_TOL, f"grad_b[{k}]")
     assert nat.device_error() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32], ids=["bf16", "f16", "f32"])
+def test_ranks_above_64_match_oracle(dtype):
+    """Adapters of rank 65 and 130 (carried as virtual slots of at most 64 ranks over the same rows)
+    beside a rank-16 one: forward and backward match the oracle; gradient shapes are the adapters'
+    own [r, K] / [N, r], contiguous."""
+    routes = _routes_from_sizes([200, 130, 3, 267], [0, 1, 2, 1])
+    case = _random_case(61, 600, 256, 320, routes, {0: 65, 1: 130, 2: 16}, dtype)
+    _run_and_compare(case, dtype, FP32_TOL if dtype == torch.float32 else BF16_TOL)
+    from lorafusion_b200 import _native as nat
+    assert nat.device_error() == 0
