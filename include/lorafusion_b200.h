@@ -234,8 +234,9 @@ LF_API int lf_backward_launch_count(const lf_problem* prob, const lf_plan_info* 
  *   0  no cooperative launches: each routed shrink is an ordinary launch of its own and no tail
  *     is K-split.  For profilers and SM-partitioned GPUs, which refuse cooperative launches (a
  *     refused launch also turns co-scheduling off for that device by itself).
- * Other values return LF_ERR_INVALID_ARG.  The default is 1, or 0 when a CUDA tool is injected
- * into the process (CUDA_INJECTION64_PATH set, as Nsight Compute and compute-sanitizer do).
+ * Other values return LF_ERR_INVALID_ARG.  The default is 1, or 0 when a CUDA tool (Nsight Compute,
+ * compute-sanitizer) is injected into the process: its injection variables are set or its
+ * injection library is mapped when the library loads.
  * No counterpart in the reference.
  */
 LF_API int lf_set_co_scheduling(int32_t enable);

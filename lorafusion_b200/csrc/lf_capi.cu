@@ -5,6 +5,7 @@
 
 #include <atomic>
 #include <chrono>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -38,13 +39,29 @@ struct DeviceState {
 std::mutex g_mu;
 DeviceState g_dev[64];
 
-// A profiling or checking tool injected into the process (Nsight Compute, compute-sanitizer and
-// the other CUDA tools load through CUDA_INJECTION64_PATH) replays or serializes kernels and
-// refuses cooperative launches, so the default is then "no co-scheduled launches".
-int default_cosched_mode() {
-  const char* inj = std::getenv("CUDA_INJECTION64_PATH");
-  return (inj != nullptr && inj[0] != '\0') ? 0 : 1;
+// A profiling or checking tool injected into the process replays or serializes kernels, and a
+// co-scheduled launch (whose CTAs wait on each other) then fails, so the default is "no
+// co-scheduled launches" when one is present.  Signs of one: the variables CUDA tools set for
+// their injection (CUDA_INJECTION64_PATH; Nsight Compute's NV_NSIGHT_INJECTION_* and
+// NV_COMPUTE_PROFILER_PERFWORKS_DIR; NVIDIA_PROCESS_INJECTION_*), or an injection library mapped
+// into the process.
+bool tool_injected() {
+  for (const char* v : {"CUDA_INJECTION64_PATH", "NV_NSIGHT_INJECTION_TRANSPORT_TYPE", "NV_COMPUTE_PROFILER_PERFWORKS_DIR",
+                        "NVIDIA_PROCESS_INJECTION_CRASH_REPORTING"}) {
+    const char* x = std::getenv(v);
+    if (x != nullptr && x[0] != '\0') return true;
+  }
+  if (FILE* f = std::fopen("/proc/self/maps", "r")) {
+    char line[1024];
+    bool found = false;
+    while (!found && std::fgets(line, sizeof(line), f))
+      found = std::strstr(line, "libcuda-injection") != nullptr || std::strstr(line, "InjectionTarget") != nullptr;
+    std::fclose(f);
+    if (found) return true;
+  }
+  return false;
 }
+int default_cosched_mode() { return tool_injected() ? 0 : 1; }
 // process-wide switch (lf_set_co_scheduling): 0 off, 1 dedicated, 2 prologue
 std::atomic<int> g_cosched_mode{default_cosched_mode()};
 

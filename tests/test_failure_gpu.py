@@ -72,3 +72,23 @@ def test_wait_limit_arguments():
     assert L.lf_set_wait_limit(61_000_000_000) == nat.LF_ERR_INVALID_ARG
     assert L.lf_set_wait_limit(0) == nat.LF_OK
     assert L.lf_inject_stale_ready(-1) == nat.LF_ERR_INVALID_ARG
+
+
+def test_injected_tool_turns_co_scheduling_off_by_default():
+    """Under an injected CUDA tool (Nsight Compute sets NV_NSIGHT_INJECTION_* for its target), whose
+    kernel replay breaks launches whose CTAs wait on each other, the library starts with
+    co-scheduled launches off; without one, on."""
+    import os
+    import subprocess
+    import sys
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = "from lorafusion_b200 import _native as nat; print(nat.co_scheduling()[0])"
+    tool_vars = ("CUDA_INJECTION64_PATH", "NV_NSIGHT_INJECTION_TRANSPORT_TYPE", "NV_COMPUTE_PROFILER_PERFWORKS_DIR",
+                 "NVIDIA_PROCESS_INJECTION_CRASH_REPORTING")
+    clean = {k: v for k, v in os.environ.items() if k not in tool_vars}
+    plain = subprocess.run([sys.executable, "-c", code], cwd=repo, env=clean, capture_output=True, text=True,
+                           timeout=300)
+    tooled = subprocess.run([sys.executable, "-c", code], cwd=repo, env=dict(clean, NV_NSIGHT_INJECTION_TRANSPORT_TYPE="uds"),
+                            capture_output=True, text=True, timeout=300)
+    assert plain.returncode == 0 and tooled.returncode == 0, plain.stderr + tooled.stderr
+    assert plain.stdout.split()[-1] == "1" and tooled.stdout.split()[-1] == "0"
