@@ -196,8 +196,8 @@ LF_API size_t lf_forward_fixed_workspace_bytes(const lf_plan_info* info, int32_t
 
 /*
  * lf_forward with the K-split tail's scratch in a buffer of its own (`tail_dev`, `tail_bytes`:
- * up to lf_forward_workspace_bytes - lf_forward_fixed_workspace_bytes; null/0 = take it from the
- * workspace as lf_forward does), so a caller can keep the workspace, which then needs only
+ * up to lf_forward_workspace_bytes - lf_forward_fixed_workspace_bytes, 16-byte aligned, else the
+ * tail is not split; null/0 = take it from the workspace as lf_forward does), so a caller can keep the workspace, which then needs only
  * lf_forward_fixed_workspace_bytes, for a later lf_backward_sf while the tail buffer is reused.
  * Also reports, in *s_f_planes, the K-half planes of S_f = s_i x A_i^T the call left in the
  * workspace: 2 when the shrink ran inside the GEMM launch, 1 when it ran as a launch of its own, 0

@@ -246,6 +246,7 @@ PairTail tail_scratch(void* ws, size_t bytes, size_t off) {
   PairTail t{};
   if (ws == nullptr || bytes < off + kTailFlagBytes + kTailPartialBytes) return t;
   char* base = static_cast<char*>(ws) + off;
+  if (!aligned16(base)) return t;  // partial tiles are moved by bulk copies: no split tail
   t.flags = reinterpret_cast<uint64_t*>(base);
   t.partial = reinterpret_cast<float*>(base + kTailFlagBytes);
   const size_t fit = (bytes - off - kTailFlagBytes) / kTailPartialBytes;

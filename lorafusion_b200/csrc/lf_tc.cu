@@ -399,8 +399,17 @@ constexpr int kPairEntPerLane = 6;
 constexpr int kPairEntBytes = 32 * kPairEntPerLane * 2 * 4;
 // barriers: the GEMM's (and a dedicated shrink role's) at +0, a shrink prologue's at +256
 constexpr int kPairBarBytes = 512;
-static_assert((2 * kPairBars + 4 + 2) * 8 + 8 <= 256 && 256 + (2 * kRoleStages + 6) * 8 <= kPairBarBytes,
+// ... and the split tail's partial-tile loads (two buffers per epilogue warp) at +448
+constexpr int kPairTailBarOff = 448;
+static_assert((2 * kPairBars + 4 + 2) * 8 + 8 <= 256 && 256 + (2 * kRoleStages + 6) * 8 <= kPairTailBarOff &&
+                  kPairTailBarOff + 8 * 8 <= kPairBarBytes,
               "barrier area");
+// The last part of a split tail tile reads the earlier parts' partial tiles into the pipeline
+// ring (idle once its last unit's MMAs are done): per epilogue warp two buffers, each one 64-column
+// chunk (32 rows x 64 fp32 = 8 KB) of every earlier part (at most three).
+constexpr int kTailChunkBytes = 32 * 64 * 4;
+constexpr int kTailBufBytes = 3 * kTailChunkBytes;
+static_assert(4 * 2 * kTailBufBytes <= kPairStages * (kPairABytes + kPairBBytes), "tail buffers fit the ring");
 constexpr int kPairSmem = 1024 + kPairStages * (kPairABytes + kPairBBytes) + kPairOutBytes + kPairBarBytes + kPairEntBytes;
 static_assert(kPairSmem <= 227 * 1024, "pair kernel shared memory");
 
@@ -449,6 +458,10 @@ __device__ __forceinline__ void pair_raster(int t, const PairParams& p, int& mp,
   n = r / gsize;
 }
 
+// k-blocks the last part of a split tail tile runs beyond an even share (about the time an
+// earlier part takes to write its fp32 partial tile and release it)
+constexpr int kTailSkew = 6;
+
 // Work units of one GEMM pair: the full tiles t = pair + k * n_pairs of the first `rounds`
 // rounds, then at most one tail unit.  Tail unit v (counted from the last pair down) is part
 // v % parts of tail tile v / parts; partial slot = tail tile * (parts - 1) + part.
@@ -487,8 +500,11 @@ __device__ __forceinline__ PairUnit pair_unit(const PairParams& p, const PairSch
   const int v = n_pairs - 1 - pair;
   const int j = v / s.parts, q = v - j * s.parts;
   pair_raster(s.tail_base + j, p, u.mp, u.n);
-  u.kb0 = q * nkb / s.parts;
-  u.kb1 = (q + 1) * nkb / s.parts;
+  // The last part (which adds the others' partials) gets `skew` extra k-blocks, so the earlier
+  // parts' partial tiles are written while it still runs its k-loop.
+  const int skew = min(kTailSkew, nkb / (4 * s.parts));
+  u.kb0 = q * (nkb - skew) / s.parts;
+  u.kb1 = q == s.parts - 1 ? nkb : (q + 1) * (nkb - skew) / s.parts;
   u.part = s.parts > 1 ? q : -1;
   u.slot0 = j * (s.parts - 1);
   u.last = q == s.parts - 1;
@@ -781,6 +797,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* rtempty = rtfull + 2;
   uint64_t* rdrain = rtempty + 2;
   uint64_t* rpub = rdrain + 1;
+  uint64_t* tail_bar = reinterpret_cast<uint64_t*>(sOut + kPairOutBytes + kPairTailBarOff);
   int* pair_ent = reinterpret_cast<int*>(sOut + kPairOutBytes + kPairBarBytes);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -809,6 +826,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 8);  // one arrive per epilogue warp of both CTAs
     }
+    for (int b = 0; b < 8; ++b) mbar_init(&tail_bar[b], 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -1043,25 +1061,59 @@ __global__ void __launch_bounds__(kThreads, 1)
     int it = 0;
     int n_stores = 0;
     const int wslot = static_cast<int>(crank) * 4 + q;  // this warp's 32 rows of a partial tile
+    uint32_t tail_pending = 0, tail_par = 0;  // lane 0: partial-tile copies in flight per buffer, their parity
     for (int k = 0; k < n_units; ++k, ++it) {
       const PairUnit un = pair_unit(prm, sched, pair, n_pairs, k, nkb);
       const int mp = un.mp, n = un.n;
       const int buf = it & 1;
       if (!warp_wait(&tfull[buf], (it >> 1) & 1, abort_flag, tb.err, kErrTimeoutAcc)) break;
       tc_fence_after();
-      if (un.part > 0 && un.last) {  // the earlier parts of this tile have published their partials?
+      // Split tail tiles move their fp32 partials through this warp's share of the ring (idle in
+      // the pair's last unit, which a tail unit always is).  An earlier part stages each chunk
+      // there and bulk-copies it out.  The last part copies the earlier parts' chunks in: all
+      // four at once after one earlier part, else chunk c into buffer c & 1 while c - 1 is added.
+      const bool tail_last = un.part > 0 && un.last;
+      uint8_t* tail_w = sA + q * (2 * kTailBufBytes);  // this warp's share of the ring
+      auto tail_chunk = [&](int c, int p) {  // chunk c of earlier part p in shared memory
+        return tail_w + (un.part == 1 ? c : (c & 1) * un.part + p) * kTailChunkBytes;
+      };
+      auto tail_src = [&](int c, int p) {  // ... and in the partial tiles
+        return prm.tail_partial + (static_cast<size_t>(un.slot0 + p) * 8 + wslot) * (4 * 2048) +
+               static_cast<size_t>(c) * 2048;
+      };
+      auto tail_load = [&](int c) {  // lane 0: chunk c, or all chunks after one earlier part
+        const int nc = un.part == 1 ? 256 / 64 : 1;
+        uint64_t* bar = tail_bar + 2 * q + (c & 1);
+        mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nc * un.part * kTailChunkBytes));
+        for (int cc = c; cc < c + nc; ++cc)
+          for (int p = 0; p < un.part; ++p) bulk_load(tail_chunk(cc, p), tail_src(cc, p), kTailChunkBytes, bar);
+        tail_pending |= 1u << (c & 1);
+        tail_par = (tail_par & ~(1u << (c & 1))) | (static_cast<uint32_t>((c >> 1) & 1) << (c & 1));
+      };
+      if (tail_last) {  // the earlier parts of this tile have published their partials?
         int ok = 1;
-        if (lane == 0)
+        if (lane == 0) {
           for (int p = 0; p < un.part && ok; ++p)
             ok = wait_units_ready(prm.tail_flag, (un.slot0 + p) * 8 + wslot, (un.slot0 + p) * 8 + wslot + 1,
                                   prm.gen, abort_flag, tb.err) ? 1 : 0;
+          if (ok) {
+            fence_proxy_async_global();  // the acquired partials, read by the copy engine
+            tail_load(0);
+          }
+        }
         if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         __syncwarp();
       }
+      bool tail_ok = true;
       // rows [row0, row0+32) of this CTA's tile: TMEM -> registers -> swizzled staging -> TMA store
       const int row0 = (2 * mp + static_cast<int>(crank)) * kBM + q * 32;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(buf * 256);
       uint8_t* stage_w = sOut + (warp - 2) * (2 * 32 * 64 * 2);
+      // The pair's last unit: the ring is idle (every MMA of the pair is done), so each warp
+      // stages all four chunks there, after its partial-tile buffers, and no store waits for an
+      // earlier one to have read its buffer.
+      const bool ring_stage = k == n_units - 1 && un.part <= 2;
+      uint8_t* ring_w = tail_w + (tail_last ? (un.part == 1 ? 4 : 2 * un.part) * kTailChunkBytes : 0);
 #pragma unroll 1
       for (int c = 0; c < 256 / 64; ++c) {
         uint32_t v[64];
@@ -1078,33 +1130,49 @@ __global__ void __launch_bounds__(kThreads, 1)
           // i * 32 + l, so each warp-wide access covers 512 contiguous bytes
           const size_t chunk_off = static_cast<size_t>(c) * 2048;
           if (!un.last) {
-            float4* dst = reinterpret_cast<float4*>(
-                              prm.tail_partial + (static_cast<size_t>(un.slot0 + un.part) * 8 + wslot) * (4 * 2048) +
-                              chunk_off) + lane;
+            float4* stg = reinterpret_cast<float4*>(tail_w + c * kTailChunkBytes) + lane;
 #pragma unroll
             for (int i = 0; i < 16; ++i)
-              dst[i * 32] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+              stg[i * 32] = make_float4(__uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
                                         __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              bulk_store(prm.tail_partial + (static_cast<size_t>(un.slot0 + un.part) * 8 + wslot) * (4 * 2048) +
+                             chunk_off,
+                         tail_w + c * kTailChunkBytes, kTailChunkBytes);
+              bulk_commit();
+            }
             continue;
           }
+          if (un.part > 1 && lane == 0 && c + 1 < 256 / 64) {  // buffer (c + 1) & 1 was read for chunk c - 1
+            fence_proxy_async_smem();
+            tail_load(c + 1);
+          }
+          if (un.part > 1 || c == 0) {
+            // every lane acquires the copy's completion (bounded wait) before reading the buffer
+            tail_ok = __all_sync(0xffffffffu, mbar_wait(tail_bar + 2 * q + (c & 1), (c >> 1) & 1, abort_flag, tb.err,
+                                                        kErrTimeoutFull));
+            if (!tail_ok) break;
+            if (lane == 0) tail_pending &= ~(1u << (c & 1));
+          }
           for (int p = 0; p < un.part; ++p) {  // add the earlier parts in part order
-            const float4* src = reinterpret_cast<const float4*>(
-                                    prm.tail_partial + (static_cast<size_t>(un.slot0 + p) * 8 + wslot) * (4 * 2048) +
-                                    chunk_off) + lane;
+            const float4* src = reinterpret_cast<const float4*>(tail_chunk(c, p)) + lane;
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
-              const float4 f = __ldcg(src + i * 32);
+              const float4 f = src[i * 32];
               v[4 * i] = __float_as_uint(__uint_as_float(v[4 * i]) + f.x);
               v[4 * i + 1] = __float_as_uint(__uint_as_float(v[4 * i + 1]) + f.y);
               v[4 * i + 2] = __float_as_uint(__uint_as_float(v[4 * i + 2]) + f.z);
               v[4 * i + 3] = __float_as_uint(__uint_as_float(v[4 * i + 3]) + f.w);
             }
           }
+          __syncwarp();  // the buffer is free for the copy of chunk c + 2
         }
         const int col0 = n * 256 + c * 64;
         if (row0 >= prm.T || col0 >= prm.Nout) continue;
-        uint8_t* sbuf = stage_w + (n_stores & 1) * (32 * 64 * 2);
-        if (lane == 0) bulk_wait_read<1>();  // the store that used this buffer has read it
+        uint8_t* sbuf = ring_stage ? ring_w + c * (32 * 64 * 2) : stage_w + (n_stores & 1) * (32 * 64 * 2);
+        if (!ring_stage && lane == 0) bulk_wait_read<1>();  // the store that used this buffer has read it
         __syncwarp();
         uint8_t* rowp = sbuf + lane * 128;
 #pragma unroll
@@ -1124,13 +1192,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ++n_stores;
       }
+      if (!tail_ok) break;
       if (un.part >= 0 && !un.last) {  // publish this warp's share of the partial tile
-        __threadfence();
+        if (lane == 0) {
+          bulk_wait_all();             // the bulk copies have written it
+          fence_proxy_async_global();  // ... ordered before the release
+          __threadfence();
+          st_release_u64(prm.tail_flag + (un.slot0 + un.part) * 8 + wslot, prm.gen);
+        }
         __syncwarp();
-        if (lane == 0) st_release_u64(prm.tail_flag + (un.slot0 + un.part) * 8 + wslot, prm.gen);
       }
     }
-    if (lane == 0) bulk_wait_all();
+    if (lane == 0) {
+      bulk_wait_all();
+      for (int b = 0; b < 2; ++b)  // partial-tile copies still in flight after an abort
+        if (tail_pending & (1u << b)) drain_wait(tail_bar + 2 * q + b, (tail_par >> b) & 1u, tb.err);
+    }
     __syncwarp();
   }
 
