@@ -2073,7 +2073,12 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
   const int n_mtiles = (T + kBM - 1) / kBM;
   p.n_mpairs = (n_mtiles + 1) / 2;
   p.n_ntiles = (Nout + 255) / 256;
-  p.group_m = 4;  // the first round touches few row tiles: their shrink units are ready first
+  // Raster groups of row pairs (tiles of a group go column block by column block, the row pairs
+  // fastest).  With a co-scheduled shrink the first round touches few row tiles, whose shrink
+  // units are ready first; otherwise 16 row pairs, whose P rows stay in L2 while the group sweeps
+  // Q, so large problems re-read Q from HBM once per 16 row pairs (measured at 32768 x 8192 ->
+  // 28672 under the power cap: 13.3 ms against 14.2 ms with groups of 4).
+  p.group_m = 16;
   p.lora = lora ? 1 : 0;
   p.r_pad = tb.r_pad;
   const int fmt = dtype == LF_BF16 ? 1 : 0;
@@ -2097,6 +2102,7 @@ cudaError_t tc_gemm_pair(int dtype, bool q_mn_major, const TcMaps& maps, int T, 
   const CUtensorMap* p2_map = &maps.p;
   const CUtensorMap* a2_map = &maps.p;
   if (shrink != nullptr && (shrink->n_pairs > 0 || shrink->prologue)) {
+    p.group_m = 4;
     p.shrink_prologue = shrink->prologue ? 1 : 0;
     p.n_shrink_pairs = shrink->prologue ? 0 : shrink->n_pairs;
     p.s_planes = 2;
