@@ -384,7 +384,7 @@ def run_ours(args):
 
     from lorafusion_b200 import _native as nat
     from lorafusion_b200 import b200_ops
-    from lorafusion_b200.sharding import allreduce_spanning_grads, assign_bins, local_layout
+    from lorafusion_b200.sharding import PeerExchange, assign_bins, local_layout
     from lorafusion_b200.workloads import WORKLOADS, adapter_ranks
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -547,22 +547,29 @@ def run_ours(args):
                                       "frac": gram_gbs / peaks["hbm_gbs"], "bytes_per_launch": counts["gram_bytes"],
                                       "ms_per_launch": b_gram}}
 
+        # at N > 1 the spanning adapters' dA/dB are summed inside the dA/dB kernel over NVLink
+        peer = PeerExchange(plan, rank_of, device) if world > 1 and plan.spanning else None
+
         def fb():
             b200_ops.fused_lora_forward(pr["x"], pr["w"], pr["lora_a"], pr["lora_b"], pr["adapters"], pr["routing"])
-            gx, ga, gb = b200_ops.fused_lora_backward(pr["grad"], pr["x"], pr["w"], pr["lora_a"], pr["lora_b"],
-                                                      pr["adapters"], pr["routing"], grad_dtype=grad_dtype)
-            allreduce_spanning_grads(plan, ga, gb, rank_of, K, N, device)
+            b200_ops.fused_lora_backward(pr["grad"], pr["x"], pr["w"], pr["lora_a"], pr["lora_b"], pr["adapters"],
+                                         pr["routing"], grad_dtype=grad_dtype, peer=peer)
 
         fb_ms = rank_max(statistics.mean(s[0] for s in timed(bracket(fb), short, 2, 2)))
         bwd_launches = b200_ops.last_launch_count()
         bwd_ms = rank_max(statistics.mean(s[0] for s in timed(bracket(
             lambda: b200_ops.fused_lora_backward(pr["grad"], pr["x"], pr["w"], pr["lora_a"], pr["lora_b"],
-                                                 pr["adapters"], pr["routing"], grad_dtype=grad_dtype)), short, 2, 2)))
+                                                 pr["adapters"], pr["routing"], grad_dtype=grad_dtype, peer=peer)),
+            short, 2, 2)))
+        if peer is not None:
+            peer.close()
         fwd_bwd = {"value": global_T / (fb_ms / 1e3), "unit": "tokens/s", "ms_per_step": fb_ms,
                    "launches_per_step": n_launch + bwd_launches, "backward_ms": bwd_ms,
                    "tflops": counts["fwdbwd_flops"] * world / (fb_ms / 1e3) / 1e12,
                    "tflops_note": "whole job (all GPUs)",
-                   "spanning_adapters": len(plan.spanning)}
+                   "spanning_adapters": len(plan.spanning),
+                   "cross_gpu_sum": "inside the dA/dB kernel (blocks pushed to every rank over NVLink peer "
+                                    "mappings, summed in rank order)" if world > 1 else None}
     del prep, y, pr
 
     # multi-projection workloads, forward + backward, strong scaling over the N GPUs
@@ -645,7 +652,7 @@ def run_workload(name, wl, world, rank, device, args, flush, barrier, rank_max, 
     import torch
 
     from lorafusion_b200 import b200_ops
-    from lorafusion_b200.sharding import allreduce_spanning_grads, assign_bins, local_layout
+    from lorafusion_b200.sharding import PeerExchange, assign_bins, local_layout
     from lorafusion_b200.workloads import adapter_ranks
 
     ranks = adapter_ranks(wl)
@@ -658,6 +665,7 @@ def run_workload(name, wl, world, rank, device, args, flush, barrier, rank_max, 
              for p in range(len(wl.projections))]
     flops = sum(algorithmic_counts(routes, ranks, p["K"], p["N"], p["T"])["fwdbwd_flops"] for p in projs)
     grad_dtype = torch.float32 if world > 1 else None
+    peer = PeerExchange(plan, rank_of, device) if world > 1 and plan.spanning else None
 
     def step(ev):
         if ev:
@@ -666,30 +674,27 @@ def run_workload(name, wl, world, rank, device, args, flush, barrier, rank_max, 
             b200_ops.fused_lora_forward(p["x"], p["w"], p["lora_a"], p["lora_b"], p["adapters"], p["routing"])
         if ev:
             ev[1].record()
-        grads = []
-        for p in projs:
-            grads.append(b200_ops.fused_lora_backward(p["grad"], p["x"], p["w"], p["lora_a"], p["lora_b"],
-                                                      p["adapters"], p["routing"], grad_dtype=grad_dtype))
+        for p in projs:  # spanning adapters' dA/dB summed across the GPUs inside each dA/dB kernel
+            b200_ops.fused_lora_backward(p["grad"], p["x"], p["w"], p["lora_a"], p["lora_b"], p["adapters"],
+                                         p["routing"], grad_dtype=grad_dtype, peer=peer)
         if ev:
             ev[2].record()
-        for p, (_, ga, gb) in zip(projs, grads):
-            allreduce_spanning_grads(plan, ga, gb, rank_of, p["K"], p["N"], device)
-        if ev:
-            ev[3].record()
 
     steps = max(3, args.steps // 3)
     for _ in range(2):
         flush.zero_()
         step(None)
     barrier()
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(steps)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(steps)]
     for i in range(steps):
         flush.zero_()
         torch.cuda._sleep(100_000)
         step(ev[i])
     barrier()
-    per = [[ev[i][j].elapsed_time(ev[i][j + 1]) for j in range(3)] for i in range(steps)]
-    fwd_ms, bwd_ms, ar_ms = (statistics.mean(s[j] for s in per) for j in range(3))
+    per = [[ev[i][j].elapsed_time(ev[i][j + 1]) for j in range(2)] for i in range(steps)]
+    fwd_ms, bwd_ms = (statistics.mean(s[j] for s in per) for j in range(2))
+    if peer is not None:
+        peer.close()
     # per projection, stages as launches of their own (this rank): forward shrink / fused GEMM,
     # backward shrinks / grad_x GEMM / grams
     from lorafusion_b200 import _native as nat
@@ -715,7 +720,7 @@ def run_workload(name, wl, world, rank, device, args, flush, barrier, rank_max, 
         stages[pname] = {"fwd_shrink": t_[0], "fwd_gemm": t_[1], "bwd_shrinks": t_[2], "bwd_grad_x": t_[3],
                          "bwd_grams": t_[4]}
         del fp, bp, yp
-    local = fwd_ms + bwd_ms + ar_ms
+    local = fwd_ms + bwd_ms
     ms = rank_max(local)
     total_flops = flops
     if world > 1:
@@ -726,7 +731,8 @@ def run_workload(name, wl, world, rank, device, args, flush, barrier, rank_max, 
     out = {"value": wl.total_rows / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
            "scaling": "strong", "global_tokens": wl.total_rows, "projections": [p[0] for p in wl.projections],
            "adapters": wl.n_adapters, "pass": "forward + backward over every projection per step",
-           "rank0_ms": {"forward": fwd_ms, "backward": bwd_ms, "allreduce": ar_ms},
+           "rank0_ms": {"forward": fwd_ms, "backward": bwd_ms},
+           "cross_gpu_sum": "inside each dA/dB kernel over NVLink peer mappings" if world > 1 else None,
            "rank0_stage_ms": stages,
            "spanning_adapters": len(plan.spanning),
            "roofline": {"bound": "tensor", "achieved": tflops, "peak": world * peaks["bf16_tflops_sustained"],

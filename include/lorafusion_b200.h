@@ -284,6 +284,59 @@ LF_API int lf_backward_ex(const lf_problem* prob, const lf_plan_info* info, cons
                           size_t workspace_bytes, lf_stream_t stream);
 
 /*
+ * Multi-GPU backward with the gradient exchange inside the gram kernel.  One process per GPU of a
+ * node; adapters whose rows span GPUs ("spanning") need dA/dB summed over the GPUs that hold
+ * them, and every GPU receives those sums.  Instead of a separate all-reduce, the dA/dB kernel
+ * pushes each fp32 block (128 columns x r_pad) it computes for a spanning virtual slot into every
+ * rank's exchange buffer over peer mappings (NVLink), releases a flag per block there, and then
+ * sums, in rank order, the blocks of every spanning virtual slot once all their holders have
+ * released them.  Every rank gets the same sums, bit for bit.
+ *
+ *   exchange[r]    rank r's exchange buffer as mapped here (lf_peer_alloc there, lf_ipc_handle /
+ *                  lf_ipc_open here; this rank's own: the local pointer), at least
+ *                  lf_peer_exchange_bytes(world, n_span * (ceil(N/128) + ceil(K/128)), r_pad_x) bytes
+ *   r_pad_x        16, 32 or 64, at least every spanning virtual slot's rank, the same on every rank
+ *                  (blocks are exchanged with that many rank columns)
+ *   slot_span_dev  [info->n_slots] index of each (virtual) slot among the spanning virtual slots, -1
+ *                  for the others (numbering shared by every rank)
+ *   span_info_dev  [n_span][3] per spanning virtual slot: its first row in this call's grad_a/grad_b
+ *                  layout (those of slots not held here follow info->rank_total), its rank, and the
+ *                  mask of ranks that hold it
+ *   gen            nonzero, different on consecutive calls, the same on every rank (calls alternate
+ *                  between the two halves of the buffers by its parity)
+ *
+ * Every rank makes the same sequence of calls; a rank whose peers do not arrive stops after the
+ * wait limit (lf_set_wait_limit) and lf_device_error reports it.  Tensor-core problems with routed
+ * rows only: LF_ERR_UNSUPPORTED otherwise.  No counterpart in the reference (it is single-GPU).
+ */
+#define LF_MAX_PEERS 8
+#define LF_IPC_HANDLE_BYTES 64
+typedef struct lf_peer_reduce {
+  int32_t world;
+  int32_t rank;
+  void* exchange[LF_MAX_PEERS];
+  const int32_t* slot_span_dev;
+  const int32_t* span_info_dev;
+  int32_t n_span;
+  int32_t r_pad_x;
+  uint64_t gen;
+} lf_peer_reduce;
+
+LF_API size_t lf_peer_exchange_bytes(int32_t world, int32_t n_blocks, int32_t r_pad);
+LF_API int lf_backward_peer(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
+                            const void* grad_out_dev, const void* s_f_dev, int32_t s_f_planes, int32_t grad_ab_dtype,
+                            void* grad_x_dev, void* grad_a_dev, void* grad_b_dev, void* workspace_dev,
+                            size_t workspace_bytes, const lf_peer_reduce* peer, lf_stream_t stream);
+
+/* Device memory for an exchange buffer (zeroed), its inter-process handle, and a peer's buffer
+ * mapped into this process (cudaIpc*; processes on one node). */
+LF_API int lf_peer_alloc(size_t bytes, void** dev_ptr);
+LF_API int lf_peer_free(void* dev_ptr);
+LF_API int lf_ipc_handle(const void* dev_ptr, void* handle);
+LF_API int lf_ipc_open(const void* handle, void** dev_ptr);
+LF_API int lf_ipc_close(void* dev_ptr);
+
+/*
  * The backward in separately launchable stages (arguments as lf_backward_ex), for callers that
  * time them or overlap them with other work (e.g. a gradient all-reduce with the grad_x GEMM).
  * `stages` is a bit mask; each stage is a launch of its own and the routed shrinks are never

@@ -56,6 +56,17 @@ class RowRun(ctypes.Structure):
                 ("dst_stride", ctypes.c_int64), ("rows", ctypes.c_int64), ("row0", ctypes.c_int64)]
 
 
+MAX_PEERS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class PeerReduce(ctypes.Structure):
+    """lf_peer_reduce: the gram kernel's exchange of spanning adapters' blocks between GPUs."""
+    _fields_ = [("world", ctypes.c_int32), ("rank", ctypes.c_int32), ("exchange", ctypes.c_void_p * MAX_PEERS),
+                ("slot_span_dev", ctypes.c_void_p), ("span_info_dev", ctypes.c_void_p), ("n_span", ctypes.c_int32),
+                ("r_pad_x", ctypes.c_int32), ("gen", ctypes.c_uint64)]
+
+
 class HostChunk(ctypes.Structure):
     _fields_ = [("row0", ctypes.c_int32), ("rows", ctypes.c_int32), ("info", ctypes.POINTER(PlanInfo)),
                 ("table_dev", ctypes.c_void_p)]
@@ -112,6 +123,21 @@ def _declare(L: ctypes.CDLL) -> None:
     L.lf_backward_ex.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_p, _c_p,
                                  ctypes.c_size_t, _c_p]
     L.lf_backward_ex.restype = ctypes.c_int
+    L.lf_backward_peer.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_p,
+                                   _c_p, ctypes.c_size_t, P(PeerReduce), _c_p]
+    L.lf_backward_peer.restype = ctypes.c_int
+    L.lf_peer_exchange_bytes.argtypes = [_c_i32, _c_i32, _c_i32]
+    L.lf_peer_exchange_bytes.restype = ctypes.c_size_t
+    L.lf_peer_alloc.argtypes = [ctypes.c_size_t, P(ctypes.c_void_p)]
+    L.lf_peer_alloc.restype = ctypes.c_int
+    L.lf_peer_free.argtypes = [_c_p]
+    L.lf_peer_free.restype = ctypes.c_int
+    L.lf_ipc_handle.argtypes = [_c_p, _c_p]
+    L.lf_ipc_handle.restype = ctypes.c_int
+    L.lf_ipc_open.argtypes = [_c_p, P(ctypes.c_void_p)]
+    L.lf_ipc_open.restype = ctypes.c_int
+    L.lf_ipc_close.argtypes = [_c_p]
+    L.lf_ipc_close.restype = ctypes.c_int
     L.lf_backward_stages.argtypes = [P(Problem), P(PlanInfo), _c_p, _c_p, _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_p,
                                      _c_p, ctypes.c_size_t, _c_i32, _c_p]
     L.lf_backward_stages.restype = ctypes.c_int

@@ -526,7 +526,8 @@ def prepare_forward(x, base_weight, lora_a, lora_b, adapters, routing) -> Prepar
     return PreparedForward(x, base_weight, lora_a, lora_b, adapters, routing)
 
 
-def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, routing, *, grad_dtype=None):
+def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, routing, *, grad_dtype=None,
+                        peer=None):
     """Return ``(grad_x, grad_lora_a, grad_lora_b)`` as ``mock_ops.fused_lora_backward``.
 
     mock_ops.py:51-95: the base weight is frozen (no gradient); the dicts hold
@@ -534,6 +535,10 @@ def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, rout
     each summed over that adapter's routes; tensors are in ``x.dtype``.
     ``grad_dtype=torch.float32`` (keyword only, no counterpart in the reference) returns the
     adapter gradients in float32, unrounded, for a caller that sums them across GPUs first.
+    ``peer`` (keyword only, a ``sharding.PeerExchange``; no counterpart in the reference) sums the
+    gradients of adapters whose rows span GPUs inside the dA/dB kernel, over NVLink: every rank
+    calls it for its own rows, and each rank's dicts then hold the summed gradients of every
+    spanning adapter, held here or not (``lf_backward_peer``).
     """
     global _last_launches
     rts = _routes(routing, x.shape[0])
@@ -561,9 +566,11 @@ def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, rout
     packs = _pack(plan, aset, dtype, K, N, device, backward=True)
     info = plan.info
     rtot = info.rank_total
+    ext = _peer_layout(plan, peer, device) if peer is not None else None
+    rows = rtot + (ext.extra_rows if ext is not None else 0)  # + spanning adapters not held here
     grad_x = torch.empty((T, K), dtype=dtype, device=device)
-    ga_flat = torch.empty(max(rtot * K, 1), dtype=gdt, device=device)
-    gb_flat = torch.empty(max(rtot * N, 1), dtype=gdt, device=device)
+    ga_flat = torch.empty(max(rows * K, 1), dtype=gdt, device=device)
+    gb_flat = torch.empty(max(rows * N, 1), dtype=gdt, device=device)
     _warn_if_cuda_core(dtype, K, N, (x, w, g, grad_x))
     L = nat.lib()
     ws_bytes = L.lf_backward_workspace_bytes(ctypes.byref(info), code)
@@ -573,15 +580,82 @@ def fused_lora_backward(grad_out, x, base_weight, lora_a, lora_b, adapters, rout
     saved = _saved_sf(x_in, rts, plan, aset) if dtype != torch.float32 else None
     sf_ptr, sf_planes = (saved[0].data_ptr(), saved[1]) if saved is not None else (None, 0)
     # S_f from the forward on these inputs, when there was one: no second s x A^T shrink
-    rc = L.lf_backward_ex(ctypes.byref(prob), ctypes.byref(info), plan.table_dev.data_ptr(), g.data_ptr(), sf_ptr,
-                          sf_planes, _DTYPE_CODE[gdt], grad_x.data_ptr(), ga_flat.data_ptr(), gb_flat.data_ptr(),
-                          ws.data_ptr(), ws.numel(), stream)
+    if ext is not None:
+        peer.ensure(len(peer.vslots) * (-(-N // 128) + -(-K // 128)))
+        pr = nat.PeerReduce(world=peer.world, rank=peer.rank, n_span=len(peer.vslots), r_pad_x=peer.r_pad_x,
+                            gen=peer.next_gen())
+        for r, ptr in enumerate(peer.ptrs):
+            pr.exchange[r] = ptr
+        pr.slot_span_dev = ext.slot_span.data_ptr()
+        pr.span_info_dev = ext.span_info.data_ptr()
+        rc = L.lf_backward_peer(ctypes.byref(prob), ctypes.byref(info), plan.table_dev.data_ptr(), g.data_ptr(),
+                                sf_ptr, sf_planes, _DTYPE_CODE[gdt], grad_x.data_ptr(), ga_flat.data_ptr(),
+                                gb_flat.data_ptr(), ws.data_ptr(), ws.numel(), ctypes.byref(pr), stream)
+    else:
+        rc = L.lf_backward_ex(ctypes.byref(prob), ctypes.byref(info), plan.table_dev.data_ptr(), g.data_ptr(),
+                              sf_ptr, sf_planes, _DTYPE_CODE[gdt], grad_x.data_ptr(), ga_flat.data_ptr(),
+                              gb_flat.data_ptr(), ws.data_ptr(), ws.numel(), stream)
     if saved is not None:
         saved[0].record_stream(torch.cuda.current_stream(device))
-    nat.check(rc, "lf_backward_ex")
+    nat.check(rc, "lf_backward_peer" if ext is not None else "lf_backward_ex")
     n_launch = max(0, int(L.lf_backward_launch_count(ctypes.byref(prob), ctypes.byref(info))))
     _last_launches = n_launch - 1 if saved is not None and n_launch == 4 else n_launch
-    return grad_x, *_grad_dicts(plan, ga_flat, gb_flat, K, N)
+    grad_a, grad_b = _grad_dicts(plan, ga_flat, gb_flat, K, N)
+    if ext is not None:  # spanning adapters not held here: their summed blocks after the local ones
+        for aid, parts in ext.nonheld.items():
+            pre, r = parts[0][0], sum(rv for _, rv in parts)
+            grad_a[aid] = ga_flat[pre * K:(pre + r) * K].view(r, K)
+            blocks = [gb_flat[p0 * N:(p0 + rv) * N].view(N, rv) for p0, rv in parts]
+            grad_b[aid] = blocks[0] if len(blocks) == 1 else torch.cat(blocks, dim=1)
+    return grad_x, grad_a, grad_b
+
+
+class _PeerLayout:
+    __slots__ = ("slot_span", "span_info", "extra_rows", "nonheld")
+
+
+_PEER_LAYOUTS: "OrderedDict[tuple, tuple]" = OrderedDict()
+
+
+def _peer_layout(plan: _Plan, peer, device) -> _PeerLayout:
+    """Device tables of lf_peer_reduce for one plan: each local virtual slot's index among the
+    spanning virtual slots (-1: not spanning, or no rows here), and per spanning virtual slot its
+    first gradient row in this call's layout (slots not held here follow rank_total), rank and
+    holder mask.  Cached per (plan, exchange)."""
+    key = (id(plan), id(peer))
+    hit = _PEER_LAYOUTS.get(key)
+    if hit is not None and hit[0] is plan and hit[1] is peer:
+        return hit[2]
+    me = 1 << peer.rank
+    held: dict[int, int] = {}
+    slot_span = []
+    prefix = 0
+    for si, c0, r in plan.vslots:
+        i = peer.index.get((plan.slots[si], c0), -1)
+        if i >= 0 and not peer.masks[i] & me:  # routes of this adapter here are all empty
+            i = -1
+        slot_span.append(i)
+        if i >= 0:
+            held[i] = prefix
+        prefix += r
+    info, extra, nonheld = [], 0, {}
+    for i, (aid, c0, r) in enumerate(peer.vslots):
+        if i in held:
+            pre = held[i]
+        else:
+            pre = plan.info.rank_total + extra
+            extra += r
+            nonheld.setdefault(aid, []).append((pre, r))
+        info += [pre, r, peer.masks[i]]
+    lay = _PeerLayout()
+    lay.slot_span = torch.tensor(slot_span or [-1], dtype=torch.int32, device=device)
+    lay.span_info = torch.tensor(info, dtype=torch.int32, device=device)
+    lay.extra_rows = extra
+    lay.nonheld = nonheld
+    while len(_PEER_LAYOUTS) >= 256:
+        _PEER_LAYOUTS.popitem(last=False)
+    _PEER_LAYOUTS[key] = (plan, peer, lay)
+    return lay
 
 
 class PreparedBackward:

@@ -554,9 +554,32 @@ namespace {
 int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev, const void* grad_out_dev,
                   const void* sf_given, int sf_planes, int grad_f32, void* grad_x_dev, void* grad_a_dev,
                   void* grad_b_dev, void* workspace_dev, size_t workspace_bytes, lf_stream_t stream,
-                  int stages = 0) {
+                  int stages = 0, const lf_peer_reduce* peer = nullptr) {
   int rc = check_problem(prob, info, table_dev);
   if (rc != LF_OK) return rc;
+  GramPeer gp{};
+  if (peer != nullptr) {  // spanning adapters' blocks exchanged by the gram: tensor-core path only
+    if (peer->world < 2 || peer->world > LF_MAX_PEERS || peer->rank < 0 || peer->rank >= peer->world ||
+        peer->n_span <= 0 || !peer->slot_span_dev || !peer->span_info_dev || peer->gen == 0 ||
+        (peer->r_pad_x != 16 && peer->r_pad_x != 32 && peer->r_pad_x != 64))
+      return LF_ERR_INVALID_ARG;
+    for (int r = 0; r < peer->world; ++r)
+      if (!peer->exchange[r] || !aligned16(peer->exchange[r])) return LF_ERR_INVALID_ARG;
+    if (prob->dtype == LF_F32 || prob->T == 0 || info->n_segtiles == 0 || info->n_slots == 0)
+      return LF_ERR_UNSUPPORTED;
+    gp.world = peer->world;
+    gp.rank = peer->rank;
+    for (int r = 0; r < peer->world; ++r) gp.xbuf[r] = static_cast<uint8_t*>(peer->exchange[r]);
+    gp.slot_span = peer->slot_span_dev;
+    gp.span_info = peer->span_info_dev;
+    gp.n_span = peer->n_span;
+    gp.cblk_b = (prob->N + 127) / 128;
+    gp.blocks_per_span = gp.cblk_b + (prob->K + 127) / 128;
+    gp.n_blocks = gp.n_span * gp.blocks_per_span;
+    gp.xr = peer->r_pad_x;
+    gp.gen = peer->gen;
+  }
+  const GramPeer* gpp = peer != nullptr ? &gp : nullptr;
   const bool staged = stages != 0;
   const bool do_shrink = !staged || (stages & LF_BSTAGE_SHRINK) != 0;
   const bool do_gx = !staged || (stages & LF_BSTAGE_GRAD_X) != 0;
@@ -590,8 +613,10 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
   const bool reuse_sf = sf_given != nullptr && prob->dtype != LF_F32 && (sf_planes == 1 || sf_planes == 2);
   if (reuse_sf) s_f = const_cast<void*>(sf_given);
 
-  if (tc_eligible(prob, {prob->x_dev, prob->w_dev, prob->a_pack_dev, prob->bt_pack_dev, prob->at_pack_dev,
-                         grad_out_dev, grad_x_dev, workspace_dev})) {
+  const bool tc_path = tc_eligible(prob, {prob->x_dev, prob->w_dev, prob->a_pack_dev, prob->bt_pack_dev,
+                                          prob->at_pack_dev, grad_out_dev, grad_x_dev, workspace_dev});
+  if (peer != nullptr && !tc_path) return LF_ERR_UNSUPPORTED;
+  if (tc_path) {
     CUtensorMap p_x, p_g, a_map, bt_map, sf_map, sb_map;
     TcMaps dx;
     const PairTail tail = tail_scratch(workspace_dev, workspace_bytes, backward_min_workspace_bytes(info));
@@ -689,11 +714,11 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
       // the grams read hi and lo planes: 2 per K half
       const int f_planes = reuse_sf ? sf_planes : planes;
       if (f_planes == planes) {
-        e = tc_gram(dt, jobs, 2, tb, ds->num_sms, st, 2 * planes, scratch, next_generation());
+        e = tc_gram(dt, jobs, 2, tb, ds->num_sms, st, 2 * planes, scratch, next_generation(), gpp);
       } else {  // S_f and S_b hold different plane counts: one launch each
-        e = tc_gram(dt, &jobs[0], 1, tb, ds->num_sms, st, 2 * f_planes, scratch, next_generation());
+        e = tc_gram(dt, &jobs[0], 1, tb, ds->num_sms, st, 2 * f_planes, scratch, next_generation(), gpp);
         if (e == cudaSuccess)
-          e = tc_gram(dt, &jobs[1], 1, tb, ds->num_sms, st, 2 * planes, scratch, next_generation());
+          e = tc_gram(dt, &jobs[1], 1, tb, ds->num_sms, st, 2 * planes, scratch, next_generation(), gpp);
       }
       if (e != cudaSuccess) return LF_ERR_CUDA;
     }
@@ -760,6 +785,55 @@ extern "C" int lf_backward_ex(const lf_problem* prob, const lf_plan_info* info, 
   return backward_impl(prob, info, table_dev, grad_out_dev, s_f_dev, s_f_dev ? s_f_planes : 0,
                        grad_ab_dtype == LF_F32 ? 1 : 0, grad_x_dev, grad_a_dev, grad_b_dev, workspace_dev,
                        workspace_bytes, stream);
+}
+
+extern "C" int lf_backward_peer(const lf_problem* prob, const lf_plan_info* info, const int32_t* table_dev,
+                                const void* grad_out_dev, const void* s_f_dev, int32_t s_f_planes,
+                                int32_t grad_ab_dtype, void* grad_x_dev, void* grad_a_dev, void* grad_b_dev,
+                                void* workspace_dev, size_t workspace_bytes, const lf_peer_reduce* peer,
+                                lf_stream_t stream) {
+  if (!prob || !peer) return LF_ERR_INVALID_ARG;
+  if (s_f_dev && s_f_planes != 1 && s_f_planes != 2) return LF_ERR_INVALID_ARG;
+  if (grad_ab_dtype != prob->dtype && grad_ab_dtype != LF_F32) return LF_ERR_INVALID_ARG;
+  return backward_impl(prob, info, table_dev, grad_out_dev, s_f_dev, s_f_dev ? s_f_planes : 0,
+                       grad_ab_dtype == LF_F32 ? 1 : 0, grad_x_dev, grad_a_dev, grad_b_dev, workspace_dev,
+                       workspace_bytes, stream, 0, peer);
+}
+
+extern "C" size_t lf_peer_exchange_bytes(int32_t world, int32_t n_blocks, int32_t r_pad) {
+  if (world < 1 || world > LF_MAX_PEERS || n_blocks < 0 || (r_pad != 16 && r_pad != 32 && r_pad != 64)) return 0;
+  return 2 * peer_half_bytes(world, n_blocks, r_pad);
+}
+
+extern "C" int lf_peer_alloc(size_t bytes, void** dev_ptr) {
+  if (!dev_ptr || bytes == 0) return LF_ERR_INVALID_ARG;
+  *dev_ptr = nullptr;
+  if (cudaMalloc(dev_ptr, bytes) != cudaSuccess) return LF_ERR_CUDA;
+  if (cudaMemset(*dev_ptr, 0, bytes) != cudaSuccess) return LF_ERR_CUDA;  // flags start below any generation
+  return LF_OK;
+}
+
+extern "C" int lf_peer_free(void* dev_ptr) { return cudaFree(dev_ptr) == cudaSuccess ? LF_OK : LF_ERR_CUDA; }
+
+extern "C" int lf_ipc_handle(const void* dev_ptr, void* handle) {
+  static_assert(sizeof(cudaIpcMemHandle_t) == LF_IPC_HANDLE_BYTES, "IPC handle size");
+  if (!dev_ptr || !handle) return LF_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr)) != cudaSuccess) return LF_ERR_CUDA;
+  memcpy(handle, &h, sizeof(h));
+  return LF_OK;
+}
+
+extern "C" int lf_ipc_open(const void* handle, void** dev_ptr) {
+  if (!handle || !dev_ptr) return LF_ERR_INVALID_ARG;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  *dev_ptr = nullptr;
+  return cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? LF_OK : LF_ERR_CUDA;
+}
+
+extern "C" int lf_ipc_close(void* dev_ptr) {
+  return cudaIpcCloseMemHandle(dev_ptr) == cudaSuccess ? LF_OK : LF_ERR_CUDA;
 }
 
 extern "C" int lf_device_error(int32_t* code) {

@@ -133,8 +133,31 @@ struct GramJobDesc {
   int transpose_out;
   int out_f32;  // write the gradient blocks as float instead of the input type
 };
+// In-kernel exchange of the dA/dB blocks of adapters whose rows span the GPUs of one node.  The
+// gram pushes each block it computes for a spanning virtual slot (128 columns x r_pad, fp32) into
+// every rank's exchange buffer over peer mappings and releases a flag per (block, epilogue warp)
+// there; afterwards every CTA sums, in rank order, blocks that all their holders have released,
+// and writes them like ordinary gradient blocks.  Exchange buffer of each rank, per half (calls
+// alternate by `gen` parity): flags [world][n_blocks][4] u64, then data
+// [world][n_blocks][128][xr] float.
+constexpr int kMaxPeers = 8;
+struct GramPeer {
+  int world = 0, rank = 0;   // world 0: no exchange
+  uint8_t* xbuf[kMaxPeers];  // every rank's exchange buffer as mapped in this process
+  const int32_t* slot_span;  // [n_slots] spanning virtual slot of each local slot, -1 else (device)
+  const int32_t* span_info;  // [n_span][3] output rank prefix, rank, holder mask (device)
+  int n_span, n_blocks;      // n_blocks = n_span * blocks_per_span
+  int blocks_per_span;       // column blocks of dB (ceil(N/128)) then of dA (ceil(K/128))
+  int cblk_b;                // ceil(N/128): where a slot's dA blocks start
+  int xr;                    // rank columns of an exchanged block (the same on every rank)
+  uint64_t gen;
+};
+__host__ __device__ inline size_t peer_half_bytes(int world, int n_blocks, int r_pad) {
+  return (static_cast<size_t>(world) * n_blocks * 4 * 8 + static_cast<size_t>(world) * n_blocks * 128 * r_pad * 4 +
+          255) & ~size_t(255);
+}
 cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables& tb, int num_sms, cudaStream_t st,
-                    int planes = 1, void* scratch = nullptr, uint64_t gen = 0);
+                    int planes = 1, void* scratch = nullptr, uint64_t gen = 0, const GramPeer* peer = nullptr);
 
 // --------------------------------------------------------------- packing
 cudaError_t pack_adapters(int src_dtype, int dst_dtype, const uint64_t* src_ptrs, const int32_t* ranks,

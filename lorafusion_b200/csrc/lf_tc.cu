@@ -1468,6 +1468,7 @@ struct GramParams {
   float* partial;      // [kGramMaxPartials][128][r_pad]
   uint64_t* counters;  // [kGramMaxCounters][4] arrival words, generation in the high half
   uint32_t gen32;
+  GramPeer peer;       // exchange of spanning adapters' blocks with the other GPUs (world 0: none)
   Tables tb;
 };
 
@@ -1560,6 +1561,23 @@ __device__ __forceinline__ GramUnit gram_unit(const GramParams& prm, const GramS
 // listed largest first, every CTA gets a similar share.
 __device__ __forceinline__ int gram_zigzag(int r, int me, int G) { return r * G + ((r & 1) ? G - 1 - me : me); }
 
+// Bounded wait until *f == gen, with system-scope acquire (the flag is written by another GPU).
+__device__ __forceinline__ bool wait_flag_sys(const uint64_t* f, uint64_t gen, volatile int* abort_flag, int* err) {
+  if (ld_acquire_sys_u64(f) == gen) return true;
+  const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit(err);
+  while (ld_acquire_sys_u64(f) != gen) {
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > limit) {
+      record_error(err, kErrTimeoutFlag);
+      *abort_flag = 1;
+      return false;
+    }
+    __nanosleep(256);
+  }
+  return true;
+}
+
 // Arrival on a per-launch counter word (generation in the high 32 bits); returns the count after
 // this arrival, or 0 after a bounded number of failed tries (error recorded).
 __device__ __forceinline__ uint32_t gen_arrive(uint64_t* ctr, uint32_t gen32, int* err) {
@@ -1649,8 +1667,10 @@ __global__ void __launch_bounds__(kGramThreads)
       for (int i0 = 0; i0 < tb.n_slots; i0 += 32) {
         const int i = i0 + lane;
         const int nst = i < tb.n_slots ? sp.nst[i] : 0;
-        // parts are the same for both jobs (one cap); lanes past the end count nothing
-        const int P = i >= tb.n_slots ? 0 : (try_split && nst > prm.cap) ? (nst + prm.cap - 1) / prm.cap : 1;
+        // parts are the same for both jobs (one cap); lanes past the end count nothing; the blocks
+        // of a spanning slot go to the other GPUs whole
+        const bool span = i < tb.n_slots && prm.peer.world > 0 && prm.peer.slot_span[sp.slot[i]] >= 0;
+        const int P = i >= tb.n_slots ? 0 : (try_split && !span && nst > prm.cap) ? (nst + prm.cap - 1) / prm.cap : 1;
         int a = P, b = P > 1 ? P : 0, c = P > 1 ? 1 : 0;  // inclusive warp scans
 #pragma unroll
         for (int d = 1; d < 32; d <<= 1) {
@@ -1808,84 +1828,85 @@ __global__ void __launch_bounds__(kGramThreads)
     const int q = warp & 3;  // the TMEM lane quadrant this warp may access
     const int col = q * 32 + lane;
     const int set = (warp - 2) >> 2;
+    // Elements (j0 .. j0+15, column cb * 128 + col) of a slot's block, [rank, C] (transposed) or
+    // [C, rank], in the input type or (out_f32) in float, written with 16-byte stores where the layout
+    // allows (C is a multiple of 8 on this path): a [C, rank] row segment from registers; a [rank, C]
+    // block in the input type through this warp's staging tile (16 ranks x 32 columns) as 16-byte
+    // row pieces; [rank, C] in float as one 128-byte row piece per warp and rank.  The whole warp
+    // calls it (same block, converged).
+    auto store16 = [&](int job, int rank_prefix, int rank, int cb, int j0, const float* v) {
+      const GramJob& jb = prm.job[job];
+      const int c = cb * 128 + col;
+      const int64_t obase = static_cast<int64_t>(rank_prefix) * jb.C;
+      if (jb.transpose_out && !jb.out_f32) {
+        OutT* stg = stage_tr + (warp - 2) * 16 * 32;
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) stg[jj * 32 + lane] = cvt_out<OutT>(v[jj]);
+        __syncwarp();
+        OutT* o = reinterpret_cast<OutT*>(jb.out) + obase;
+        const int cw = cb * 128 + q * 32;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const int idx = lane + 32 * t, rr = idx >> 2, ch = idx & 3;
+          const int j = j0 + rr, c8 = cw + ch * 8;
+          if (j < rank && c8 < jb.C)
+            *reinterpret_cast<uint4*>(o + static_cast<int64_t>(j) * jb.C + c8) =
+                *reinterpret_cast<const uint4*>(stg + rr * 32 + ch * 8);
+        }
+        __syncwarp();
+        return;
+      }
+      if (c >= jb.C) return;
+      if (jb.transpose_out) {
+        float* o = reinterpret_cast<float*>(jb.out) + obase;
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj)
+          if (j0 + jj < rank) o[static_cast<int64_t>(j0 + jj) * jb.C + c] = v[jj];
+        return;
+      }
+      const int64_t row = obase + static_cast<int64_t>(c) * rank;
+      if (jb.out_f32) {
+        float* o = reinterpret_cast<float*>(jb.out) + row;
+#pragma unroll
+        for (int q4 = 0; q4 < 16; q4 += 4) {
+          const int j = j0 + q4;
+          if (rank % 4 == 0 && j + 4 <= rank)
+            *reinterpret_cast<float4*>(o + j) = make_float4(v[q4], v[q4 + 1], v[q4 + 2], v[q4 + 3]);
+          else
+            for (int e = 0; e < 4; ++e)
+              if (j + e < rank) o[j + e] = v[q4 + e];
+        }
+        return;
+      }
+      OutT* o = reinterpret_cast<OutT*>(jb.out) + row;
+#pragma unroll
+      for (int q8 = 0; q8 < 16; q8 += 8) {
+        const int j = j0 + q8;
+        if (rank % 8 == 0 && j + 8 <= rank) {
+          uint4 pk;
+          pk.x = pack2<OutT>(v[q8], v[q8 + 1]);
+          pk.y = pack2<OutT>(v[q8 + 2], v[q8 + 3]);
+          pk.z = pack2<OutT>(v[q8 + 4], v[q8 + 5]);
+          pk.w = pack2<OutT>(v[q8 + 6], v[q8 + 7]);
+          *reinterpret_cast<uint4*>(o + j) = pk;
+        } else {
+          for (int e = 0; e < 8; ++e)
+            if (j + e < rank) o[j + e] = cvt_out<OutT>(v[q8 + e]);
+        }
+      }
+    };
     for (int k = set; k < n_mine; k += kGramEpiSets) {
       const GramUnit g = unit(k);
       const GramJob& jb = prm.job[g.job];
       const int buf = k & 1;
-      const int c = g.cb * 128 + col;
       const int rank = g.rank;
-      // Elements (j0 .. j0+15, c) of this slot's block, [rank, C] (transposed) or [C, rank], in the
-      // input type or (out_f32) in float, written with 16-byte stores where the layout allows
-      // (C is a multiple of 8 on this path): a [C, rank] row segment from registers; a [rank, C]
-      // block in the input type through this warp's staging tile (16 ranks x 32 columns) as 16-byte
-      // row pieces; [rank, C] in float as one 128-byte row piece per warp and rank.  The whole warp
-      // calls it (same unit, converged).
-      const int64_t obase = static_cast<int64_t>(g.rank_prefix) * jb.C;
-      auto store16 = [&](int j0, const float* v) {
-        if (jb.transpose_out && !jb.out_f32) {
-          OutT* stg = stage_tr + (warp - 2) * 16 * 32;
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) stg[jj * 32 + lane] = cvt_out<OutT>(v[jj]);
-          __syncwarp();
-          OutT* o = reinterpret_cast<OutT*>(jb.out) + obase;
-          const int cw = g.cb * 128 + q * 32;
-#pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int idx = lane + 32 * t, rr = idx >> 2, ch = idx & 3;
-            const int j = j0 + rr, c8 = cw + ch * 8;
-            if (j < rank && c8 < jb.C)
-              *reinterpret_cast<uint4*>(o + static_cast<int64_t>(j) * jb.C + c8) =
-                  *reinterpret_cast<const uint4*>(stg + rr * 32 + ch * 8);
-          }
-          __syncwarp();
-          return;
-        }
-        if (c >= jb.C) return;
-        if (jb.transpose_out) {
-          float* o = reinterpret_cast<float*>(jb.out) + obase;
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj)
-            if (j0 + jj < rank) o[static_cast<int64_t>(j0 + jj) * jb.C + c] = v[jj];
-          return;
-        }
-        const int64_t row = obase + static_cast<int64_t>(c) * rank;
-        if (jb.out_f32) {
-          float* o = reinterpret_cast<float*>(jb.out) + row;
-#pragma unroll
-          for (int q4 = 0; q4 < 16; q4 += 4) {
-            const int j = j0 + q4;
-            if (rank % 4 == 0 && j + 4 <= rank)
-              *reinterpret_cast<float4*>(o + j) = make_float4(v[q4], v[q4 + 1], v[q4 + 2], v[q4 + 3]);
-            else
-              for (int e = 0; e < 4; ++e)
-                if (j + e < rank) o[j + e] = v[q4 + e];
-          }
-          return;
-        }
-        OutT* o = reinterpret_cast<OutT*>(jb.out) + row;
-#pragma unroll
-        for (int q8 = 0; q8 < 16; q8 += 8) {
-          const int j = j0 + q8;
-          if (rank % 8 == 0 && j + 8 <= rank) {
-            uint4 pk;
-            pk.x = pack2<OutT>(v[q8], v[q8 + 1]);
-            pk.y = pack2<OutT>(v[q8 + 2], v[q8 + 3]);
-            pk.z = pack2<OutT>(v[q8 + 4], v[q8 + 5]);
-            pk.w = pack2<OutT>(v[q8 + 6], v[q8 + 7]);
-            *reinterpret_cast<uint4*>(o + j) = pk;
-          } else {
-            for (int e = 0; e < 8; ++e)
-              if (j + e < rank) o[j + e] = cvt_out<OutT>(v[q8 + e]);
-          }
-        }
-      };
       if (!warp_wait(&tfull[buf], (k >> 1) & 1, abort_flag, tb.err, kErrTimeoutAcc)) break;
       tc_fence_after();
       if (g.b == g.e) {
         float zeros[16];
 #pragma unroll
         for (int jj = 0; jj < 16; ++jj) zeros[jj] = 0.f;
-        for (int j0 = 0; j0 < rank; j0 += 16) store16(j0, zeros);
+        for (int j0 = 0; j0 < rank; j0 += 16) store16(g.job, g.rank_prefix, rank, g.cb, j0, zeros);
         tc_fence_before();
         mbar_arrive(&tempty[buf]);
         continue;
@@ -1915,6 +1936,41 @@ __global__ void __launch_bounds__(kGramThreads)
             }
         }
       };
+      const int sv = prm.peer.world > 0 ? prm.peer.slot_span[g.slot] : -1;
+      if (sv >= 0) {
+        // spanning slot (never split): this warp's 32 columns of the block go to every rank's
+        // exchange buffer (this rank's row there), then one release per rank; the sums are
+        // formed after the units
+        const GramPeer& pr = prm.peer;
+        const int blk = sv * pr.blocks_per_span + (jb.transpose_out ? pr.cblk_b : 0) + g.cb;
+        const size_t half = peer_half_bytes(pr.world, pr.n_blocks, pr.xr) * static_cast<size_t>(pr.gen & 1);
+        const size_t data_off = static_cast<size_t>(pr.world) * pr.n_blocks * 4 * 8;
+        const size_t mine = ((static_cast<size_t>(pr.rank) * pr.n_blocks + blk) * 128 + col) * pr.xr;
+        for (int j0 = 0; j0 < pr.xr; j0 += 16) {
+          float v[16];
+          if (j0 < r_pad) {
+            load_sum16(j0, v);
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) v[jj] = 0.f;
+          }
+          for (int d = 0; d < pr.world; ++d) {
+            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(pr.xbuf[d] + half + data_off) + mine + j0);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) dst[t] = make_float4(v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&tempty[buf]);
+        __threadfence_system();
+        __syncwarp();
+        if (lane == 0)
+          for (int d = 0; d < pr.world; ++d)
+            st_release_sys_u64(reinterpret_cast<uint64_t*>(pr.xbuf[d] + half) +
+                                   (static_cast<size_t>(pr.rank) * pr.n_blocks + blk) * 4 + q,
+                               pr.gen);
+        continue;
+      }
       if (g.parts > 1) {
         // part of a split slot: fp32 partial of this warp's 32 columns; the last of the slot's
         // parts to arrive (per column block and warp) adds the parts in part order
@@ -1957,7 +2013,7 @@ __global__ void __launch_bounds__(kGramThreads)
               acc[4 * t + 3] += v4[t].w;
             }
           }
-          if (j0 < rank) store16(j0, acc);
+          if (j0 < rank) store16(g.job, g.rank_prefix, rank, g.cb, j0, acc);
         }
         continue;
       }
@@ -1966,10 +2022,58 @@ __global__ void __launch_bounds__(kGramThreads)
       for (int j0 = 0; j0 < r_pad; j0 += 16) {
         float v[16];
         load_sum16(j0, v);
-        if (j0 < rank) store16(j0, v);
+        if (j0 < rank) store16(g.job, g.rank_prefix, rank, g.cb, j0, v);
       }
       tc_fence_before();
       mbar_arrive(&tempty[buf]);
+    }
+    if (prm.peer.world > 0 && !*abort_flag) {
+      // Sums of the spanning blocks of this launch's jobs (held here or not): block t goes to set
+      // t % 2 of CTA t / 2 (mod the grid); once every holder has released it (this warp's 32
+      // columns), the holders' rows are added in rank order and written like a local block.
+      const GramPeer& pr = prm.peer;
+      const size_t half = peer_half_bytes(pr.world, pr.n_blocks, pr.xr) * static_cast<size_t>(pr.gen & 1);
+      const uint64_t* flags = reinterpret_cast<const uint64_t*>(pr.xbuf[pr.rank] + half);
+      const float* data = reinterpret_cast<const float*>(pr.xbuf[pr.rank] + half +
+                                                         static_cast<size_t>(pr.world) * pr.n_blocks * 4 * 8);
+      const int n_sum0 = pr.n_span * prm.job[0].n_cblk;
+      const int n_sum = n_sum0 + (prm.n_jobs > 1 ? pr.n_span * prm.job[1].n_cblk : 0);
+      for (int t = me * kGramEpiSets + set; t < n_sum; t += G * kGramEpiSets) {
+        const int j = t < n_sum0 ? 0 : 1;
+        const GramJob& jb = prm.job[j];
+        const int tt = t - (j ? n_sum0 : 0);
+        const int sv = tt / jb.n_cblk, cb = tt - sv * jb.n_cblk;
+        const int blk = sv * pr.blocks_per_span + (jb.transpose_out ? pr.cblk_b : 0) + cb;
+        const int out_prefix = pr.span_info[3 * sv], rank = pr.span_info[3 * sv + 1];
+        const uint32_t holders = static_cast<uint32_t>(pr.span_info[3 * sv + 2]);
+        int ok = 1;
+        if (lane == 0)
+          for (int src = 0; src < pr.world && ok; ++src)
+            if ((holders >> src) & 1u)
+              ok = wait_flag_sys(flags + (static_cast<size_t>(src) * pr.n_blocks + blk) * 4 + q, pr.gen, abort_flag,
+                                 tb.err) ? 1 : 0;
+        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        __syncwarp();
+        for (int j0 = 0; j0 < pr.xr && j0 < rank; j0 += 16) {
+          float acc[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) acc[jj] = 0.f;
+          for (int src = 0; src < pr.world; ++src)
+            if ((holders >> src) & 1u) {
+              const float4* sp4 = reinterpret_cast<const float4*>(
+                  data + ((static_cast<size_t>(src) * pr.n_blocks + blk) * 128 + col) * pr.xr + j0);
+#pragma unroll
+              for (int t4 = 0; t4 < 4; ++t4) {
+                const float4 f = __ldcg(sp4 + t4);
+                acc[4 * t4] += f.x;
+                acc[4 * t4 + 1] += f.y;
+                acc[4 * t4 + 2] += f.z;
+                acc[4 * t4 + 3] += f.w;
+              }
+            }
+          store16(j, out_prefix, rank, cb, j0, acc);
+        }
+      }
     }
   }
 
@@ -2225,9 +2329,10 @@ cudaError_t tc_shrink(int dtype, const CUtensorMap& p_map, const CUtensorMap& a_
 }
 
 cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables& tb, int num_sms, cudaStream_t st,
-                    int planes, void* scratch, uint64_t gen) {
+                    int planes, void* scratch, uint64_t gen, const GramPeer* peer) {
   if (n_jobs < 1 || n_jobs > 2) return cudaErrorInvalidValue;
   GramParams p{};
+  if (peer != nullptr) p.peer = *peer;
   p.n_jobs = n_jobs;
   int64_t steps = 0, most = 0;
   for (int j = 0; j < n_jobs; ++j) {

@@ -16,9 +16,12 @@ the op needs to run one process per GPU:
 * :func:`local_layout` turns a rank's row ranges into its own fused rows and a
   rebased :class:`TileRoutingConfig`.
 * The forward needs no communication (base weight replicated, adapters
-  resident on every rank).  In the backward, :func:`allreduce_spanning_grads`
-  sums dA/dB of adapters whose routes land on more than one rank with a
-  single ``all_reduce(SUM)`` over one packed float32 buffer.
+  resident on every rank).  In the backward, the gradients of adapters whose
+  routes land on more than one rank are summed over the ranks: inside the
+  dA/dB kernel over NVLink peer mappings (:class:`PeerExchange`, passed as
+  ``fused_lora_backward(..., peer=...)``), or by
+  :func:`allreduce_spanning_grads` with a single ``all_reduce(SUM)`` over one
+  packed float32 buffer.
 """
 
 from __future__ import annotations
@@ -41,6 +44,7 @@ class ShardPlan:
     bin_rows: list[tuple[int, int]]     # [start, end) of every bin in the global fused rows
     spanning: list[int]                 # adapters whose routes land on more than one rank, ascending
     rank_ranges: tuple = ()             # per rank: its global row ranges [start, end), ascending
+    holders: tuple = ()                 # (adapter, ranks holding its rows) of every spanning adapter
 
     def rank_bins(self, rank: int) -> list[int]:
         return [b for b, r in enumerate(self.bin_rank) if r == rank]
@@ -111,7 +115,7 @@ def assign_bins(bins: list[list[tuple[int, int]]], world_size: int) -> ShardPlan
                 owners.setdefault(a, set()).add(k)
     spanning = sorted(a for a, rk in owners.items() if len(rk) > 1)
     return ShardPlan(world_size=world_size, bin_rank=owner, bin_rows=starts, spanning=spanning,
-                     rank_ranges=rank_ranges)
+                     rank_ranges=rank_ranges, holders=tuple((a, tuple(sorted(owners[a]))) for a in spanning))
 
 
 def local_layout(plan: ShardPlan, bins: list[list[tuple[int, int]]], rank: int, tile_size: int):
@@ -179,3 +183,93 @@ def allreduce_spanning_grads(plan: ShardPlan, grad_a: dict[int, torch.Tensor], g
             grad_b[a] = vb.clone()
     if back_dst:
         torch._foreach_copy_(back_dst, back_src)
+
+
+class PeerExchange:
+    """The exchange buffers ``fused_lora_backward(..., peer=...)`` needs, one set per process.
+
+    Every rank holds one buffer (device memory of its own GPU) and maps every other rank's through
+    CUDA IPC handles exchanged over ``group`` (processes of one node).  The dA/dB kernel of each
+    rank pushes the blocks it computes for spanning adapters into all of them over NVLink and sums,
+    in rank order, what the adapters' holders pushed: every rank ends with the same sums, and no
+    separate all-reduce runs.  Creation and growth are collective: every rank makes the same calls
+    in the same order.  The buffer grows to the largest projection it has served.
+    """
+
+    def __init__(self, plan: ShardPlan, ranks: dict[int, int], device, group=None):
+        import torch.distributed as dist
+
+        self.plan, self.group = plan, group
+        self.device = torch.device(device)
+        self.world = plan.world_size
+        self.rank = dist.get_rank(group)
+        holders = dict(plan.holders)
+        # spanning virtual slots (a slot of rank > 64 is several), numbered alike on every rank
+        self.vslots: list[tuple[int, int, int]] = []
+        for a in plan.spanning:
+            r = int(ranks[a])
+            self.vslots += [(a, c0, min(64, r - c0)) for c0 in range(0, r, 64)]
+        self.index = {(a, c0): i for i, (a, c0, _) in enumerate(self.vslots)}
+        self.masks = [sum(1 << k for k in holders.get(a, ())) for a, _, _ in self.vslots]
+        rmax = max((r for _, _, r in self.vslots), default=16)
+        self.r_pad_x = 16 if rmax <= 16 else 32 if rmax <= 32 else 64
+        self.gen = 0
+        self.bytes = 0
+        self.local = None
+        self.ptrs: list[int] = []
+        self.opened: list[int] = []
+
+    def ensure(self, n_blocks: int) -> None:
+        """Collective: buffers of at least the bytes `n_blocks` exchanged blocks need."""
+        import torch.distributed as dist
+
+        from lorafusion_b200 import _native as nat
+
+        need = int(nat.lib().lf_peer_exchange_bytes(self.world, n_blocks, self.r_pad_x))
+        if need <= self.bytes:
+            return
+        L = nat.lib()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no rank still uses the old buffers
+        self._release()
+        ptr = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            nat.check(L.lf_peer_alloc(need, ctypes.byref(ptr)), "lf_peer_alloc")
+        self.local, self.bytes = ptr.value, need
+        handle = (ctypes.c_char * nat.IPC_HANDLE_BYTES)()
+        nat.check(L.lf_ipc_handle(ctypes.c_void_p(self.local), handle), "lf_ipc_handle")
+        handles: list = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=self.group)
+        self.ptrs = []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    self.ptrs.append(self.local)
+                    continue
+                peer = ctypes.c_void_p()
+                buf = (ctypes.c_char * nat.IPC_HANDLE_BYTES).from_buffer_copy(h)
+                nat.check(L.lf_ipc_open(buf, ctypes.byref(peer)), "lf_ipc_open")
+                self.ptrs.append(peer.value)
+                self.opened.append(peer.value)
+        dist.barrier(group=self.group)
+
+    def next_gen(self) -> int:
+        self.gen += 1
+        return self.gen
+
+    def _release(self) -> None:
+        from lorafusion_b200 import _native as nat
+        L = nat.lib()
+        for p in self.opened:
+            L.lf_ipc_close(ctypes.c_void_p(p))
+        self.opened = []
+        if self.local is not None:
+            L.lf_peer_free(ctypes.c_void_p(self.local))
+        self.local, self.bytes, self.ptrs = None, 0, []
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers and free this rank's."""
+        import torch.distributed as dist
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        self._release()
