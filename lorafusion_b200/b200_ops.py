@@ -762,12 +762,12 @@ class _ChunkPlans:
         rk = np.asarray(ranks, dtype=np.int32)
         sc = np.asarray(scales, dtype=np.float32)
         n_slots = len(rts.slots)
-        bounds = list(range(0, total_rows, chunk_rows))
+        bounds = _chunk_bounds(total_rows, chunk_rows)
         self.n = len(bounds)
         self.array = (nat.HostChunk * max(self.n, 1))()
         self.infos, self.tables, self.ws_bytes, self.launches = [], [], 256, 0
         for i, c0 in enumerate(bounds):
-            c1 = min(total_rows, c0 + chunk_rows)
+            c1 = bounds[i + 1] if i + 1 < len(bounds) else total_rows
             sel = (rts.starts < c1) & (rts.ends > c0)
             starts = np.ascontiguousarray(np.maximum(rts.starts[sel], c0) - c0, dtype=np.int32)
             ends = np.ascontiguousarray(np.minimum(rts.ends[sel], c1) - c0, dtype=np.int32)
@@ -780,6 +780,27 @@ class _ChunkPlans:
             self.array[i].info = ctypes.pointer(info)
             self.array[i].table_dev = table_dev.data_ptr()
             self.ws_bytes = max(self.ws_bytes, int(L.lf_forward_workspace_bytes(ctypes.byref(info), code)))
+
+
+EDGE_CHUNK_ROWS = 256
+
+
+def _chunk_bounds(total_rows: int, chunk_rows: int) -> list[int]:
+    """First row of every chunk of the host-streamed forward, all on the 128-row tile grid.  The
+    first and the last chunk are short (EDGE_CHUNK_ROWS): the GPU work starts once the first
+    chunk is copied in, and only the last chunk's copy back follows the last GEMM, so short edge
+    chunks shorten the part of the call that the copies in both directions do not overlap.
+    Batches too small for that are cut every chunk_rows."""
+    edge = EDGE_CHUNK_ROWS
+    if total_rows <= 2 * edge + chunk_rows:
+        return list(range(0, total_rows, chunk_rows))
+    bounds, cur = [0], edge
+    last = (total_rows - edge) // 128 * 128
+    while cur < last:
+        bounds.append(cur)
+        cur += chunk_rows
+    bounds.append(last)
+    return bounds
 
 
 def _chunk_plans(rts: _Routes, aset: _AdapterSet, total_rows: int, chunk_rows: int, device, code: int) -> _ChunkPlans:
@@ -798,9 +819,9 @@ def fused_lora_forward_host(x_host, base_weight, lora_a, lora_b, adapters, routi
     """``fused_lora_forward`` of a batch that lives in host memory; the result lands in host memory.
 
     One native call (``lf_forward_host``) enqueues everything: the rows travel in chunks of
-    ``chunk_rows`` (a multiple of 256); chunk i is copied to the GPU on one stream while chunk
-    i-1 is computed on the caller's current stream and chunk i-2 is copied back on a third, so
-    both PCIe directions and the GPU work overlap.  Each output row depends only on its own input
+    ``chunk_rows`` (a multiple of 256) between a short first and a short last chunk; chunk i is
+    copied to the GPU on one stream while chunk i-1 is computed on the caller's current stream and
+    chunk i-2 is copied back on a third, so both PCIe directions and the GPU work overlap.  Each output row depends only on its own input
     row, chunks start on the 128-row tile grid and their tables use the whole batch's slots, so
     the result equals one ``fused_lora_forward`` over the whole batch (bit for bit whenever the
     chunks and the whole batch run the routed shrink the same way: both co-scheduled, or both as
