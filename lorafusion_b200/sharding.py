@@ -199,6 +199,8 @@ class PeerExchange:
     def __init__(self, plan: ShardPlan, ranks: dict[int, int], device, group=None):
         import torch.distributed as dist
 
+        if any(plan.rank_rows(r) == 0 for r in range(plan.world_size)):
+            raise ValueError("every rank needs rows of its own for the in-kernel exchange")
         self.plan, self.group = plan, group
         self.device = torch.device(device)
         self.world = plan.world_size
