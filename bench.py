@@ -628,8 +628,9 @@ def run_ours(args):
                     "h2d_bytes_per_step": T * K * 2, "d2h_bytes_per_step": T * N * 2,
                     "timing": "host wall clock from before the call to after the stream synchronize, max over ranks",
                     "path": "b200_ops.fused_lora_forward_host -> lf_forward_host: pinned host x/y, 1024-row "
-                            "chunks enqueued by one native call, copies in both directions overlapped with the "
-                            "fused forward; at N > 1 every rank's copies share the host's PCIe and memory"},
+                            "chunks between a 256-row first and last chunk, enqueued by one native call, copies in "
+                            "both directions overlapped with the fused forward; at N > 1 every rank's copies share "
+                            "the host's PCIe and memory"},
             "backward": backward,
             "fwd_bwd": fwd_bwd,
             "workloads": workloads,
