@@ -288,9 +288,10 @@ LF_API int lf_backward_ex(const lf_problem* prob, const lf_plan_info* info, cons
  * node; adapters whose rows span GPUs ("spanning") need dA/dB summed over the GPUs that hold
  * them, and every GPU receives those sums.  Instead of a separate all-reduce, the dA/dB kernel
  * pushes each fp32 block (128 columns x r_pad) it computes for a spanning virtual slot into every
- * rank's exchange buffer over peer mappings (NVLink), releases a flag per block there, and then
- * sums, in rank order, the blocks of every spanning virtual slot once all their holders have
- * released them.  Every rank gets the same sums, bit for bit.
+ * rank's exchange buffer over peer mappings (NVLink), and then sums, in rank order, the blocks of
+ * every spanning virtual slot as their holders' entries arrive.  Every rank gets the same sums, bit
+ * for bit.  Each 64-bit entry carries the call's generation beside the value, so the push needs
+ * no fence and no flag.
  *
  *   exchange[r]    rank r's exchange buffer as mapped here (lf_peer_alloc there, lf_ipc_handle /
  *                  lf_ipc_open here; this rank's own: the local pointer), at least
@@ -302,8 +303,8 @@ LF_API int lf_backward_ex(const lf_problem* prob, const lf_plan_info* info, cons
  *   span_info_dev  [n_span][3] per spanning virtual slot: its first row in this call's grad_a/grad_b
  *                  layout (those of slots not held here follow info->rank_total), its rank, and the
  *                  mask of ranks that hold it
- *   gen            nonzero, different on consecutive calls, the same on every rank (calls alternate
- *                  between the two halves of the buffers by its parity)
+ *   gen            low 32 bits nonzero, different on consecutive calls, the same on every rank
+ *                  (calls alternate between the two halves of the buffers by its parity)
  *
  * Every rank makes the same sequence of calls; a rank whose peers do not arrive stops after the
  * wait limit (lf_set_wait_limit) and lf_device_error reports it.  Tensor-core problems with routed

@@ -560,7 +560,7 @@ int backward_impl(const lf_problem* prob, const lf_plan_info* info, const int32_
   GramPeer gp{};
   if (peer != nullptr) {  // spanning adapters' blocks exchanged by the gram: tensor-core path only
     if (peer->world < 2 || peer->world > LF_MAX_PEERS || peer->rank < 0 || peer->rank >= peer->world ||
-        peer->n_span <= 0 || !peer->slot_span_dev || !peer->span_info_dev || peer->gen == 0 ||
+        peer->n_span <= 0 || !peer->slot_span_dev || !peer->span_info_dev || static_cast<uint32_t>(peer->gen) == 0 ||
         (peer->r_pad_x != 16 && peer->r_pad_x != 32 && peer->r_pad_x != 64))
       return LF_ERR_INVALID_ARG;
     for (int r = 0; r < peer->world; ++r)

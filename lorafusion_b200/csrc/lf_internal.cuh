@@ -152,9 +152,10 @@ struct GramPeer {
   int xr;                    // rank columns of an exchanged block (the same on every rank)
   uint64_t gen;
 };
+// One half of an exchange buffer: per (source rank, block, rank-column pair, column) one 16-byte
+// entry of two 64-bit words {generation << 32 | float bits}.
 __host__ __device__ inline size_t peer_half_bytes(int world, int n_blocks, int r_pad) {
-  return (static_cast<size_t>(world) * n_blocks * 4 * 8 + static_cast<size_t>(world) * n_blocks * 128 * r_pad * 4 +
-          255) & ~size_t(255);
+  return (static_cast<size_t>(world) * n_blocks * 128 * r_pad * 8 + 255) & ~size_t(255);
 }
 cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables& tb, int num_sms, cudaStream_t st,
                     int planes = 1, void* scratch = nullptr, uint64_t gen = 0, const GramPeer* peer = nullptr);

@@ -121,15 +121,15 @@ __device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t* p) {
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-// System-scope forms, for flags another GPU writes into this GPU's memory (or this GPU into a
-// peer's, through a peer mapping).
-__device__ __forceinline__ uint64_t ld_acquire_sys_u64(const uint64_t* p) {
-  uint64_t v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
+// Two 64-bit words in one 16-byte access, system scope (a peer GPU's memory through a peer mapping,
+// or words a peer writes into this GPU's memory).  Each 64-bit word is a single-copy-atomic
+// access of its own, so a word that carries its own validity tag (a generation in its high half)
+// needs no fence or flag: a reader that sees the tag sees the value stored with it.
+__device__ __forceinline__ void st_volatile_v2u64(void* p, uint64_t a, uint64_t b) {
+  asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
 }
-__device__ __forceinline__ void st_release_sys_u64(uint64_t* p, uint64_t v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void ld_volatile_v2u64(const void* p, uint64_t& a, uint64_t& b) {
+  asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 // With an earlier relaxed load that observed a released value, makes this thread acquire it.
 __device__ __forceinline__ void fence_acquire_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }

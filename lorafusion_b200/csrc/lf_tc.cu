@@ -1561,20 +1561,56 @@ __device__ __forceinline__ GramUnit gram_unit(const GramParams& prm, const GramS
 // listed largest first, every CTA gets a similar share.
 __device__ __forceinline__ int gram_zigzag(int r, int me, int G) { return r * G + ((r & 1) ? G - 1 - me : me); }
 
-// Bounded wait until *f == gen, with system-scope acquire (the flag is written by another GPU).
-__device__ __forceinline__ bool wait_flag_sys(const uint64_t* f, uint64_t gen, volatile int* abort_flag, int* err) {
-  if (ld_acquire_sys_u64(f) == gen) return true;
-  const uint64_t t0 = globaltimer_ns();
-  const uint64_t limit = wait_limit(err);
-  while (ld_acquire_sys_u64(f) != gen) {
-    if (*abort_flag) return false;
-    if (globaltimer_ns() - t0 > limit) {
-      record_error(err, kErrTimeoutFlag);
-      *abort_flag = 1;
-      return false;
-    }
-    __nanosleep(256);
+// Exchange entries (see peer_half_bytes): entry (src, blk, jp, col) holds elements 2jp and 2jp+1 of
+// column col of block blk as rank src computed it, each as {gen << 32 | float bits}.  A warp's 32
+// columns of one pair are 512 contiguous bytes.
+__device__ __forceinline__ size_t span_entry(const GramPeer& pr, int src, int blk, int jp, int col) {
+  return ((static_cast<size_t>(src) * pr.n_blocks + blk) * (pr.xr / 2) + jp) * 128 + col;
+}
+// Elements j0 .. j0+15 of this lane's column of block `blk`, into every rank's exchange buffer
+// (this rank's entries there); plain stores, no fence: each word carries the generation.
+__device__ __forceinline__ void span_put16(const GramPeer& pr, size_t half, int blk, int col, int j0, const float* v) {
+  const uint64_t tag = static_cast<uint64_t>(static_cast<uint32_t>(pr.gen)) << 32;
+  const size_t e0 = span_entry(pr, pr.rank, blk, j0 / 2, col);
+  for (int d = 0; d < pr.world; ++d) {
+    uint8_t* base = pr.xbuf[d] + half;
+#pragma unroll 2
+    for (int t = 0; t < 8; ++t)
+      st_volatile_v2u64(base + (e0 + static_cast<size_t>(t) * 128) * 16, tag | __float_as_uint(v[2 * t]),
+                        tag | __float_as_uint(v[2 * t + 1]));
   }
+}
+// Adds rank src's elements j0 .. j0+15 of this lane's column of block `blk` (local exchange buffer)
+// to acc, once they carry this call's generation: all eight entries are loaded at once, those not
+// yet written are polled (bounded).  False after a timeout or an abort.
+__device__ __forceinline__ bool span_add16(const GramPeer& pr, const uint8_t* base, int src, int blk, int col, int j0,
+                                           float* acc, volatile int* abort_flag, int* err) {
+  const uint32_t gen = static_cast<uint32_t>(pr.gen);
+  const uint8_t* p = base + span_entry(pr, src, blk, j0 / 2, col) * 16;
+  uint64_t w[16];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) ld_volatile_v2u64(p + static_cast<size_t>(t) * 128 * 16, w[2 * t], w[2 * t + 1]);
+  bool ready = true;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) ready = ready && static_cast<uint32_t>(w[i] >> 32) == gen;
+  if (!ready) {
+    const uint64_t t0 = globaltimer_ns();
+    const uint64_t limit = wait_limit(err);
+#pragma unroll
+    for (int t = 0; t < 8; ++t)
+      while (static_cast<uint32_t>(w[2 * t] >> 32) != gen || static_cast<uint32_t>(w[2 * t + 1] >> 32) != gen) {
+        if (*abort_flag) return false;
+        if (globaltimer_ns() - t0 > limit) {
+          record_error(err, kErrTimeoutFlag);
+          *abort_flag = 1;
+          return false;
+        }
+        __nanosleep(128);
+        ld_volatile_v2u64(p + static_cast<size_t>(t) * 128 * 16, w[2 * t], w[2 * t + 1]);
+      }
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i] += __uint_as_float(static_cast<uint32_t>(w[i]));
   return true;
 }
 
@@ -1667,10 +1703,8 @@ __global__ void __launch_bounds__(kGramThreads)
       for (int i0 = 0; i0 < tb.n_slots; i0 += 32) {
         const int i = i0 + lane;
         const int nst = i < tb.n_slots ? sp.nst[i] : 0;
-        // parts are the same for both jobs (one cap); lanes past the end count nothing; the blocks
-        // of a spanning slot go to the other GPUs whole
-        const bool span = i < tb.n_slots && prm.peer.world > 0 && prm.peer.slot_span[sp.slot[i]] >= 0;
-        const int P = i >= tb.n_slots ? 0 : (try_split && !span && nst > prm.cap) ? (nst + prm.cap - 1) / prm.cap : 1;
+        // parts are the same for both jobs (one cap); lanes past the end count nothing
+        const int P = i >= tb.n_slots ? 0 : (try_split && nst > prm.cap) ? (nst + prm.cap - 1) / prm.cap : 1;
         int a = P, b = P > 1 ? P : 0, c = P > 1 ? 1 : 0;  // inclusive warp scans
 #pragma unroll
         for (int d = 1; d < 32; d <<= 1) {
@@ -1936,16 +1970,14 @@ __global__ void __launch_bounds__(kGramThreads)
             }
         }
       };
+      // A spanning slot's block (this warp's 32 columns, summed over this rank's rows) goes to every
+      // rank's exchange buffer; the sums over the ranks are formed after the units.  A split
+      // slot's last part pushes the parts' sum.
       const int sv = prm.peer.world > 0 ? prm.peer.slot_span[g.slot] : -1;
-      if (sv >= 0) {
-        // spanning slot (never split): this warp's 32 columns of the block go to every rank's
-        // exchange buffer (this rank's row there), then one release per rank; the sums are
-        // formed after the units
+      if (sv >= 0 && g.parts == 1) {
         const GramPeer& pr = prm.peer;
         const int blk = sv * pr.blocks_per_span + (jb.transpose_out ? pr.cblk_b : 0) + g.cb;
         const size_t half = peer_half_bytes(pr.world, pr.n_blocks, pr.xr) * static_cast<size_t>(pr.gen & 1);
-        const size_t data_off = static_cast<size_t>(pr.world) * pr.n_blocks * 4 * 8;
-        const size_t mine = ((static_cast<size_t>(pr.rank) * pr.n_blocks + blk) * 128 + col) * pr.xr;
         for (int j0 = 0; j0 < pr.xr; j0 += 16) {
           float v[16];
           if (j0 < r_pad) {
@@ -1954,21 +1986,10 @@ __global__ void __launch_bounds__(kGramThreads)
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) v[jj] = 0.f;
           }
-          for (int d = 0; d < pr.world; ++d) {
-            float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(pr.xbuf[d] + half + data_off) + mine + j0);
-#pragma unroll
-            for (int t = 0; t < 4; ++t) dst[t] = make_float4(v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]);
-          }
+          span_put16(pr, half, blk, col, j0, v);
         }
         tc_fence_before();
         mbar_arrive(&tempty[buf]);
-        __threadfence_system();
-        __syncwarp();
-        if (lane == 0)
-          for (int d = 0; d < pr.world; ++d)
-            st_release_sys_u64(reinterpret_cast<uint64_t*>(pr.xbuf[d] + half) +
-                                   (static_cast<size_t>(pr.rank) * pr.n_blocks + blk) * 4 + q,
-                               pr.gen);
         continue;
       }
       if (g.parts > 1) {
@@ -1995,6 +2016,31 @@ __global__ void __launch_bounds__(kGramThreads)
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) continue;
         __threadfence();
+        if (sv >= 0) {  // spanning slot: the parts' sum goes to the exchange (zeros past r_pad)
+          const GramPeer& pr = prm.peer;
+          const int blk = sv * pr.blocks_per_span + (jb.transpose_out ? pr.cblk_b : 0) + g.cb;
+          const size_t half = peer_half_bytes(pr.world, pr.n_blocks, pr.xr) * static_cast<size_t>(pr.gen & 1);
+          for (int j0 = 0; j0 < pr.xr; j0 += 16) {
+            float acc[16];
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) acc[jj] = 0.f;
+            if (j0 < r_pad)
+              for (int pp = 0; pp < g.parts; ++pp) {
+                const float4* src = reinterpret_cast<const float4*>(
+                    prm.partial + (static_cast<int64_t>(g.pbase + pp * jb.n_cblk) * 128 + col) * r_pad + j0);
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                  const float4 f = __ldcg(src + t);
+                  acc[4 * t] += f.x;
+                  acc[4 * t + 1] += f.y;
+                  acc[4 * t + 2] += f.z;
+                  acc[4 * t + 3] += f.w;
+                }
+              }
+            span_put16(pr, half, blk, col, j0, acc);
+          }
+          continue;
+        }
         for (int j0 = 0; j0 < r_pad; j0 += 16) {  // 16 sums per step, parts added in order
           float acc[16];
 #pragma unroll
@@ -2029,16 +2075,15 @@ __global__ void __launch_bounds__(kGramThreads)
     }
     if (prm.peer.world > 0 && !*abort_flag) {
       // Sums of the spanning blocks of this launch's jobs (held here or not): block t goes to set
-      // t % 2 of CTA t / 2 (mod the grid); once every holder has released it (this warp's 32
-      // columns), the holders' rows are added in rank order and written like a local block.
+      // t % 2 of CTA t / 2 (mod the grid); each lane adds its column's entries from the holders
+      // in rank order, as they arrive, and the warp writes the sums like a local block.
       const GramPeer& pr = prm.peer;
       const size_t half = peer_half_bytes(pr.world, pr.n_blocks, pr.xr) * static_cast<size_t>(pr.gen & 1);
-      const uint64_t* flags = reinterpret_cast<const uint64_t*>(pr.xbuf[pr.rank] + half);
-      const float* data = reinterpret_cast<const float*>(pr.xbuf[pr.rank] + half +
-                                                         static_cast<size_t>(pr.world) * pr.n_blocks * 4 * 8);
+      const uint8_t* base = pr.xbuf[pr.rank] + half;
       const int n_sum0 = pr.n_span * prm.job[0].n_cblk;
       const int n_sum = n_sum0 + (prm.n_jobs > 1 ? pr.n_span * prm.job[1].n_cblk : 0);
-      for (int t = me * kGramEpiSets + set; t < n_sum; t += G * kGramEpiSets) {
+      bool ok = true;
+      for (int t = me * kGramEpiSets + set; t < n_sum && ok; t += G * kGramEpiSets) {
         const int j = t < n_sum0 ? 0 : 1;
         const GramJob& jb = prm.job[j];
         const int tt = t - (j ? n_sum0 : 0);
@@ -2046,31 +2091,14 @@ __global__ void __launch_bounds__(kGramThreads)
         const int blk = sv * pr.blocks_per_span + (jb.transpose_out ? pr.cblk_b : 0) + cb;
         const int out_prefix = pr.span_info[3 * sv], rank = pr.span_info[3 * sv + 1];
         const uint32_t holders = static_cast<uint32_t>(pr.span_info[3 * sv + 2]);
-        int ok = 1;
-        if (lane == 0)
-          for (int src = 0; src < pr.world && ok; ++src)
-            if ((holders >> src) & 1u)
-              ok = wait_flag_sys(flags + (static_cast<size_t>(src) * pr.n_blocks + blk) * 4 + q, pr.gen, abort_flag,
-                                 tb.err) ? 1 : 0;
-        if (!__shfl_sync(0xffffffffu, ok, 0)) break;
-        __syncwarp();
         for (int j0 = 0; j0 < pr.xr && j0 < rank; j0 += 16) {
           float acc[16];
 #pragma unroll
           for (int jj = 0; jj < 16; ++jj) acc[jj] = 0.f;
-          for (int src = 0; src < pr.world; ++src)
-            if ((holders >> src) & 1u) {
-              const float4* sp4 = reinterpret_cast<const float4*>(
-                  data + ((static_cast<size_t>(src) * pr.n_blocks + blk) * 128 + col) * pr.xr + j0);
-#pragma unroll
-              for (int t4 = 0; t4 < 4; ++t4) {
-                const float4 f = __ldcg(sp4 + t4);
-                acc[4 * t4] += f.x;
-                acc[4 * t4 + 1] += f.y;
-                acc[4 * t4 + 2] += f.z;
-                acc[4 * t4 + 3] += f.w;
-              }
-            }
+          for (int src = 0; src < pr.world && ok; ++src)
+            if ((holders >> src) & 1u) ok = span_add16(pr, base, src, blk, col, j0, acc, abort_flag, tb.err);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
           store16(j, out_prefix, rank, cb, j0, acc);
         }
       }
