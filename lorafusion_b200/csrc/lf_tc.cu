@@ -1813,8 +1813,9 @@ __global__ void __launch_bounds__(kGramThreads)
       const uint32_t s_bytes = static_cast<uint32_t>(kBM * r_pad * 2);
       for (int k = 0; k < n_mine && ok; ++k) {
         const GramUnit g = unit(k);
-        const int buf = k & 1;  // unit k goes through buffer k % 2 to epilogue set k % 2
-        if (!mbar_wait(&tempty[buf], ((k >> 1) & 1) ^ 1, abort_flag, tb.err, kErrTimeoutAcc)) {
+        // unit k goes through accumulator buffer k % n_bufs to epilogue set k % 2
+        const int buf = k % prm.n_bufs;
+        if (!mbar_wait(&tempty[buf], ((k / prm.n_bufs) & 1) ^ 1, abort_flag, tb.err, kErrTimeoutAcc)) {
           ok = false;
           break;
         }
@@ -1932,9 +1933,9 @@ __global__ void __launch_bounds__(kGramThreads)
     for (int k = set; k < n_mine; k += kGramEpiSets) {
       const GramUnit g = unit(k);
       const GramJob& jb = prm.job[g.job];
-      const int buf = k & 1;
+      const int buf = k % prm.n_bufs;
       const int rank = g.rank;
-      if (!warp_wait(&tfull[buf], (k >> 1) & 1, abort_flag, tb.err, kErrTimeoutAcc)) break;
+      if (!warp_wait(&tfull[buf], (k / prm.n_bufs) & 1, abort_flag, tb.err, kErrTimeoutAcc)) break;
       tc_fence_after();
       if (g.b == g.e) {
         float zeros[16];
@@ -2380,13 +2381,21 @@ cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables
   if (p.n_stages > kGramMaxStages) p.n_stages = kGramMaxStages;
   const int fmt = dtype == LF_BF16 ? 1 : 0;
   const int width = planes * tb.r_pad;  // MMA N
-  // two accumulator buffers (one per epilogue set), each with as many accumulation chains
-  // (rotating over K steps, added in fixed order: see kRoleChains) as fit, up to four
-  p.chains = 4;
-  while (p.chains > 1 && 2 * p.chains * width > 512) p.chains >>= 1;
+  // Accumulator buffers, each with its accumulation chains (rotating over K steps, added in fixed
+  // order: see kRoleChains).  The epilogue (tensor-memory reads and stores of a unit) takes longer
+  // than a short unit's MMAs, so where two chains of the MMA width fit in a quarter of the tensor
+  // memory there are four buffers and the MMA runs up to four units ahead of the epilogue sets;
+  // otherwise two buffers with as many chains as fit, up to four.
+  if (4 * 2 * width <= 512) {
+    p.n_bufs = 4;
+    p.chains = 2;
+  } else {
+    p.n_bufs = 2;
+    p.chains = 4;
+    while (p.chains > 1 && 2 * p.chains * width > 512) p.chains >>= 1;
+  }
   p.acc_cols = p.chains * width;
   p.tmem_cols = 512;  // one CTA per SM: the whole TMEM
-  p.n_bufs = 2;
   p.idesc = umma_idesc_f16(kBM, width, fmt, 1, 1);
   p.s_layout = umma_layout_for_span(tb.r_pad * 2);
   p.s_sbo = sw_sbo(tb.r_pad);
