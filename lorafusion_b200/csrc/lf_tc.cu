@@ -2383,12 +2383,13 @@ cudaError_t tc_gram(int dtype, const GramJobDesc* jobs, int n_jobs, const Tables
   const int width = planes * tb.r_pad;  // MMA N
   // Accumulator buffers, each with its accumulation chains (rotating over K steps, added in fixed
   // order: see kRoleChains).  The epilogue (tensor-memory reads and stores of a unit) takes longer
-  // than a short unit's MMAs, so where two chains of the MMA width fit in a quarter of the tensor
-  // memory there are four buffers and the MMA runs up to four units ahead of the epilogue sets;
-  // otherwise two buffers with as many chains as fit, up to four.
-  if (4 * 2 * width <= 512) {
+  // than a short unit's MMAs, so where four buffers fit the MMA runs up to four units ahead of the
+  // epilogue sets, with one chain (each chain is more columns for the epilogue to read: one chain
+  // measured faster than two or four, and than eight buffers); otherwise two buffers with as many
+  // chains as fit, up to four.
+  if (4 * width <= 512) {
     p.n_bufs = 4;
-    p.chains = 2;
+    p.chains = 1;
   } else {
     p.n_bufs = 2;
     p.chains = 4;
