@@ -238,3 +238,19 @@ def test_ranks_above_64_become_virtual_slots():
                                   3, 310, rk.ctypes.data_as(i32p), sc.ctypes.data_as(ctypes.POINTER(ctypes.c_float)),
                                   3, buf.ctypes.data_as(i32p), cap, ctypes.byref(inf))
     assert rc == nat.LF_ERR_CAPACITY and inf.table_words > cap
+
+
+def test_peer_exchange_sizes():
+    """lf_peer_exchange_bytes: two halves (alternate calls), each one 16-byte entry of two
+    generation-tagged 64-bit words per (source rank, block, rank-column pair, column), rounded up
+    to 256 bytes; unsupported arguments give 0."""
+    L = nat.lib()
+
+    def half(world, n_blocks, r_pad):
+        return (world * n_blocks * 128 * r_pad * 8 + 255) // 256 * 256
+
+    for world, n_blocks, r_pad in ((2, 1, 16), (4, 3 * 64, 16), (8, 7, 64), (2, 5, 32), (3, 1, 16)):
+        assert L.lf_peer_exchange_bytes(world, n_blocks, r_pad) == 2 * half(world, n_blocks, r_pad)
+    assert L.lf_peer_exchange_bytes(1, 0, 16) == 0  # nothing to exchange
+    for world, n_blocks, r_pad in ((0, 1, 16), (nat.MAX_PEERS + 1, 1, 16), (2, -1, 16), (2, 1, 24), (2, 1, 128)):
+        assert L.lf_peer_exchange_bytes(world, n_blocks, r_pad) == 0
