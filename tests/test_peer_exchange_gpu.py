@@ -148,3 +148,97 @@ def test_in_kernel_exchange_matches_whole_batch_oracle(world):
                                        ("grad_b", res[r]["calls"][c]["gb"][aid], rgb[aid])):
                     ok, msg = mock_oracle.allclose_report(got, ref, **tol)
                     assert ok, f"call {c} rank {r} {name}[{aid}]: {msg}"
+
+
+def _withheld_worker(rank, world, port, result_q):
+    """Call 1 on both ranks; call 2 on rank 0 only (rank 1 withholds its blocks, between steps, with
+    nothing of its own in flight) under a 50 ms wait limit; call 3 on both ranks again."""
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    peer = None
+    try:
+        from lorafusion_b200 import _native as nat
+        from lorafusion_b200 import b200_ops
+        from lorafusion_b200.config import AdapterSpec
+        from lorafusion_b200.sharding import PeerExchange, assign_bins, local_layout
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        packing, x, g, w, a, b, _ = _global_problem()
+        plan = assign_bins(packing.bins, world)
+        rows, local = local_layout(plan, packing.bins, rank, CAP)
+        t = lambda v: torch.from_numpy(np.ascontiguousarray(v)).to(dev, torch.bfloat16)  # noqa: E731
+        xl, gl, wd = t(x[rows]), t(g[rows]), t(w)
+        ad = {i: t(v) for i, v in a.items()}
+        bd = {i: t(v) for i, v in b.items()}
+        specs = {i: AdapterSpec(i, r, 2.0 * r, K, N) for i, r in enumerate(RANKS)}
+        peer = PeerExchange(plan, dict(enumerate(RANKS)), dev)
+        b200_ops.fused_lora_forward(xl, wd, ad, bd, specs, local)
+
+        def backward():
+            _, ga, gb = b200_ops.fused_lora_backward(gl, xl, wd, ad, bd, specs, local, grad_dtype=torch.float32,
+                                                     peer=peer)
+            torch.cuda.synchronize()
+            return {k: v.cpu().numpy() for k, v in ga.items()}, {k: v.cpu().numpy() for k, v in gb.items()}
+
+        first = backward()
+        status_first = nat.device_error()
+        dist.barrier()
+        code = 0
+        if rank == 0:
+            nat.set_wait_limit(50_000_000)
+            try:
+                backward()
+                code = nat.device_error()  # reads and clears the code the timed-out polls recorded
+            finally:
+                nat.set_wait_limit(0)
+        else:
+            peer.next_gen()  # the generation rank 0 used alone: skipped, so the next call pairs again
+        dist.barrier()
+        again = backward()
+        same = all(np.array_equal(first[0][k], again[0][k]) for k in first[0]) and \
+            all(np.array_equal(first[1][k], again[1][k]) for k in first[1])
+        result_q.put((rank, {"code": code, "status_first": status_first, "status": nat.device_error(),
+                             "same": same}))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        result_q.put((rank, repr(e)))
+        raise
+    finally:
+        if peer is not None:
+            peer.close()
+        dist.destroy_process_group()
+
+
+def test_withheld_blocks_time_out_and_the_next_call_recovers():
+    """A rank that does not take part in a call (its blocks never arrive) makes the other rank's
+    polls of the exchange run out: the call returns, lf_device_error reports ERR_TIMEOUT_FLAG,
+    and the next call on both ranks gives the first call's sums bit for bit."""
+    from lorafusion_b200 import _native as nat
+    world = 2
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip("the in-kernel exchange needs one GPU per rank (2 GPUs)")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_withheld_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(world):
+            r, out = q.get(timeout=300)
+            res[r] = out
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    for r in range(world):
+        assert isinstance(res[r], dict), res[r]
+        assert res[r]["status_first"] == 0 and res[r]["status"] == 0, res[r]
+        assert res[r]["same"], r
+    assert res[0]["code"] == nat.ERR_TIMEOUT_FLAG, hex(res[0]["code"])
